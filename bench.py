@@ -1,0 +1,490 @@
+#!/usr/bin/env python
+"""Benchmark of the batched FP32 geqrf hot path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one factorization of one batch of the workload config (default:
+config 2, b=4096 n=32 iid N(0,1) seed 1) per rank. Scaling is weak: every rank
+factors its own shard of ``N x batch`` matrices (rank r takes matrices
+[r*b, (r+1)*b) of the seeded global batch); there is no collective on the hot
+path. Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA
+events on the launching stream, with a 256 MiB write between steps to flush L2
+(the workload fits in L2). The timed region is bracketed by a barrier and
+``torch.cuda.synchronize()``; the reported time is the MAX over ranks of the
+summed step times. Rank 0 prints one JSON line.
+
+``--impl reference`` times the reference's own CPU implementation of the path,
+``torch.geqrf`` on the host cores (``src/qrbench/reference.py:18-20``), on the
+same config and metric (rank 0 only; other ranks exit 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "median ms/batch + matrices/s of batched fp32 geqrf at 1/2/4/8 B200; % roofline"
+UNIT = "matrices/s"
+L2_FLUSH_BYTES = 256 << 20
+FP32_FFMA_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # at clocks.max.sm
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", type=int, default=2, help="workload config index (1-5)")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-config sweep")
+    ap.add_argument("--no-cpu", action="store_true", help="skip CPU geqrf timings")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget")
+    return ap.parse_args(argv)
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region (NVML reads only)
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    REASONS = {
+        0x0000000000000001: "gpu_idle",
+        0x0000000000000002: "applications_clocks_setting",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sync_boost",
+        0x0000000000000040: "sw_thermal_slowdown",
+        0x0000000000000080: "hw_thermal_slowdown",
+        0x0000000000000100: "hw_power_brake_slowdown",
+        0x0000000000000200: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.err = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = device_index
+            if vis:
+                ids = [v.strip() for v in vis.split(",") if v.strip()]
+                if device_index < len(ids) and ids[device_index].isdigit():
+                    idx = int(ids[device_index])
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nv = None
+            self.err = repr(e)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, rs))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": self.err or "no samples"}
+        mhz = [s for s, _ in self.samples]
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = [name for bit, name in self.REASONS.items() if mask & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def measured_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs"), "bf16_tflops": d.get("bf16_tflops"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profile_traffic(workload: str):
+    p = REPO / "profiles" / "roofline_traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get(workload)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own CPU path, torch.geqrf (LAPACK) on the host
+# ---------------------------------------------------------------------------
+
+
+def cpu_geqrf_rate(A_cpu, budget_s: float, min_reps: int = 2, max_reps: int = 200):
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    torch.geqrf(A_cpu[: min(A_cpu.shape[0], 64)])  # warm-up (threads, MKL init)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < max_reps and (len(times) < min_reps or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        torch.geqrf(A_cpu)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {
+        "value": A_cpu.shape[0] / med,
+        "unit": UNIT,
+        "median_ms": med * 1e3,
+        "reps": len(times),
+        "cores": torch.get_num_threads(),
+        "kind": "reference",
+        "sample": (f"torch.geqrf on CPU (LAPACK sgeqrf; the reference's geqrf_reference, "
+                   f"src/qrbench/reference.py:18-20), full batch of {A_cpu.shape[0]} x "
+                   f"{A_cpu.shape[1]}x{A_cpu.shape[2]}, median of {len(times)} runs"),
+        "cpu_model": _cpu_model(),
+    }
+
+
+def _cpu_model() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, info) -> int:
+    """Reference arm: CPU torch.geqrf on this arm's config, rank 0 only."""
+    from gpumode_qr_b200 import inputs
+
+    if info.rank != 0:
+        return 0
+    import torch
+
+    cfg = inputs.config(args.config)
+    A = inputs.make_config_input(cfg)
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(max(1, min(args.warmup, 3))):
+        torch.geqrf(A)
+    steps = max(1, args.steps)
+    # bound the run: cap the number of timed steps to ~60 s of CPU work
+    t0 = time.perf_counter()
+    torch.geqrf(A)
+    est = time.perf_counter() - t0
+    steps = max(1, min(steps, int(60.0 / max(est, 1e-6))))
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        torch.geqrf(A)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = cfg.batch * steps / total
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": total / steps * 1e3,
+        "median_ms": statistics.median(times) * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded torch.Generator, CPU)",
+        "config": {"workload": cfg.name, "batch": cfg.batch, "n": cfg.n, "seed": cfg.seed},
+        "cpu_baseline": {
+            "value": value,
+            "unit": UNIT,
+            "cores": torch.get_num_threads(),
+            "kind": "reference",
+            "sample": (f"torch.geqrf on CPU (the reference's geqrf_reference), {steps} steps of "
+                       f"the full {cfg.batch}-matrix batch"),
+        },
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+
+def time_device_steps(step, steps: int, warmup: int, flush_buf, stream):
+    """Per-step CUDA-event times (ms) with an L2 flush between steps."""
+    import torch
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for k in range(steps):
+        flush_buf.fill_(k & 0x7F)
+        starts[k].record(stream)
+        step()
+        ends[k].record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
+    import torch
+
+    from gpumode_qr_b200 import api, checker, inputs
+
+    out = {}
+    gpu_ms, cpu_ms = [], []
+    stream = torch.cuda.current_stream(dev)
+    for cfg in inputs.CONFIGS:
+        A_cpu = inputs.make_config_input(cfg)
+        A = A_cpu.to(dev)
+        H = torch.empty_like(A)
+        tau = torch.empty(cfg.batch, cfg.n, device=dev)
+        fn = api.geqrf_into_fn(A, H, tau)
+        iters = 10
+        times = time_device_steps(fn, iters, 3, flush_buf, stream)
+        med = statistics.median(times)
+        gpu_ms.append(med)
+        gate = checker.check(A, H, tau)
+        rec = {
+            "batch": cfg.batch,
+            "n": cfg.n,
+            "median_ms": med,
+            "min_ms": min(times),
+            "matrices_per_s": cfg.batch / (med / 1e3),
+            "gates": {"factor": gate.factor_residual, "factor_thr": gate.factor_threshold,
+                      "orth": gate.orth_residual, "orth_thr": gate.orth_threshold,
+                      "passed": gate.passed},
+        }
+        if cfg.n <= 64:
+            gbs = cfg.bytes / (med / 1e3) / 1e9
+            rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
+                               "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"]}
+        else:
+            tf = cfg.flops / (med / 1e3) / 1e12
+            rec["roofline"] = {"bound": "fp32_ffma", "achieved": tf, "peak": FP32_FFMA_NOMINAL_TFLOPS,
+                               "unit": "TFLOP/s", "frac": tf / FP32_FFMA_NOMINAL_TFLOPS,
+                               "peak_source": "nominal 148 SMs x 128 FFMA x 2 x 1965 MHz"}
+        if cpu:
+            torch.set_num_threads(os.cpu_count() or 1)
+            torch.geqrf(A_cpu[:1])
+            ct = []
+            for _ in range(3 if cfg.n < 4096 else 2):
+                t0 = time.perf_counter()
+                Hr, tr = torch.geqrf(A_cpu)
+                ct.append((time.perf_counter() - t0) * 1e3)
+            cmed = statistics.median(ct)
+            cpu_ms.append(cmed)
+            rec["cpu_geqrf_median_ms"] = cmed
+            rec["speedup_vs_cpu"] = cmed / med
+            if cfg.parity:
+                par = checker.parity(H.cpu(), tau.cpu(), Hr, tr)
+                rec["parity_vs_geqrf"] = {"h_rel": par.h_rel, "tau_rel": par.tau_rel,
+                                          "col_rel": par.col_rel, "ok": par.ok()}
+        out[cfg.name] = rec
+        del A, H, tau, A_cpu
+        torch.cuda.empty_cache()
+    gm = math.exp(sum(math.log(x) for x in gpu_ms) / len(gpu_ms))
+    res = {"configs": out, "gpu_geomean_ms": gm}
+    if cpu_ms:
+        cg = math.exp(sum(math.log(x) for x in cpu_ms) / len(cpu_ms))
+        res["cpu_geomean_ms"] = cg
+        res["geomean_speedup_vs_cpu"] = cg / gm
+        res["cpu_cores"] = torch.get_num_threads()
+        res["cpu_model"] = _cpu_model()
+    return res
+
+
+def run_ours(args, info) -> int:
+    import torch
+
+    from gpumode_qr_b200 import _lib, api, checker, inputs, sharding
+
+    dev = torch.device("cuda", info.local_rank if info.initialized else 0)
+    torch.cuda.set_device(dev)
+    cfg = inputs.config(args.config)
+    b = cfg.batch
+    world = info.world
+    g_cfg = inputs.Config(cfg.index, b * world, cfg.n, cfg.kind, cfg.seed, cfg.log10_cond, cfg.parity)
+    A_all = inputs.make_config_input(g_cfg) if world > 1 else inputs.make_config_input(cfg)
+    s, e = sharding.shard_range(b * world, info.rank, world)
+    A_cpu = A_all[s:e].contiguous()
+    del A_all
+    A = A_cpu.to(dev)
+    H = torch.empty_like(A)
+    tau = torch.empty(A.shape[0], cfg.n, device=dev)
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    step = api.geqrf_into_fn(A, H, tau)
+
+    # correctness gate on this rank's shard before timing
+    step()
+    torch.cuda.synchronize()
+    gate = checker.check(A, H, tau)
+    if not gate.passed:
+        print(f"[bench] rank {info.rank}: gate FAILED {gate.as_dict()}", file=sys.stderr)
+
+    # timed region: device-resident inputs
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sharding.barrier(info)
+    torch.cuda.synchronize()
+    _lib.set_config("launches", 0)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clk:
+        for k in range(args.steps):
+            flush_buf.fill_(k & 0x7F)
+            starts[k].record(stream)
+            step()
+            ends[k].record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.get_config("launches")
+    sharding.barrier(info)
+    torch.cuda.synchronize()
+    times = [a.elapsed_time(z) for a, z in zip(starts, ends)]
+    total_ms = sharding.max_over_ranks(sum(times), info)
+    med_ms = sharding.max_over_ranks(statistics.median(times), info)
+    total_mats = b * world * args.steps
+    value = total_mats / (total_ms / 1e3)
+    launches_total = int(sharding.sum_over_ranks(launches, info))
+
+    # e2e through the public API with pinned host buffers (copies in the timed region)
+    A_host = A_cpu.pin_memory()
+    H_host = torch.empty_like(A_host).pin_memory()
+    tau_host = torch.empty(A_host.shape[0], cfg.n).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+
+    def e2e_step():
+        api.geqrf_host(A_host, H_host, tau_host, device=dev)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    sharding.barrier(info)
+    e_s = torch.cuda.Event(enable_timing=True)
+    e_e = torch.cuda.Event(enable_timing=True)
+    e_s.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_e.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = sharding.max_over_ranks(e_s.elapsed_time(e_e), info)
+    sharding.barrier(info)
+    e2e_value = b * world * e2e_steps / (e2e_ms / 1e3)
+    h2d = A_host.numel() * 4
+    d2h = H_host.numel() * 4 + tau_host.numel() * 4
+
+    peaks = measured_peaks()
+    extra = {}
+    if info.rank == 0 and world == 1 and not args.no_configs:
+        extra["per_config"] = per_config_sweep(dev, flush_buf, not args.no_cpu, peaks)
+    cpu = None
+    if info.rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_geqrf_rate(A_cpu, args.cpu_seconds)
+
+    if info.rank == 0:
+        alg_bytes = 2 * b * cfg.n * cfg.n * 4
+        ach = alg_bytes / (statistics.mean(times) / 1e3) / 1e9
+        traffic = profile_traffic(cfg.name)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps,
+            "median_ms": med_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded torch.Generator on CPU, copied to HBM)",
+            "config": {
+                "workload": cfg.name,
+                "batch_per_gpu": b,
+                "global_batch": b * world,
+                "n": cfg.n,
+                "seed": cfg.seed,
+                "l2": "flushed between steps (256 MiB write, outside the step events)",
+                "parallelism": f"batch-sharded dp{world}, no collective on the hot path",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": ach,
+                "peak": peaks["hbm_gbs"],
+                "unit": "GB/s",
+                "frac": ach / peaks["hbm_gbs"],
+                "traffic": traffic,
+                "peak_source": peaks["source"],
+                "kernel": "k_fused_warp (one launch per step)" if cfg.n <= 32 else "whole step",
+                "algorithmic_bytes_per_launch": alg_bytes,
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "api": "gpumode_qr_b200.api.geqrf_host (pinned host in/out)"},
+            "gpu_launches": launches_total,
+            "clocks": clk.summary(),
+            "gates": {"factor": gate.factor_residual, "orth": gate.orth_residual,
+                      "passed": gate.passed},
+            **extra,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    from gpumode_qr_b200 import sharding
+
+    info = sharding.init_from_env()
+    try:
+        if args.impl == "reference":
+            return run_reference(args, info)
+        return run_ours(args, info)
+    finally:
+        sharding.destroy(info)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

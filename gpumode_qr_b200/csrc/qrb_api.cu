@@ -1,0 +1,199 @@
+// C ABI of libqrb200: argument validation, configuration hooks and the
+// blocked-QR driver (the panel loop of the reference's
+// _hh_panel_blocked_qr, src/qrbench/variants.py:761-805, run here on the host
+// side of the library as one stream-ordered kernel sequence per call).
+#include <atomic>
+#include <cstring>
+
+#include "qrb_common.cuh"
+
+namespace {
+
+std::atomic<int64_t> g_fail_next{0};
+std::atomic<int64_t> g_sync_check{0};
+std::atomic<int64_t> g_larfb_tc{64};
+std::atomic<int64_t> g_launches{0};
+
+// Host-side fault injection: consume one pending injected failure.
+bool take_injected_failure() {
+  int64_t v = g_fail_next.load();
+  while (v > 0) {
+    if (g_fail_next.compare_exchange_weak(v, v - 1)) return true;
+  }
+  return false;
+}
+
+int finish(int rc, cudaStream_t stream) {
+  if (rc != QRB_OK) return rc;
+  if (g_sync_check.load() != 0) {
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return QRB_ERR_LAUNCH;
+    if (cudaGetLastError() != cudaSuccess) return QRB_ERR_LAUNCH;
+  }
+  return QRB_OK;
+}
+
+bool bad_matrix_strides(int64_t sb, int64_t srow, int64_t rows, int64_t cols,
+                        int64_t batch) {
+  if (srow < cols) return true;                       // rows overlap
+  if (batch > 1 && sb < (rows - 1) * srow + cols) return true;  // matrices overlap
+  return false;
+}
+
+}  // namespace
+
+namespace qrb {
+void note_launches(int64_t count) { g_launches.fetch_add(count); }
+}  // namespace qrb
+
+extern "C" {
+
+int qrb_version(void) { return 100; }
+
+const char* qrb_status_string(int status) {
+  switch (status) {
+    case QRB_OK: return "qrb: ok";
+    case QRB_ERR_INVALID_ARG: return "qrb: invalid argument";
+    case QRB_ERR_UNSUPPORTED: return "qrb: unsupported size";
+    case QRB_ERR_WORKSPACE: return "qrb: workspace missing or too small";
+    case QRB_ERR_LAUNCH: return "qrb: kernel launch or execution failed";
+    case QRB_ERR_DEVICE: return "qrb: no usable CUDA device";
+    case QRB_ERR_INJECTED: return "qrb: injected failure (fail_next)";
+    default: return "qrb: unknown status";
+  }
+}
+
+int32_t qrb_max_n(void) { return qrb::kMaxN; }
+int32_t qrb_fused_max_n(void) { return qrb::kFusedMaxN; }
+
+size_t qrb_workspace_bytes(int64_t batch, int32_t n) {
+  if (batch <= 0 || n <= qrb::kFusedMaxN) return 0;
+  // One 32 x 32 compact-WY factor T per matrix.
+  return (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float);
+}
+
+int qrb_fused_qr_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
+                     float* H, float* tau, int64_t batch, int32_t n,
+                     void* stream) {
+  if (batch < 0 || n < 0) return QRB_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0) return QRB_OK;
+  if (!A || !H || !tau) return QRB_ERR_INVALID_ARG;
+  if (n > qrb::kFusedMaxN) return QRB_ERR_UNSUPPORTED;
+  if (bad_matrix_strides(strideA_b, strideA_row, n, n, batch)) return QRB_ERR_INVALID_ARG;
+  if (take_injected_failure()) return QRB_ERR_INJECTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return finish(qrb::launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s), s);
+}
+
+int qrb_panel_qr_f32(const float* P, int64_t strideP_b, int64_t strideP_row,
+                     float* H, float* V, float* tau, float* T, int64_t batch,
+                     int32_t r, int32_t w, void* stream) {
+  if (batch < 0 || r < 0 || w < 0) return QRB_ERR_INVALID_ARG;
+  if (batch == 0 || r == 0 || w == 0) return QRB_OK;
+  if (!P || !H || !tau || !T) return QRB_ERR_INVALID_ARG;
+  if (w > qrb::kPanelW || r < w) return QRB_ERR_UNSUPPORTED;
+  if (qrb::panel_cluster_size(r) > qrb::kMaxCluster) return QRB_ERR_UNSUPPORTED;
+  if (bad_matrix_strides(strideP_b, strideP_row, r, w, batch)) return QRB_ERR_INVALID_ARG;
+  if (take_injected_failure()) return QRB_ERR_INJECTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rc = qrb::launch_panel(P, strideP_b, strideP_row, H, (int64_t)r * w, w, tau, w, T,
+                                   (int64_t)w * w, w, V, batch, r, w, s);
+  return finish(rc, s);
+}
+
+int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row,
+                  const float* T, float* C, int64_t strideC_b,
+                  int64_t strideC_row, int64_t batch, int32_t r, int32_t k,
+                  int32_t c, void* stream) {
+  if (batch < 0 || r < 0 || k < 0 || c < 0) return QRB_ERR_INVALID_ARG;
+  if (batch == 0 || r == 0 || k == 0 || c == 0) return QRB_OK;
+  if (!V || !T || !C) return QRB_ERR_INVALID_ARG;
+  if (k > qrb::kPanelW || r < k) return QRB_ERR_UNSUPPORTED;
+  if (bad_matrix_strides(strideV_b, strideV_row, r, k, batch)) return QRB_ERR_INVALID_ARG;
+  if (bad_matrix_strides(strideC_b, strideC_row, r, c, batch)) return QRB_ERR_INVALID_ARG;
+  if (take_injected_failure()) return QRB_ERR_INJECTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rc = qrb::launch_larfb(V, strideV_b, strideV_row, T, (int64_t)k * k, k, C,
+                                   strideC_b, strideC_row, C, strideC_b, strideC_row, batch,
+                                   r, k, c, (int)g_larfb_tc.load(), s);
+  return finish(rc, s);
+}
+
+int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
+                  float* H, float* tau, int64_t batch, int32_t n,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (batch < 0 || n < 0) return QRB_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0) return QRB_OK;
+  if (!A || !H || !tau) return QRB_ERR_INVALID_ARG;
+  if (n > qrb::kMaxN) return QRB_ERR_UNSUPPORTED;
+  if (bad_matrix_strides(strideA_b, strideA_row, n, n, batch)) return QRB_ERR_INVALID_ARG;
+  if (A == H && (strideA_row != n || strideA_b != (int64_t)n * n)) return QRB_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n <= qrb::kFusedMaxN) {
+    if (take_injected_failure()) return QRB_ERR_INJECTED;
+    return finish(qrb::launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s), s);
+  }
+  const size_t need = qrb_workspace_bytes(batch, n);
+  if (workspace == nullptr || workspace_bytes < need) return QRB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
+  if (take_injected_failure()) return QRB_ERR_INJECTED;
+
+  float* T = static_cast<float*>(workspace);
+  const int64_t nn = (int64_t)n * n;
+  const int W = qrb::kPanelW;
+  const int tc = (int)g_larfb_tc.load();
+  for (int j0 = 0; j0 < n; j0 += W) {
+    const int w = n - j0 < W ? n - j0 : W;
+    const int r = n - j0;
+    // The first step reads A and writes H, so no separate copy pass is needed.
+    const float* src = (j0 == 0) ? A : H;
+    const int64_t sb = (j0 == 0) ? strideA_b : nn;
+    const int64_t ld = (j0 == 0) ? strideA_row : n;
+    float* Hp = H + (int64_t)j0 * n + j0;
+    int rc = qrb::launch_panel(src + (int64_t)j0 * ld + j0, sb, ld, Hp, nn, n, tau + j0, n, T,
+                               (int64_t)W * W, W, nullptr, batch, r, w, s);
+    if (rc != QRB_OK) return rc;
+    const int c = n - j0 - w;
+    if (c > 0) {
+      rc = qrb::launch_larfb(Hp, nn, n, T, (int64_t)W * W, W, src + (int64_t)j0 * ld + j0 + w, sb,
+                             ld, Hp + w, nn, n, batch, r, w, c, tc, s);
+      if (rc != QRB_OK) return rc;
+    }
+  }
+  return finish(QRB_OK, s);
+}
+
+int qrb_set_config(const char* key, int64_t value) {
+  if (!key) return QRB_ERR_INVALID_ARG;
+  if (std::strcmp(key, "fail_next") == 0) {
+    if (value < 0) return QRB_ERR_INVALID_ARG;
+    g_fail_next.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "sync_check") == 0) {
+    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    g_sync_check.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "larfb_tc") == 0) {
+    if (value != 64) return QRB_ERR_INVALID_ARG;
+    g_larfb_tc.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "launches") == 0) {
+    if (value != 0) return QRB_ERR_INVALID_ARG;
+    g_launches.store(0);
+    return QRB_OK;
+  }
+  return QRB_ERR_INVALID_ARG;
+}
+
+int qrb_get_config(const char* key, int64_t* value) {
+  if (!key || !value) return QRB_ERR_INVALID_ARG;
+  if (std::strcmp(key, "fail_next") == 0) { *value = g_fail_next.load(); return QRB_OK; }
+  if (std::strcmp(key, "sync_check") == 0) { *value = g_sync_check.load(); return QRB_OK; }
+  if (std::strcmp(key, "larfb_tc") == 0) { *value = g_larfb_tc.load(); return QRB_OK; }
+  if (std::strcmp(key, "launches") == 0) { *value = g_launches.load(); return QRB_OK; }
+  return QRB_ERR_INVALID_ARG;
+}
+
+}  // extern "C"

@@ -1,0 +1,72 @@
+// Shared device helpers and internal launcher declarations of libqrb200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qrb200.h"
+
+namespace qrb {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kPanelW = 32;        // panel / block-reflector width
+constexpr int kFusedMaxN = 32;     // largest n of the warp-per-matrix kernel
+constexpr int kMaxN = 8192;        // 4096 rows per CTA-cluster of 8 x 512 x 2
+constexpr int kMaxCluster = 8;
+
+// Householder coefficients for one column, LAPACK slarfg convention as the
+// reference kernels state it (src/qrbench/triton_kernels.py:691-700):
+//   sigma = ||x(j+1:)||^2, norm = sqrt(alpha^2 + sigma),
+//   beta = -sign(alpha) * norm (alpha >= 0 -> -norm), tau = (beta-alpha)/beta,
+//   v = x / (alpha - beta); sigma <= 0 -> tau = 0, beta = alpha (identity).
+struct Reflector {
+  float beta, tau, scale;
+};
+
+__device__ __forceinline__ Reflector make_reflector(float alpha, float sigma) {
+  Reflector h;
+  if (sigma > 0.f) {
+    const float norm = sqrtf(fmaf(alpha, alpha, sigma));
+    const float beta = alpha >= 0.f ? -norm : norm;
+    h.beta = beta;
+    h.tau = (beta - alpha) / beta;
+    h.scale = 1.0f / (alpha - beta);
+  } else {
+    h.beta = alpha;
+    h.tau = 0.f;
+    h.scale = 0.f;
+  }
+  return h;
+}
+
+// Internal launchers (one per kernel family); all return qrb status codes and
+// only enqueue work on `stream`.
+int launch_fused_small(const float* A, int64_t sAb, int64_t sAr, float* H,
+                       float* tau, int64_t batch, int n, cudaStream_t stream);
+
+// Factor the r x w panel starting at (row 0, col 0) of src (row stride ld_src,
+// matrix stride sb_src) into dst; tau to tau_out[m*tau_sb + c]; T to
+// T_out[m*T_sb + row*t_ld + col] (t_ld == 32: a zero-padded 32 x 32 block;
+// t_ld == w: a dense w x w block). V_out, when non-null, receives the explicit
+// unit-lower reflectors (r x w, contiguous per matrix).
+int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
+                 int64_t sb_dst, int64_t ld_dst, float* tau_out, int64_t tau_sb,
+                 float* T_out, int64_t T_sb, int t_ld, float* V_out,
+                 int64_t batch, int r, int w, cudaStream_t stream);
+
+// C_dst <- C_src - V T^T V^T C_src for r x c blocks, k <= 32 reflectors whose
+// strictly-lower part is read from V (unit diagonal implied). T is 32 x 32 per
+// matrix (leading k x k used) when t_ld == 32, else k x k (t_ld = k).
+int launch_larfb(const float* V, int64_t sVb, int64_t ldv, const float* T,
+                 int64_t sTb, int t_ld, const float* Csrc, int64_t sCsb,
+                 int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
+                 int64_t batch, int r, int k, int c, int tile_c,
+                 cudaStream_t stream);
+
+int panel_cluster_size(int r);
+
+// Count of kernel launches enqueued by this library (all devices, all calls);
+// read through qrb_get_config("launches").
+void note_launches(int64_t count);
+
+}  // namespace qrb

@@ -1,0 +1,331 @@
+// Block-reflector trailing update C <- C - V (T^T (V^T C)), FP32 FFMA.
+//
+// One CTA owns one matrix's r x TC column tile of C and runs the three
+// products of the reference's trailing update (src/qrbench/variants.py:800-804,
+// W1 = V^T C, W2 = T^T W1, C -= V W2) without writing the k x TC intermediate
+// to global memory:
+//   pass 1  W = V^T C over all r rows, 32-row chunks double-buffered into
+//           shared memory with cp.async; four row-interleaved thread groups
+//           each hold an 8 x 4 register block of W and are summed at the end;
+//   mid     W <- T^T W (T upper triangular, from shared memory);
+//   pass 2  C -= V W over 128-row chunks: V is staged transposed in shared
+//           memory, each thread updates an 8 x 4 block of C in registers.
+// V is read through its strictly lower part only: the diagonal is taken as 1
+// and everything above it as 0 (so V can point into a packed H), columns at or
+// beyond k as 0.
+#include "qrb_common.cuh"
+
+namespace qrb {
+
+namespace {
+
+constexpr int K = 32;        // reflectors per block (padded)
+constexpr int TC = 64;       // columns of C per CTA
+constexpr int NT = 256;      // threads per CTA
+constexpr int RC1 = 32;      // rows per pass-1 chunk
+constexpr int RC2 = 128;     // rows per pass-2 chunk
+constexpr int VS_LD = K + 4;     // pass-1 V chunk row stride (floats)
+constexpr int CS_LD = TC + 4;    // pass-1 C chunk row stride
+constexpr int VT_LD = RC2 + 4;   // pass-2 transposed V row stride
+constexpr int WS_LD = TC + 4;    // W row stride
+constexpr int T_LD = K + 1;
+
+struct __align__(16) Smem {
+  float Vs[2][RC1 * VS_LD];
+  float Cs[2][RC1 * CS_LD];
+  float Wp[4][K * TC];
+  float Ws[K * WS_LD];
+  float Vt[K * VT_LD];
+  float Ts[K * T_LD];
+};
+
+__device__ __forceinline__ void cp_async16(void* s, const void* g, bool valid) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
+  const int sz = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(g), "r"(sz)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* s, const void* g, bool valid) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
+  const int sz = valid ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(g), "r"(sz)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Value of the implicit reflector matrix at (row i, column a) given the stored
+// element x: unit diagonal, zero above, zero for columns >= k.
+__device__ __forceinline__ float vmask(float x, int i, int a, int k) {
+  return (a >= k || i < a) ? 0.f : (i == a ? 1.f : x);
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(NT)
+k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
+        const float* __restrict__ T, int64_t sTb, int t_ld,
+        const float* __restrict__ Csrc, int64_t sCsb, int64_t ldcs,
+        float* __restrict__ Cdst, int64_t sCdb, int64_t ldcd, int r, int k,
+        int c) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int64_t m = blockIdx.y;
+  const int c0 = blockIdx.x * TC;
+  const float* __restrict__ Vm = V + m * sVb;
+  const float* __restrict__ Cm = Csrc + m * sCsb;
+  float* __restrict__ Dm = Cdst + m * sCdb;
+
+  for (int e = tid; e < K * K; e += NT) {
+    const int i = e / K, a = e % K;
+    sm.Ts[i * T_LD + a] = (i < k && a < k) ? __ldg(T + m * sTb + (int64_t)i * t_ld + a) : 0.f;
+  }
+
+  // ---------------- pass 1: W = V^T C ----------------
+  const int kg = tid >> 6;            // row-interleave group 0..3
+  const int t64 = tid & 63;
+  const int wa = (t64 >> 4) << 3;     // W rows wa..wa+7
+  const int wc = (t64 & 15) << 2;     // W cols wc..wc+3
+  float acc[8][4];
+#pragma unroll
+  for (int x = 0; x < 8; ++x)
+#pragma unroll
+    for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+
+  const int nch = (r + RC1 - 1) / RC1;
+  auto load_chunk = [&](int ch, int buf) {
+    const int i0 = ch * RC1;
+    if (VEC) {
+      {  // V: 32 rows x 32 cols = 256 float4
+        const int row = tid >> 3, c4 = (tid & 7) << 2;
+        const int i = i0 + row;
+        const bool ok = i < r;
+        const float* g = ok ? Vm + (int64_t)i * ldv + c4 : Vm;
+        cp_async16(&sm.Vs[buf][row * VS_LD + c4], g, ok);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {  // C: 32 rows x 64 cols = 512 float4
+        const int idx = tid + e * NT;
+        const int row = idx >> 4, c4 = (idx & 15) << 2;
+        const int i = i0 + row, col = c0 + c4;
+        const bool ok = i < r && col < c;
+        const float* g = ok ? Cm + (int64_t)i * ldcs + col : Cm;
+        cp_async16(&sm.Cs[buf][row * CS_LD + c4], g, ok);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int idx = tid + e * NT;
+        const int row = idx >> 5, col = idx & 31;
+        const int i = i0 + row;
+        const bool ok = i < r && col < k;
+        const float* g = ok ? Vm + (int64_t)i * ldv + col : Vm;
+        cp_async4(&sm.Vs[buf][row * VS_LD + col], g, ok);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int idx = tid + e * NT;
+        const int row = idx >> 6, cc = idx & 63;
+        const int i = i0 + row, col = c0 + cc;
+        const bool ok = i < r && col < c;
+        const float* g = ok ? Cm + (int64_t)i * ldcs + col : Cm;
+        cp_async4(&sm.Cs[buf][row * CS_LD + cc], g, ok);
+      }
+    }
+    cp_async_commit();
+  };
+
+  load_chunk(0, 0);
+  for (int ch = 0; ch < nch; ++ch) {
+    const int buf = ch & 1;
+    if (ch + 1 < nch) {
+      load_chunk(ch + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (ch == 0 || k < K) {  // unit-lower mask on the top rows, zero cols >= k
+      const int i0 = ch * RC1;
+      for (int e = tid; e < RC1 * K; e += NT) {
+        const int row = e / K, a = e % K;
+        const int i = i0 + row;
+        if (a >= k || i <= a) {
+          float& s = sm.Vs[buf][row * VS_LD + a];
+          s = vmask(s, i, a, k);
+        }
+      }
+      __syncthreads();
+    }
+    const float* vb = sm.Vs[buf];
+    const float* cb = sm.Cs[buf];
+#pragma unroll
+    for (int rr = kg; rr < RC1; rr += 4) {
+      const float4 v0 = *reinterpret_cast<const float4*>(vb + rr * VS_LD + wa);
+      const float4 v1 = *reinterpret_cast<const float4*>(vb + rr * VS_LD + wa + 4);
+      const float4 cc = *reinterpret_cast<const float4*>(cb + rr * CS_LD + wc);
+      const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      const float cv[4] = {cc.x, cc.y, cc.z, cc.w};
+#pragma unroll
+      for (int x = 0; x < 8; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(vv[x], cv[y], acc[x][y]);
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int x = 0; x < 8; ++x)
+    *reinterpret_cast<float4*>(&sm.Wp[kg][(wa + x) * TC + wc]) =
+        make_float4(acc[x][0], acc[x][1], acc[x][2], acc[x][3]);
+  __syncthreads();
+
+  // ---------------- W <- T^T W ----------------
+  {
+    const int cc = tid & 63;
+    const int ab = (tid >> 6) << 3;
+    float o[8];
+#pragma unroll
+    for (int x = 0; x < 8; ++x) o[x] = 0.f;
+#pragma unroll 4
+    for (int q = 0; q < K; ++q) {
+      const float wq = sm.Wp[0][q * TC + cc] + sm.Wp[1][q * TC + cc] +
+                       sm.Wp[2][q * TC + cc] + sm.Wp[3][q * TC + cc];
+#pragma unroll
+      for (int x = 0; x < 8; ++x) o[x] = fmaf(sm.Ts[q * T_LD + ab + x], wq, o[x]);
+    }
+#pragma unroll
+    for (int x = 0; x < 8; ++x) sm.Ws[(ab + x) * WS_LD + cc] = o[x];
+  }
+
+  // ---------------- pass 2: C -= V W ----------------
+  const int rg = (tid >> 4) << 3;    // chunk rows rg..rg+7
+  const int cg4 = (tid & 15) << 2;   // tile cols cg4..cg4+3
+  const int col = c0 + cg4;
+  for (int i0 = 0; i0 < r; i0 += RC2) {
+    __syncthreads();  // Ws ready (first iteration) / Vt free (later ones)
+    // Stage V rows i0..i0+127 transposed: Vt[a][row].
+#pragma unroll
+    for (int e = 0; e < (RC2 * K) / (4 * NT); ++e) {
+      const int idx = tid + e * NT;
+      const int row = idx & (RC2 - 1), c4 = (idx / RC2) << 2;
+      const int i = i0 + row;
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < r) {
+        const float* g = Vm + (int64_t)i * ldv + c4;
+        if (VEC) {
+          t = __ldg(reinterpret_cast<const float4*>(g));
+        } else {
+          t.x = c4 + 0 < k ? __ldg(g + 0) : 0.f;
+          t.y = c4 + 1 < k ? __ldg(g + 1) : 0.f;
+          t.z = c4 + 2 < k ? __ldg(g + 2) : 0.f;
+          t.w = c4 + 3 < k ? __ldg(g + 3) : 0.f;
+        }
+      }
+      sm.Vt[(c4 + 0) * VT_LD + row] = vmask(t.x, i, c4 + 0, k);
+      sm.Vt[(c4 + 1) * VT_LD + row] = vmask(t.y, i, c4 + 1, k);
+      sm.Vt[(c4 + 2) * VT_LD + row] = vmask(t.z, i, c4 + 2, k);
+      sm.Vt[(c4 + 3) * VT_LD + row] = vmask(t.w, i, c4 + 3, k);
+    }
+    float cv[8][4];
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+      const int i = i0 + rg + x;
+      const float* g = Cm + (int64_t)i * ldcs + col;
+      if (VEC) {
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < r && col < c) t = *reinterpret_cast<const float4*>(g);
+        cv[x][0] = t.x;
+        cv[x][1] = t.y;
+        cv[x][2] = t.z;
+        cv[x][3] = t.w;
+      } else {
+#pragma unroll
+        for (int y = 0; y < 4; ++y) cv[x][y] = (i < r && col + y < c) ? g[y] : 0.f;
+      }
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int a = 0; a < K; ++a) {
+      const float4 w4 = *reinterpret_cast<const float4*>(&sm.Ws[a * WS_LD + cg4]);
+      const float4 v0 = *reinterpret_cast<const float4*>(&sm.Vt[a * VT_LD + rg]);
+      const float4 v1 = *reinterpret_cast<const float4*>(&sm.Vt[a * VT_LD + rg + 4]);
+      const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      const float ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int x = 0; x < 8; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) cv[x][y] = fmaf(-vv[x], ww[y], cv[x][y]);
+    }
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+      const int i = i0 + rg + x;
+      if (i >= r) continue;
+      float* g = Dm + (int64_t)i * ldcd + col;
+      if (VEC) {
+        if (col < c) *reinterpret_cast<float4*>(g) = make_float4(cv[x][0], cv[x][1], cv[x][2], cv[x][3]);
+      } else {
+#pragma unroll
+        for (int y = 0; y < 4; ++y)
+          if (col + y < c) g[y] = cv[x][y];
+      }
+    }
+  }
+}
+
+template <bool VEC>
+int launch_larfb_t(const float* V, int64_t sVb, int64_t ldv, const float* T,
+                   int64_t sTb, int t_ld, const float* Csrc, int64_t sCsb,
+                   int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
+                   int64_t batch, int r, int k, int c, cudaStream_t stream) {
+  static bool attr_set[64] = {};  // per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = sizeof(Smem);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(k_larfb<VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return QRB_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  const dim3 grid((unsigned)((c + TC - 1) / TC), (unsigned)batch, 1);
+  k_larfb<VEC><<<grid, NT, smem, stream>>>(V, sVb, ldv, T, sTb, t_ld, Csrc, sCsb, ldcs,
+                                           Cdst, sCdb, ldcd, r, k, c);
+  note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+int launch_larfb(const float* V, int64_t sVb, int64_t ldv, const float* T,
+                 int64_t sTb, int t_ld, const float* Csrc, int64_t sCsb,
+                 int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
+                 int64_t batch, int r, int k, int c, int tile_c,
+                 cudaStream_t stream) {
+  (void)tile_c;
+  if (r < 1 || k < 1 || k > K || c < 1) return QRB_ERR_UNSUPPORTED;
+  const bool vec = k == K && c % 4 == 0 && ldv % 4 == 0 && sVb % 4 == 0 &&
+                   ldcs % 4 == 0 && sCsb % 4 == 0 && ldcd % 4 == 0 &&
+                   sCdb % 4 == 0 && aligned16(V) && aligned16(Csrc) && aligned16(Cdst);
+  constexpr int64_t kMaxGridY = 65535;
+  for (int64_t b0 = 0; b0 < batch; b0 += kMaxGridY) {
+    const int64_t nb = batch - b0 < kMaxGridY ? batch - b0 : kMaxGridY;
+    const int rc = vec ? launch_larfb_t<true>(V + b0 * sVb, sVb, ldv, T + b0 * sTb, sTb, t_ld,
+                                              Csrc + b0 * sCsb, sCsb, ldcs, Cdst + b0 * sCdb,
+                                              sCdb, ldcd, nb, r, k, c, stream)
+                       : launch_larfb_t<false>(V + b0 * sVb, sVb, ldv, T + b0 * sTb, sTb, t_ld,
+                                               Csrc + b0 * sCsb, sCsb, ldcs, Cdst + b0 * sCdb,
+                                               sCdb, ldcd, nb, r, k, c, stream);
+    if (rc != QRB_OK) return rc;
+  }
+  return QRB_OK;
+}
+
+}  // namespace qrb

@@ -1,0 +1,299 @@
+// Householder factorization of an r x w panel (w <= 32) plus its compact-WY
+// factor T, one thread-block cluster per matrix.
+//
+// Layout: thread t of cluster rank q owns panel rows q*rows_per_cta + t +
+// p*blockDim.x (p < RPT), all 32 columns of each, in registers. Nothing of the
+// panel lives in shared memory; shared memory carries only reductions.
+//
+// One column step j is one 32-slot reduction over the rows below j:
+//     slot[m] = sum_{i>j} x_i * a_im,   x = column j (unscaled)
+// which yields, at once, sigma = slot[j] (the norm below the diagonal), the
+// trailing dot products d_k = a_jk + scale * slot[k] (k > j), and the Gram
+// column G[m][j] = v_m(j) + scale * slot[m] (m < j) used by the T recurrence.
+// The reduction is a warp reduce-scatter (31 shuffles), a cross-warp sum in
+// shared memory, and for clusters a cross-CTA sum over distributed shared
+// memory with one cluster barrier per step (exchange buffers alternate by
+// step parity so no second barrier is needed).
+//
+// Semantics follow the reference panel kernel (src/qrbench/triton_kernels.py
+// :839-871 reflectors and packing, :873-884 unit-lower V, :886-909 forward
+// LARFT recurrence T[i,i] = tau_i, T[:i,i] = -tau_i T[:i,:i] (V[:,:i]^T v_i)).
+#include <cooperative_groups.h>
+
+#include "qrb_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace qrb {
+
+namespace {
+
+constexpr int W = kPanelW;
+constexpr int kMaxThreads = 512;
+
+// Reduce 32 per-lane slot values across a warp; afterwards lane l holds the
+// warp total of slot l in v[0]. 16+8+4+2+1 shuffles.
+__device__ __forceinline__ void reduce_scatter32(float (&v)[W], int lane) {
+#pragma unroll
+  for (int half = 16; half >= 1; half >>= 1) {
+    const bool upper = (lane & half) != 0;
+#pragma unroll
+    for (int q = 0; q < half; ++q) {
+      const float keep = upper ? v[q + half] : v[q];
+      const float send = upper ? v[q] : v[q + half];
+      v[q] = keep + __shfl_xor_sync(kFull, send, half);
+    }
+  }
+}
+
+template <int RPT>
+__global__ void __launch_bounds__(kMaxThreads, 1)
+k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
+        float* __restrict__ dst, int64_t sb_dst, int64_t ld_dst,
+        float* __restrict__ tau_out, int64_t tau_sb, float* __restrict__ T_out,
+        int64_t T_sb, int t_ld, float* __restrict__ V_out, int r, int w,
+        int cs, int vec_src, int vec_dst) {
+  __shared__ float red[kMaxThreads / 32][W];
+  __shared__ float xch[2][2][W];  // [parity][0 = slot sums, 1 = row j]
+  __shared__ float fco[W];        // tau_j * d_k for trailing columns k > j
+  __shared__ float coef[4];       // beta, tau, scale
+  __shared__ float Gs[W][W + 1];  // Gram V^T V, strictly upper part
+  __shared__ float taus[W];
+
+  const int nt = blockDim.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = nt >> 5;
+  int rank = 0;
+  if (cs > 1) rank = (int)cg::this_cluster().block_rank();
+  const int64_t m = blockIdx.x / cs;
+  const int row0 = rank * nt * RPT;
+
+  for (int e = tid; e < W * (W + 1); e += nt) (&Gs[0][0])[e] = 0.f;
+  if (tid < W) taus[tid] = 0.f;
+
+  float a[RPT][W];
+  const float* __restrict__ S = src + m * sb_src;
+#pragma unroll
+  for (int p = 0; p < RPT; ++p) {
+    const int i = row0 + tid + p * nt;
+    const float* rowp = S + (int64_t)i * ld_src;
+    if (i < r && vec_src) {
+#pragma unroll
+      for (int c4 = 0; c4 < W / 4; ++c4) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(rowp) + c4);
+        a[p][4 * c4 + 0] = t.x;
+        a[p][4 * c4 + 1] = t.y;
+        a[p][4 * c4 + 2] = t.z;
+        a[p][4 * c4 + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < W; ++c) a[p][c] = (i < r && c < w) ? __ldg(rowp + c) : 0.f;
+    }
+  }
+  __syncthreads();
+
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    if (j >= w) break;  // uniform across the cluster
+    const int par = j & 1;
+
+    // Phase A: slot partials over this thread's rows below j.
+    float sl[W];
+#pragma unroll
+    for (int q = 0; q < W; ++q) sl[q] = 0.f;
+#pragma unroll
+    for (int p = 0; p < RPT; ++p) {
+      const int i = row0 + tid + p * nt;
+      const float x = (i > j) ? a[p][j] : 0.f;
+#pragma unroll
+      for (int q = 0; q < W; ++q) sl[q] = fmaf(x, a[p][q], sl[q]);
+      if (i == j) {
+#pragma unroll
+        for (int q = 0; q < W; ++q) xch[par][1][q] = a[p][q];
+      }
+    }
+    reduce_scatter32(sl, lane);
+    red[warp][lane] = sl[0];
+    __syncthreads();
+
+    float tot = 0.f, rowv = 0.f;
+    if (warp == 0) {
+      for (int w2 = 0; w2 < nwarps; ++w2) tot += red[w2][lane];
+      xch[par][0][lane] = tot;
+    }
+    if (cs > 1) {
+      cg::this_cluster().sync();
+      if (warp == 0) {
+        tot = 0.f;
+        for (int q = 0; q < cs; ++q)
+          tot += cg::this_cluster().map_shared_rank(&xch[par][0][0], q)[lane];
+        rowv = cg::this_cluster().map_shared_rank(&xch[par][1][0], 0)[lane];
+      }
+    } else if (warp == 0) {
+      rowv = xch[par][1][lane];
+    }
+
+    if (warp == 0) {
+      const float sigma = __shfl_sync(kFull, tot, j);
+      const float alpha = __shfl_sync(kFull, rowv, j);
+      const Reflector h = make_reflector(alpha, sigma);
+      const float d = fmaf(h.scale, tot, rowv);
+      if (lane > j) fco[lane] = h.tau * d;
+      if (lane < j) Gs[lane][j] = d;
+      if (lane == 0) {
+        coef[0] = h.beta;
+        coef[1] = h.tau;
+        coef[2] = h.scale;
+        taus[j] = h.tau;
+      }
+    }
+    __syncthreads();
+
+    // Phase B: apply H_j to this thread's rows of the trailing columns.
+    const float beta = coef[0];
+    const float scale = coef[2];
+#pragma unroll
+    for (int p = 0; p < RPT; ++p) {
+      const int i = row0 + tid + p * nt;
+      if (i > j) {
+        const float v = a[p][j] * scale;
+#pragma unroll
+        for (int k = j + 1; k < W; ++k) a[p][k] = fmaf(-fco[k], v, a[p][k]);
+        a[p][j] = v;
+      } else if (i == j) {
+#pragma unroll
+        for (int k = j + 1; k < W; ++k) a[p][k] -= fco[k];
+        a[p][j] = beta;
+      }
+    }
+  }
+
+  // Write the factored panel rows back (R on/above the diagonal, v below).
+  float* __restrict__ D = dst + m * sb_dst;
+#pragma unroll
+  for (int p = 0; p < RPT; ++p) {
+    const int i = row0 + tid + p * nt;
+    if (i >= r) continue;
+    float* rowp = D + (int64_t)i * ld_dst;
+    if (vec_dst) {
+#pragma unroll
+      for (int c4 = 0; c4 < W / 4; ++c4)
+        reinterpret_cast<float4*>(rowp)[c4] =
+            make_float4(a[p][4 * c4], a[p][4 * c4 + 1], a[p][4 * c4 + 2], a[p][4 * c4 + 3]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < W; ++c)
+        if (c < w) rowp[c] = a[p][c];
+    }
+    if (V_out != nullptr) {
+      float* vrow = V_out + m * (int64_t)r * w + (int64_t)i * w;
+#pragma unroll
+      for (int c = 0; c < W; ++c)
+        if (c < w) vrow[c] = (i > c) ? a[p][c] : (i == c ? 1.f : 0.f);
+    }
+  }
+
+  if (rank == 0) {
+    if (tid < w) tau_out[m * tau_sb + tid] = taus[tid];
+    if (warp == 0 && T_out != nullptr) {
+      // Forward LARFT: lane `row` computes row `row` of T.
+      const int row = lane;
+      float trow[W];
+#pragma unroll
+      for (int i = 0; i < W; ++i) {
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < i; ++q) t = fmaf(trow[q], Gs[q][i], t);
+        trow[i] = row < i ? -taus[i] * t : (row == i ? taus[i] : 0.f);
+      }
+      if (row < w) {
+        float* Tm = T_out + m * T_sb + (int64_t)row * t_ld;
+#pragma unroll
+        for (int i = 0; i < W; ++i)
+          if (i < t_ld && (t_ld == W || i < w)) Tm[i] = (i < w) ? trow[i] : 0.f;
+      } else if (t_ld == W) {
+        float* Tm = T_out + m * T_sb + (int64_t)row * t_ld;
+#pragma unroll
+        for (int i = 0; i < W; ++i) Tm[i] = 0.f;
+      }
+    }
+  }
+  if (cs > 1) cg::this_cluster().sync();  // peers may still read our xch
+}
+
+template <int RPT>
+int launch_panel_rpt(const float* src, int64_t sb_src, int64_t ld_src,
+                     float* dst, int64_t sb_dst, int64_t ld_dst, float* tau_out,
+                     int64_t tau_sb, float* T_out, int64_t T_sb, int t_ld,
+                     float* V_out, int64_t batch, int r, int w, int cs,
+                     int nt, cudaStream_t stream) {
+  const bool vec_src = w == W && ld_src % 4 == 0 && sb_src % 4 == 0 &&
+                       (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  const bool vec_dst = w == W && ld_dst % 4 == 0 && sb_dst % 4 == 0 &&
+                       (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(batch * cs), 1, 1);
+  cfg.blockDim = dim3((unsigned)nt, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cs > 1 ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(
+      &cfg, k_panel<RPT>, src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
+      tau_sb, T_out, T_sb, t_ld, V_out, r, w, cs, (int)vec_src, (int)vec_dst);
+  note_launches(1);
+  return e == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
+}
+
+}  // namespace
+
+// Rows per thread 2 above 256 rows, else 1; CTAs of up to 512 threads; a
+// cluster of cs CTAs (a power of two, <= 8 for the launch to be accepted)
+// covers the panel's rows.
+static void panel_shape(int r, int* rpt, int* cs, int* nt) {
+  const int R = r > 256 ? 2 : 1;
+  const int per_cta_max = kMaxThreads * R;
+  const int need = (r + per_cta_max - 1) / per_cta_max;
+  int c = 1;
+  while (c < need) c <<= 1;  // cluster sizes 1, 2, 4, 8
+  int threads = (r + R * c - 1) / (R * c);
+  threads = ((threads + 31) / 32) * 32;
+  if (threads < 32) threads = 32;
+  *rpt = R;
+  *cs = c;
+  *nt = threads;
+}
+
+int panel_cluster_size(int r) {
+  int rpt, cs, nt;
+  panel_shape(r, &rpt, &cs, &nt);
+  return cs;
+}
+
+int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
+                 int64_t sb_dst, int64_t ld_dst, float* tau_out, int64_t tau_sb,
+                 float* T_out, int64_t T_sb, int t_ld, float* V_out,
+                 int64_t batch, int r, int w, cudaStream_t stream) {
+  if (r < 1 || w < 1 || w > W) return QRB_ERR_UNSUPPORTED;
+  int rpt, cs, nt;
+  panel_shape(r, &rpt, &cs, &nt);
+  if (cs > kMaxCluster) return QRB_ERR_UNSUPPORTED;
+  if (batch * cs > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
+  if (rpt == 1)
+    return launch_panel_rpt<1>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
+                               tau_sb, T_out, T_sb, t_ld, V_out, batch, r, w, cs,
+                               nt, stream);
+  return launch_panel_rpt<2>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
+                             tau_sb, T_out, T_sb, t_ld, V_out, batch, r, w, cs,
+                             nt, stream);
+}
+
+}  // namespace qrb

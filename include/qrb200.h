@@ -1,0 +1,147 @@
+/*
+ * qrb200.h — C ABI of libqrb200.so, a B200-native (sm_100a) batched FP32
+ * compact-Householder QR factorization with torch.geqrf / LAPACK sgeqrf
+ * semantics.
+ *
+ * Layout conventions shared by every entry point:
+ *   - Matrices are batched, row-major, FP32: element (i, j) of matrix m lives at
+ *     base + m * stride_b + i * stride_row + j (the column stride is 1).
+ *   - All pointers are device pointers; `stream` is a cudaStream_t (NULL = the
+ *     legacy default stream). Work is enqueued stream-ordered and the call
+ *     returns without synchronising.
+ *   - The library allocates no device memory per call. Scratch space, when an
+ *     entry point needs it, is passed in by the caller (see
+ *     qrb_workspace_bytes).
+ *   - Every entry point returns a qrb_status code. Argument errors are detected
+ *     on the host before anything is enqueued. There is no CPU fallback.
+ *
+ * Output convention (identical to torch.geqrf): for A = Q R with
+ * Q = H_0 H_1 ... H_{n-1}, H_j = I - tau_j v_j v_j^T, v_j(j) = 1 implicit,
+ * the output H holds R on and above the diagonal and the essential part of v_j
+ * below the diagonal of column j; tau[j] = tau_j; beta = -sign(alpha)*||x||
+ * (alpha >= 0 gives a negative diagonal); a column with nothing below the
+ * diagonal to annihilate gets tau = 0.
+ */
+#ifndef QRB200_H
+#define QRB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QRB_API __attribute__((visibility("default")))
+#else
+#define QRB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+enum {
+  QRB_OK = 0,
+  QRB_ERR_INVALID_ARG = 1,   /* null pointer, negative size, bad stride, ... */
+  QRB_ERR_UNSUPPORTED = 2,   /* size outside what the kernels handle */
+  QRB_ERR_WORKSPACE = 3,     /* workspace missing or smaller than required */
+  QRB_ERR_LAUNCH = 4,        /* a kernel launch failed (cudaGetLastError) */
+  QRB_ERR_DEVICE = 5,        /* no usable sm_100 device / device query failed */
+  QRB_ERR_INJECTED = 6       /* failure injected by qrb_set_config("fail_next") */
+};
+
+/* Library version as 10000*major + 100*minor + patch. */
+QRB_API int qrb_version(void);
+
+/* Human-readable text for a status code (static storage, never NULL). */
+QRB_API const char* qrb_status_string(int status);
+
+/* Largest n that qrb_geqrf_f32 accepts. */
+QRB_API int32_t qrb_max_n(void);
+
+/* Bytes of device workspace qrb_geqrf_f32 needs for (batch, n); 0 when the
+ * size is handled without scratch memory. */
+QRB_API size_t qrb_workspace_bytes(int64_t batch, int32_t n);
+
+/*
+ * Batched square QR: the full hot path, one call per factorization.
+ * Replaces the reference's registered impl callable
+ *   impl(A: [b, n, n] fp32) -> (H, tau)
+ * (src/qrbench/reference.py:15 QRImpl; src/qrbench/variants.py:876-917
+ * make_hh_panel_tuned(...).impl, the CHAMPION at variants.py:106), including
+ * its dispatch between the fused small-n kernel and the blocked panel route.
+ *
+ *   A      input, batch x n x n, strides (strideA_b, strideA_row), read only.
+ *   H      output, batch x n x n contiguous (stride n*n, row stride n).
+ *          H may equal A only when A is itself contiguous (in-place mode).
+ *   tau    output, batch x n contiguous.
+ */
+QRB_API int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
+                  float* H, float* tau, int64_t batch, int32_t n,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Fused whole-matrix QR for small n (n <= 32): one warp factors one matrix in
+ * registers with a single launch. Replaces hh_fused_qr / _hh_fused_qr_kernel
+ * (src/qrbench/triton_kernels.py:722-755, :641-720).
+ */
+QRB_API int qrb_fused_qr_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
+                     float* H, float* tau, int64_t batch, int32_t n,
+                     void* stream);
+
+/* Largest n accepted by qrb_fused_qr_f32. */
+QRB_API int32_t qrb_fused_max_n(void);
+
+/*
+ * Householder factorization of a batch of r x w panels (w <= 32) plus the
+ * compact-WY factor T. Replaces hh_panel_qr / _hh_panel_kernel
+ * (src/qrbench/triton_kernels.py:912-967, :787-910).
+ *
+ *   P      input panels, batch x r x w, strides (strideP_b, strideP_row).
+ *   H      output, batch x r x w contiguous: R in the top w x w upper triangle,
+ *          essential reflectors strictly below the diagonal.
+ *   V      optional output (NULL to skip), batch x r x w contiguous: unit lower
+ *          reflector matrix (1 on the diagonal, 0 above).
+ *   tau    output, batch x w contiguous.
+ *   T      output, batch x w x w contiguous, upper triangular, with
+ *          Q = I - V T V^T (forward, column-wise LARFT).
+ */
+QRB_API int qrb_panel_qr_f32(const float* P, int64_t strideP_b, int64_t strideP_row,
+                     float* H, float* V, float* tau, float* T,
+                     int64_t batch, int32_t r, int32_t w, void* stream);
+
+/*
+ * Block-reflector trailing update C <- C - V (T^T (V^T C)), applying Q^T of a
+ * factored panel to the trailing columns. Replaces the three batched GEMMs of
+ * _hh_panel_blocked_qr (src/qrbench/variants.py:800-804).
+ *
+ *   V      reflectors, batch x r x k (k <= 32), strides (strideV_b,
+ *          strideV_row). Only the strictly lower part is read: the diagonal is
+ *          taken as 1 and the upper part as 0, so V may point into a packed H.
+ *   T      batch x k x k contiguous (stride k*k), upper triangular.
+ *   C      batch x r x c, strides (strideC_b, strideC_row), updated in place.
+ */
+QRB_API int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row,
+                  const float* T, float* C, int64_t strideC_b,
+                  int64_t strideC_row, int64_t batch, int32_t r, int32_t k,
+                  int32_t c, void* stream);
+
+/*
+ * Tuning and test hooks (never needed for correct use). Keys:
+ *   "fail_next"   value v > 0: the next v calls of any compute entry point
+ *                 return QRB_ERR_INJECTED without enqueuing work (host-side
+ *                 fault injection for tests).
+ *   "sync_check"  1: every compute call synchronises its stream and reports
+ *                 asynchronous kernel faults as QRB_ERR_LAUNCH (debug mode).
+ *   "larfb_tc"    column-tile width of the trailing update (64).
+ *   "launches"    number of kernel launches this library has enqueued since
+ *                 load or since the last qrb_set_config("launches", 0).
+ * Returns QRB_ERR_INVALID_ARG for an unknown key or value.
+ */
+QRB_API int qrb_set_config(const char* key, int64_t value);
+QRB_API int qrb_get_config(const char* key, int64_t* value);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QRB200_H */

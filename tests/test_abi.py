@@ -1,0 +1,116 @@
+"""The C ABI loads, exports what include/qrb200.h declares, and validates its
+arguments on the host (no GPU work is enqueued by anything in this file)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+
+import pytest
+from conftest import REPO
+
+from gpumode_qr_b200 import _lib
+from gpumode_qr_b200.build import LIB_PATH
+
+HEADER = REPO / "include" / "qrb200.h"
+FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails or returns early
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"QRB_API\s+[\w\s\*]+?\b(qrb_\w+)\s*\(", text)
+
+
+def test_header_declares_the_expected_entry_points():
+    assert set(declared_symbols()) == {
+        "qrb_version", "qrb_status_string", "qrb_max_n", "qrb_workspace_bytes", "qrb_geqrf_f32",
+        "qrb_fused_qr_f32", "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32",
+        "qrb_set_config", "qrb_get_config",
+    }
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB_PATH)], capture_output=True, text=True)
+    exported = set(re.findall(r"\b(qrb_\w+)\b", out.stdout))
+    for name in declared_symbols():
+        assert name in exported, name
+        assert hasattr(L, name)
+        assert name in _lib.SIGNATURES
+    # nothing else leaks out of the library with a qrb_ prefix
+    assert exported == set(declared_symbols())
+
+
+def test_status_strings_and_constants():
+    L = _lib.lib()
+    assert L.qrb_version() >= 100
+    for code in range(7):
+        s = _lib.status_string(code)
+        assert s.startswith("qrb:")
+    assert "unknown" in _lib.status_string(99)
+    assert L.qrb_max_n() == 8192
+    assert L.qrb_fused_max_n() == 32
+
+
+def test_workspace_bytes():
+    L = _lib.lib()
+    assert L.qrb_workspace_bytes(4096, 32) == 0
+    assert L.qrb_workspace_bytes(8, 64) == 8 * 32 * 32 * 4
+    assert L.qrb_workspace_bytes(0, 512) == 0
+
+
+def test_argument_validation_without_gpu():
+    L = _lib.lib()
+    ws = ctypes.c_void_p(0x2000)
+    # empty problems succeed without touching memory
+    assert L.qrb_geqrf_f32(None, 0, 0, None, None, 0, 64, None, 0, None) == 0
+    assert L.qrb_geqrf_f32(None, 0, 0, None, None, 4, 0, None, 0, None) == 0
+    # negative sizes, null pointers, overlapping strides
+    assert L.qrb_geqrf_f32(FAKE, 4096, 64, FAKE, FAKE, -1, 64, ws, 1 << 20, None) == 1
+    assert L.qrb_geqrf_f32(None, 4096, 64, FAKE, FAKE, 1, 64, ws, 1 << 20, None) == 1
+    assert L.qrb_geqrf_f32(FAKE, 4096, 63, FAKE, FAKE, 1, 64, ws, 1 << 20, None) == 1
+    assert L.qrb_geqrf_f32(FAKE, 100, 64, FAKE, FAKE, 2, 64, ws, 1 << 20, None) == 1
+    # too large
+    assert L.qrb_geqrf_f32(FAKE, 8193 * 8193, 8193, FAKE, FAKE, 1, 8193, ws, 1 << 30, None) == 2
+    # blocked path needs workspace
+    assert L.qrb_geqrf_f32(FAKE, 4096, 64, FAKE, FAKE, 2, 64, None, 0, None) == 3
+    assert L.qrb_geqrf_f32(FAKE, 4096, 64, FAKE, FAKE, 2, 64, ws, 100, None) == 3
+    # in-place requires a contiguous A
+    assert L.qrb_geqrf_f32(FAKE, 8192, 128, FAKE, FAKE, 2, 64, ws, 1 << 20, None) == 1
+    # kernel-level entry points
+    assert L.qrb_fused_qr_f32(FAKE, 64 * 64, 64, FAKE, FAKE, 1, 64, None) == 2
+    assert L.qrb_panel_qr_f32(FAKE, 100 * 33, 33, FAKE, None, FAKE, FAKE, 1, 100, 33, None) == 2
+    assert L.qrb_panel_qr_f32(FAKE, 100, 10, FAKE, None, FAKE, FAKE, 1, 5, 10, None) == 2
+    assert L.qrb_larfb_f32(FAKE, 64 * 8, 8, None, FAKE, 64 * 8, 8, 1, 64, 8, 8, None) == 1
+    assert L.qrb_larfb_f32(FAKE, 64 * 40, 40, FAKE, FAKE, 64 * 8, 8, 1, 64, 40, 8, None) == 2
+
+
+def test_fault_injection_is_host_side():
+    # "fail_next" makes the next compute call fail before anything is enqueued.
+    L = _lib.lib()
+    ws = ctypes.c_void_p(0x2000)
+    _lib.set_config("fail_next", 2)
+    assert _lib.get_config("fail_next") == 2
+    assert L.qrb_geqrf_f32(FAKE, 4096, 64, FAKE, FAKE, 2, 64, ws, 1 << 20, None) == 6
+    assert L.qrb_fused_qr_f32(FAKE, 32 * 32, 32, FAKE, FAKE, 2, 32, None) == 6
+    assert _lib.get_config("fail_next") == 0
+    with pytest.raises(_lib.QRBError) as ei:
+        _lib.check(6)
+    assert ei.value.status == 6 and "injected" in str(ei.value)
+
+
+def test_config_keys():
+    assert _lib.get_config("sync_check") == 0
+    _lib.set_config("sync_check", 1)
+    assert _lib.get_config("sync_check") == 1
+    _lib.set_config("sync_check", 0)
+    _lib.set_config("launches", 0)
+    assert _lib.get_config("launches") == 0
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("no_such_key", 1)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("sync_check", 7)
+    with pytest.raises(_lib.QRBError):
+        _lib.get_config("no_such_key")
+

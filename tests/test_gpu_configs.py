@@ -1,0 +1,42 @@
+"""The five workload configs on the GPU: FP64 gates on every config, elementwise
+parity vs the reference's oracle (CPU torch.geqrf, LAPACK) on the configs with
+cond <= 1e2 (1, 2, 3, 5) within the north-star tolerance 1e-3 relative.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from gpumode_qr_b200 import api, checker, inputs
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+NORTH_STAR_RTOL = 1e-3
+
+
+@pytest.mark.parametrize("idx", [1, 2, 3, 4, 5])
+def test_config_gates_and_parity(idx):
+    cfg = inputs.config(idx)
+    A_cpu = inputs.make_config_input(cfg)
+    A = A_cpu.to(DEV)
+    H, tau = api.geqrf(A)
+    torch.cuda.synchronize()
+    gate = checker.check(A, H, tau)
+    assert gate.passed, (cfg.name, gate.as_dict())
+    if cfg.parity:
+        sub = slice(0, min(cfg.batch, 64))  # bound the CPU oracle's time
+        Hl, tl = oracle.lapack_geqrf(A_cpu[sub])
+        par = checker.parity(H[sub].cpu(), tau[sub].cpu(), Hl, tl)
+        assert par.ok(NORTH_STAR_RTOL), (cfg.name, par)
+
+
+def test_config_results_are_reproducible():
+    cfg = inputs.config(2)
+    A = inputs.make_config_input(cfg).to(DEV)
+    H1, t1 = api.geqrf(A)
+    H2, t2 = api.geqrf(A)
+    torch.cuda.synchronize()
+    assert torch.equal(H1, H2) and torch.equal(t1, t2)

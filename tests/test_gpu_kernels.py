@@ -1,0 +1,128 @@
+"""GPU parity of each kernel family through the C ABI against the oracle.
+
+Tolerances: H and tau within 1e-4 of the reference's outputs relative to
+max|H| (FP32 rounding-level; the north-star bar is 1e-3), T within 1e-4
+absolute, trailing update within 1e-5 relative to max|C| of the FP64 oracle.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import golden_cases
+
+import oracle
+from gpumode_qr_b200 import _lib, api, checker
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+RTOL = 1e-4
+
+
+def _rel(x, ref):
+    x = x.detach().cpu().numpy() if hasattr(x, "detach") else x
+    return float(np.abs(x - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def test_fused_kernel_matches_reference_kernel(ref_fused):
+    for case in golden_cases(ref_fused):
+        A = torch.from_numpy(ref_fused[f"{case}_A"])
+        if A.shape[-1] > api.fused_max_n():
+            continue
+        H, tau = api.hh_fused_qr(A.to(DEV))
+        gate = checker.check(A, H.cpu(), tau.cpu())
+        assert gate.passed, (case, gate.as_dict())
+        if case == "rank4":
+            continue  # reflectors of a rank-deficient matrix are not unique
+        assert _rel(H, ref_fused[f"{case}_H"]) < RTOL, case
+        assert np.abs(tau.cpu().numpy() - ref_fused[f"{case}_tau"]).max() < RTOL, case
+
+
+@pytest.mark.parametrize("n", list(range(1, 33)))
+def test_fused_kernel_every_small_n(n):
+    A = torch.randn(37, n, n, generator=torch.Generator().manual_seed(n))
+    H, tau = api.hh_fused_qr(A.to(DEV))
+    Ho, to = oracle.geqr2(A.numpy(), f64=True)
+    par = checker.parity(H.cpu(), tau.cpu(), Ho, to)
+    assert par.ok(RTOL), (n, par)
+    assert checker.check(A, H.cpu(), tau.cpu()).passed
+    if n == 1:
+        assert (tau == 0).all()
+    assert (tau[:, -1] == 0).all()
+
+
+def test_panel_kernel_matches_reference_kernel(ref_panel):
+    for case in golden_cases(ref_panel):
+        P = torch.from_numpy(ref_panel[f"{case}_P"])
+        H, V, tau, T = api.hh_panel_qr(P.to(DEV))
+        assert _rel(H, ref_panel[f"{case}_H"]) < RTOL, case
+        assert np.abs(V.cpu().numpy() - ref_panel[f"{case}_V"]).max() < RTOL, case
+        assert np.abs(tau.cpu().numpy() - ref_panel[f"{case}_tau"]).max() < RTOL, case
+        assert np.abs(T.cpu().numpy() - ref_panel[f"{case}_T"]).max() < RTOL, case
+
+
+@pytest.mark.parametrize("r,w", [(32, 32), (33, 32), (64, 32), (257, 32), (512, 32), (513, 32),
+                                 (1024, 32), (1500, 32), (2048, 32), (3000, 32), (4096, 32),
+                                 (8192, 32), (100, 7), (2049, 16), (40, 1)])
+def test_panel_kernel_shapes_and_clusters(r, w):
+    b = 3 if r <= 4096 else 1
+    P = torch.randn(b, r, w, generator=torch.Generator().manual_seed(r + w))
+    H, V, tau, T = api.hh_panel_qr(P.to(DEV))
+    Ho, Vo, to, To = oracle.panel(P.numpy(), f64=True)
+    assert _rel(H, Ho) < RTOL
+    assert np.abs(V.cpu().numpy() - Vo).max() < RTOL
+    assert np.abs(tau.cpu().numpy() - to).max() < RTOL
+    assert np.abs(T.cpu().numpy() - To).max() < 5 * RTOL
+    # algebra: Q^T P reproduces triu(H) and Q = I - V T V^T is orthonormal on V's span
+    Vd, Td, Pd = V.double().cpu(), T.double().cpu(), P.double()
+    R = Pd - Vd @ (Td.transpose(1, 2) @ (Vd.transpose(1, 2) @ Pd))
+    assert (R[:, :w] - torch.triu(H.double().cpu()[:, :w])).abs().max() < 1e-4 * Pd.abs().max()
+    assert R[:, w:].abs().max() < 1e-4 * Pd.abs().max()
+
+
+@pytest.mark.parametrize("r,k,c", [(64, 32, 64), (64, 32, 1), (100, 32, 37), (512, 32, 480),
+                                   (4096, 32, 200), (33, 32, 5), (50, 8, 13), (129, 31, 70),
+                                   (300, 1, 3)])
+def test_larfb_kernel_matches_fp64(r, k, c):
+    g = torch.Generator().manual_seed(r * 7 + k + c)
+    b = 3
+    Vfull = torch.randn(b, r, k, generator=g)
+    Vexp = torch.tril(Vfull, -1) + torch.eye(r, k)
+    T = torch.triu(torch.randn(b, k, k, generator=g)) * 0.5
+    C = torch.randn(b, r, c, generator=g)
+    want = oracle.larfb(Vexp.numpy(), T.numpy(), C.numpy(), f64=True)
+    # V is passed with garbage on and above the diagonal: only the strict lower part is read
+    Cd = C.to(DEV)
+    api.larfb(Vfull.to(DEV), T.to(DEV), Cd)
+    assert _rel(Cd, want) < 1e-5
+
+
+def test_larfb_strided_views_inside_a_matrix():
+    # V and C as views into one packed matrix, as the blocked driver uses them
+    g = torch.Generator().manual_seed(9)
+    n, j0 = 200, 64
+    Hm = torch.randn(2, n, n, generator=g)
+    V = Hm[:, j0:, j0:j0 + 32]
+    C = Hm[:, j0:, j0 + 32:]
+    T = torch.triu(torch.randn(2, 32, 32, generator=g)) * 0.3
+    Vexp = torch.tril(V, -1) + torch.eye(n - j0, 32)
+    want = oracle.larfb(Vexp.numpy(), T.numpy(), C.numpy(), f64=True)
+    Hd = Hm.to(DEV)
+    api.larfb(Hd[:, j0:, j0:j0 + 32], T.to(DEV), Hd[:, j0:, j0 + 32:])
+    got = Hd[:, j0:, j0 + 32:].cpu().numpy()
+    assert np.abs(got - want).max() / np.abs(want).max() < 1e-5
+    # everything outside C untouched
+    mask = torch.ones(2, n, n, dtype=torch.bool)
+    mask[:, j0:, j0 + 32:] = False
+    assert torch.equal(Hd.cpu()[mask], Hm[mask])
+
+
+def test_launch_counter_counts_kernels():
+    A = torch.randn(4, 96, 96, device=DEV)
+    torch.cuda.synchronize()
+    _lib.set_config("launches", 0)
+    api.geqrf(A)
+    torch.cuda.synchronize()
+    # 3 panels + 2 trailing updates
+    assert _lib.get_config("launches") == 5
