@@ -78,7 +78,8 @@ def test_panel_kernel_shapes_and_clusters(r, w):
     Vd, Td, Pd = V.double().cpu(), T.double().cpu(), P.double()
     R = Pd - Vd @ (Td.transpose(1, 2) @ (Vd.transpose(1, 2) @ Pd))
     assert (R[:, :w] - torch.triu(H.double().cpu()[:, :w])).abs().max() < 1e-4 * Pd.abs().max()
-    assert R[:, w:].abs().max() < 1e-4 * Pd.abs().max()
+    if r > w:
+        assert R[:, w:].abs().max() < 1e-4 * Pd.abs().max()
 
 
 @pytest.mark.parametrize("r,k,c", [(64, 32, 64), (64, 32, 1), (100, 32, 37), (512, 32, 480),
