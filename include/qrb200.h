@@ -80,6 +80,27 @@ QRB_API int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row
                   void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * qrb_geqrf_f32 for callers that cannot allocate device memory (a fixed
+ * memory budget reserved up front, a host application that owns the only
+ * allocator, a runtime that forbids cudaMalloc after start-up). It has no
+ * counterpart in the reference. Same arguments and results as qrb_geqrf_f32
+ * minus the workspace: the scratch it needs lives in a 4 MiB array built into
+ * the library, which every GPU that loads the library holds until the process
+ * exits. It allocates nothing.
+ *   - Limit: for n > 32 at most 1024 matrices per call (one 4 KiB T factor
+ *     each); a larger batch returns QRB_ERR_UNSUPPORTED before any work is
+ *     enqueued. n <= 32 needs no scratch and has no batch limit.
+ *   - The first call on a device looks up the array's device address; make it
+ *     before any stream capture starts.
+ *   - All calls on a device share the array: calls whose GPU work overlaps
+ *     (unordered streams) race and give wrong results. Nothing in the array
+ *     has to be cleared between calls.
+ */
+QRB_API int qrb_geqrf_f32_noalloc(const float* A, int64_t strideA_b,
+                                  int64_t strideA_row, float* H, float* tau,
+                                  int64_t batch, int32_t n, void* stream);
+
+/*
  * Fused whole-matrix QR for small n (n <= 32): one warp factors one matrix in
  * registers with a single launch. Replaces hh_fused_qr / _hh_fused_qr_kernel
  * (src/qrbench/triton_kernels.py:722-755, :641-720).

@@ -25,7 +25,7 @@ def declared_symbols() -> list[str]:
 def test_header_declares_the_expected_entry_points():
     assert set(declared_symbols()) == {
         "qrb_version", "qrb_status_string", "qrb_max_n", "qrb_workspace_bytes", "qrb_geqrf_f32",
-        "qrb_fused_qr_f32", "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32",
+        "qrb_geqrf_f32_noalloc", "qrb_fused_qr_f32", "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32",
         "qrb_set_config", "qrb_get_config",
     }
 
