@@ -138,17 +138,19 @@ def geqrf_out(A: torch.Tensor, H: torch.Tensor, tau: torch.Tensor) -> tuple[torc
 
 
 def geqrf_host(A_host: torch.Tensor, H_host: torch.Tensor, tau_host: torch.Tensor,
-               device: torch.device | int | str = "cuda", chunks: int = 4) -> None:
+               device: torch.device | int | str = "cuda", chunks: int = 8) -> None:
     """Factor a host-resident batch end to end: host -> device -> QR -> host.
 
     ``A_host`` ``[b, n, n]``, ``H_host`` ``[b, n, n]`` and ``tau_host`` ``[b, n]``
     are contiguous float32 CPU tensors, ideally pinned (then every copy is
-    asynchronous). The batch is split into ``chunks`` pieces that alternate
-    between two CUDA streams, so the host-to-device copy of one piece, the
-    factorization of another and the device-to-host copy of a third overlap.
-    Work is ordered after, and the call's completion is joined back into, the
-    device's current stream; synchronise that stream before reading the
-    outputs on the host.
+    asynchronous). The batch is split into ``chunks`` pieces and run as a
+    three-stage pipeline on three streams of the device: all host-to-device
+    copies back to back on a copy-in stream, each piece's factorization on a
+    compute stream once its copy has landed, and its device-to-host copy on a
+    copy-out stream once it is factored. The two copy directions run at the
+    same time on separate copy engines. Work is ordered after, and its
+    completion joined back into, the device's current stream; synchronise that
+    stream before reading the outputs on the host.
     """
     dev = torch.device(device)
     if dev.type != "cuda":
@@ -166,37 +168,40 @@ def geqrf_host(A_host: torch.Tensor, H_host: torch.Tensor, tau_host: torch.Tenso
     if b == 0 or n == 0:
         return
     chunks = max(1, min(int(chunks), b))
+    per = (b + chunks - 1) // chunks
     with torch.cuda.device(dev):
         main = torch.cuda.current_stream(dev)
-        streams = _host_streams(dev)
-        start = torch.cuda.Event()
-        start.record(main)
+        s_in, s_comp, s_out = _host_streams(dev)
         A_d = torch.empty((b, n, n), dtype=torch.float32, device=dev)
         H_d = torch.empty((b, n, n), dtype=torch.float32, device=dev)
         t_d = torch.empty((b, n), dtype=torch.float32, device=dev)
-        ws_n = workspace_bytes((b + chunks - 1) // chunks, n)
-        wss = [torch.empty(max(ws_n, 16), dtype=torch.uint8, device=dev) for _ in streams]
+        ws_n = workspace_bytes(per, n)
+        ws = torch.empty(max(ws_n, 16), dtype=torch.uint8, device=dev)
         L = _lib.lib()
-        per = (b + chunks - 1) // chunks
-        for ci, s0 in enumerate(range(0, b, per)):
+        for st in (s_in, s_comp, s_out):
+            st.wait_stream(main)
+        for s0 in range(0, b, per):
             s1 = min(b, s0 + per)
-            st = streams[ci % len(streams)]
-            st.wait_event(start)
-            with torch.cuda.stream(st):
+            landed = torch.cuda.Event()
+            factored = torch.cuda.Event()
+            with torch.cuda.stream(s_in):
                 A_d[s0:s1].copy_(A_host[s0:s1], non_blocking=True)
-                ws = wss[ci % len(streams)]
-                rc = L.qrb_geqrf_f32(
-                    A_d[s0:s1].data_ptr(), n * n, n, H_d[s0:s1].data_ptr(), t_d[s0:s1].data_ptr(),
-                    s1 - s0, n, ws.data_ptr(), ws_n, st.cuda_stream,
-                )
-                _lib.check(rc)
+                landed.record(s_in)
+            s_comp.wait_event(landed)
+            rc = L.qrb_geqrf_f32(
+                A_d[s0:s1].data_ptr(), n * n, n, H_d[s0:s1].data_ptr(), t_d[s0:s1].data_ptr(),
+                s1 - s0, n, ws.data_ptr(), ws_n, s_comp.cuda_stream,
+            )
+            _lib.check(rc)
+            factored.record(s_comp)
+            s_out.wait_event(factored)
+            with torch.cuda.stream(s_out):
                 H_host[s0:s1].copy_(H_d[s0:s1], non_blocking=True)
                 tau_host[s0:s1].copy_(t_d[s0:s1], non_blocking=True)
-        for st in streams:
+        for st in (s_in, s_comp, s_out):
             main.wait_stream(st)
-        for t in (A_d, H_d, t_d, *wss):
-            t.record_stream(main)
-            for st in streams:
+        for t in (A_d, H_d, t_d, ws):
+            for st in (main, s_in, s_comp, s_out):
                 t.record_stream(st)
 
 
@@ -206,7 +211,7 @@ _HOST_STREAMS: dict[int, list] = {}
 def _host_streams(dev: torch.device) -> list:
     key = dev.index
     if key not in _HOST_STREAMS:
-        _HOST_STREAMS[key] = [torch.cuda.Stream(device=dev) for _ in range(2)]
+        _HOST_STREAMS[key] = [torch.cuda.Stream(device=dev) for _ in range(3)]
     return _HOST_STREAMS[key]
 
 

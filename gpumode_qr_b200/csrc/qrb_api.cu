@@ -4,6 +4,7 @@
 // side of the library as one stream-ordered kernel sequence per call).
 #include <atomic>
 #include <cstring>
+#include <mutex>
 
 #include "qrb_common.cuh"
 
@@ -11,8 +12,9 @@ namespace {
 
 std::atomic<int64_t> g_fail_next{0};
 std::atomic<int64_t> g_sync_check{0};
-std::atomic<int64_t> g_larfb_tc{64};
+std::atomic<int64_t> g_larfb_kind{0};  // 0 = FFMA, 1 = tcgen05 3xTF32
 std::atomic<int64_t> g_launches{0};
+std::atomic<int64_t> g_groups{2};
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -28,8 +30,24 @@ int finish(int rc, cudaStream_t stream) {
   if (g_sync_check.load() != 0) {
     if (cudaStreamSynchronize(stream) != cudaSuccess) return QRB_ERR_LAUNCH;
     if (cudaGetLastError() != cudaSuccess) return QRB_ERR_LAUNCH;
+    int flag = 0;
+    if (qrb::device_error_flag(&flag, false) != QRB_OK) return QRB_ERR_DEVICE;
+    if (flag != 0) return QRB_ERR_DEVICE_WAIT;
   }
   return QRB_OK;
+}
+
+// Trailing update: the tensor-core kernel where it applies and is selected,
+// the FFMA kernel otherwise.
+int larfb_any(const float* V, int64_t sVb, int64_t ldv, const float* T, int64_t sTb, int t_ld,
+              const float* Csrc, int64_t sCsb, int64_t ldcs, float* Cdst, int64_t sCdb,
+              int64_t ldcd, int64_t batch, int r, int k, int c, cudaStream_t s) {
+  if (g_larfb_kind.load() == 1 &&
+      qrb::larfb_tc_supported(V, sVb, ldv, Csrc, sCsb, ldcs, Cdst, sCdb, ldcd, k, c))
+    return qrb::launch_larfb_tc(V, sVb, ldv, T, sTb, t_ld, Csrc, sCsb, ldcs, Cdst, sCdb, ldcd,
+                                batch, r, c, s);
+  return qrb::launch_larfb(V, sVb, ldv, T, sTb, t_ld, Csrc, sCsb, ldcs, Cdst, sCdb, ldcd, batch,
+                           r, k, c, 64, s);
 }
 
 bool bad_matrix_strides(int64_t sb, int64_t srow, int64_t rows, int64_t cols,
@@ -37,6 +55,63 @@ bool bad_matrix_strides(int64_t sb, int64_t srow, int64_t rows, int64_t cols,
   if (srow < cols) return true;                       // rows overlap
   if (batch > 1 && sb < (rows - 1) * srow + cols) return true;  // matrices overlap
   return false;
+}
+
+// The blocked factorization of one contiguous group of matrices on `s`:
+// per 32-column panel one panel kernel (reflectors, tau, T) and one trailing
+// update of the columns to its right. The first step reads A and writes H,
+// so no separate copy pass is needed; later steps work in place on H.
+int blocked_qr(const float* A, int64_t strideA_b, int64_t strideA_row, float* H,
+               float* tau, float* T, int64_t batch, int n, cudaStream_t s) {
+  const int64_t nn = (int64_t)n * n;
+  const int W = qrb::kPanelW;
+  for (int j0 = 0; j0 < n; j0 += W) {
+    const int w = n - j0 < W ? n - j0 : W;
+    const int r = n - j0;
+    const float* src = (j0 == 0) ? A : H;
+    const int64_t sb = (j0 == 0) ? strideA_b : nn;
+    const int64_t ld = (j0 == 0) ? strideA_row : n;
+    float* Hp = H + (int64_t)j0 * n + j0;
+    int rc = qrb::launch_panel(src + (int64_t)j0 * ld + j0, sb, ld, Hp, nn, n, tau + j0, n, T,
+                               (int64_t)W * W, W, nullptr, batch, r, w, s);
+    if (rc != QRB_OK) return rc;
+    const int c = n - j0 - w;
+    if (c > 0) {
+      rc = larfb_any(Hp, nn, n, T, (int64_t)W * W, W, src + (int64_t)j0 * ld + j0 + w, sb, ld,
+                     Hp + w, nn, n, batch, r, w, c, s);
+      if (rc != QRB_OK) return rc;
+    }
+  }
+  return QRB_OK;
+}
+
+// Internal streams for batch groups, created once per device and kept for the
+// life of the process (streams and events, no device memory).
+constexpr int kMaxGroups = 4;
+struct SideStreams {
+  std::mutex mu;
+  cudaStream_t s[kMaxGroups] = {};
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join[kMaxGroups] = {};
+  bool ok = false;
+};
+constexpr int kMaxDevices = 64;
+SideStreams g_side[kMaxDevices];
+std::once_flag g_side_once[kMaxDevices];
+
+SideStreams* side_streams() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  SideStreams* ss = &g_side[dev];
+  std::call_once(g_side_once[dev], [ss] {
+    bool ok = cudaEventCreateWithFlags(&ss->fork, cudaEventDisableTiming) == cudaSuccess;
+    for (int g = 0; g < kMaxGroups && ok; ++g) {
+      ok = cudaStreamCreateWithFlags(&ss->s[g], cudaStreamNonBlocking) == cudaSuccess &&
+           cudaEventCreateWithFlags(&ss->join[g], cudaEventDisableTiming) == cudaSuccess;
+    }
+    ss->ok = ok;
+  });
+  return ss->ok ? ss : nullptr;
 }
 
 }  // namespace
@@ -58,6 +133,7 @@ const char* qrb_status_string(int status) {
     case QRB_ERR_LAUNCH: return "qrb: kernel launch or execution failed";
     case QRB_ERR_DEVICE: return "qrb: no usable CUDA device";
     case QRB_ERR_INJECTED: return "qrb: injected failure (fail_next)";
+    case QRB_ERR_DEVICE_WAIT: return "qrb: a device-side wait timed out (device_error set)";
     default: return "qrb: unknown status";
   }
 }
@@ -112,9 +188,8 @@ int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row,
   if (bad_matrix_strides(strideC_b, strideC_row, r, c, batch)) return QRB_ERR_INVALID_ARG;
   if (take_injected_failure()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int rc = qrb::launch_larfb(V, strideV_b, strideV_row, T, (int64_t)k * k, k, C,
-                                   strideC_b, strideC_row, C, strideC_b, strideC_row, batch,
-                                   r, k, c, (int)g_larfb_tc.load(), s);
+  const int rc = larfb_any(V, strideV_b, strideV_row, T, (int64_t)k * k, k, C, strideC_b,
+                           strideC_row, C, strideC_b, strideC_row, batch, r, k, c, s);
   return finish(rc, s);
 }
 
@@ -138,28 +213,34 @@ int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
   if (take_injected_failure()) return QRB_ERR_INJECTED;
 
   float* T = static_cast<float*>(workspace);
-  const int64_t nn = (int64_t)n * n;
-  const int W = qrb::kPanelW;
-  const int tc = (int)g_larfb_tc.load();
-  for (int j0 = 0; j0 < n; j0 += W) {
-    const int w = n - j0 < W ? n - j0 : W;
-    const int r = n - j0;
-    // The first step reads A and writes H, so no separate copy pass is needed.
-    const float* src = (j0 == 0) ? A : H;
-    const int64_t sb = (j0 == 0) ? strideA_b : nn;
-    const int64_t ld = (j0 == 0) ? strideA_row : n;
-    float* Hp = H + (int64_t)j0 * n + j0;
-    int rc = qrb::launch_panel(src + (int64_t)j0 * ld + j0, sb, ld, Hp, nn, n, tau + j0, n, T,
-                               (int64_t)W * W, W, nullptr, batch, r, w, s);
-    if (rc != QRB_OK) return rc;
-    const int c = n - j0 - w;
-    if (c > 0) {
-      rc = qrb::launch_larfb(Hp, nn, n, T, (int64_t)W * W, W, src + (int64_t)j0 * ld + j0 + w, sb,
-                             ld, Hp + w, nn, n, batch, r, w, c, tc, s);
-      if (rc != QRB_OK) return rc;
+  const int groups = (int)(batch >= 4 ? g_groups.load() : 1);
+  if (groups <= 1) {
+    const int rc = blocked_qr(A, strideA_b, strideA_row, H, tau, T, batch, n, s);
+    return finish(rc, s);
+  }
+  // Split the batch into groups that run the same kernel sequence on separate
+  // internal streams, forked from and joined back into the caller's stream, so
+  // that one group's (latency-bound) panel kernels overlap another group's
+  // trailing updates.
+  int rc = QRB_OK;
+  {
+    SideStreams* ss = side_streams();
+    if (ss == nullptr) return QRB_ERR_DEVICE;
+    std::lock_guard<std::mutex> lock(ss->mu);
+    if (cudaEventRecord(ss->fork, s) != cudaSuccess) return QRB_ERR_LAUNCH;
+    const int64_t nn = (int64_t)n * n;
+    for (int g = 0; g < groups && rc == QRB_OK; ++g) {
+      const int64_t b0 = batch * g / groups, b1 = batch * (g + 1) / groups;
+      if (b1 <= b0) continue;
+      cudaStream_t gs = ss->s[g];
+      if (cudaStreamWaitEvent(gs, ss->fork, 0) != cudaSuccess) return QRB_ERR_LAUNCH;
+      rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
+                      T + b0 * (int64_t)qrb::kPanelW * qrb::kPanelW, b1 - b0, n, gs);
+      if (cudaEventRecord(ss->join[g], gs) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
+      if (cudaStreamWaitEvent(s, ss->join[g], 0) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
     }
   }
-  return finish(QRB_OK, s);
+  return finish(rc, s);
 }
 
 int qrb_set_config(const char* key, int64_t value) {
@@ -174,9 +255,19 @@ int qrb_set_config(const char* key, int64_t value) {
     g_sync_check.store(value);
     return QRB_OK;
   }
-  if (std::strcmp(key, "larfb_tc") == 0) {
-    if (value != 64) return QRB_ERR_INVALID_ARG;
-    g_larfb_tc.store(value);
+  if (std::strcmp(key, "larfb_kind") == 0) {
+    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    g_larfb_kind.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "device_error") == 0) {
+    if (value != 0) return QRB_ERR_INVALID_ARG;
+    int v = 0;
+    return qrb::device_error_flag(&v, true);
+  }
+  if (std::strcmp(key, "groups") == 0) {
+    if (value < 1 || value > kMaxGroups) return QRB_ERR_INVALID_ARG;
+    g_groups.store(value);
     return QRB_OK;
   }
   if (std::strcmp(key, "launches") == 0) {
@@ -191,8 +282,15 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (!key || !value) return QRB_ERR_INVALID_ARG;
   if (std::strcmp(key, "fail_next") == 0) { *value = g_fail_next.load(); return QRB_OK; }
   if (std::strcmp(key, "sync_check") == 0) { *value = g_sync_check.load(); return QRB_OK; }
-  if (std::strcmp(key, "larfb_tc") == 0) { *value = g_larfb_tc.load(); return QRB_OK; }
+  if (std::strcmp(key, "larfb_kind") == 0) { *value = g_larfb_kind.load(); return QRB_OK; }
+  if (std::strcmp(key, "device_error") == 0) {
+    int v = 0;
+    const int rc = qrb::device_error_flag(&v, false);
+    *value = v;
+    return rc;
+  }
   if (std::strcmp(key, "launches") == 0) { *value = g_launches.load(); return QRB_OK; }
+  if (std::strcmp(key, "groups") == 0) { *value = g_groups.load(); return QRB_OK; }
   return QRB_ERR_INVALID_ARG;
 }
 

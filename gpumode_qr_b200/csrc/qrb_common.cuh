@@ -19,6 +19,12 @@ constexpr int kMaxCluster = 8;
 //   sigma = ||x(j+1:)||^2, norm = sqrt(alpha^2 + sigma),
 //   beta = -sign(alpha) * norm (alpha >= 0 -> -norm), tau = (beta-alpha)/beta,
 //   v = x / (alpha - beta); sigma <= 0 -> tau = 0, beta = alpha (identity).
+// Evaluated without divisions by the identities (u = |alpha| + norm > 0)
+//   alpha - beta = sign(alpha) * u,   tau = u / norm = 1 + |alpha| / norm,
+// with 1/norm from the hardware reciprocal square root refined by one Newton
+// step (r <- r (3 - n2 r^2) / 2) and 1/u from the IEEE reciprocal. Both forms
+// are exact in real arithmetic; in FP32 they agree to a few ulp. Outside
+// 1e-30 < alpha^2 + sigma < 1e30 the plain IEEE formulas are used.
 struct Reflector {
   float beta, tau, scale;
 };
@@ -26,11 +32,24 @@ struct Reflector {
 __device__ __forceinline__ Reflector make_reflector(float alpha, float sigma) {
   Reflector h;
   if (sigma > 0.f) {
-    const float norm = sqrtf(fmaf(alpha, alpha, sigma));
-    const float beta = alpha >= 0.f ? -norm : norm;
-    h.beta = beta;
-    h.tau = (beta - alpha) / beta;
-    h.scale = 1.0f / (alpha - beta);
+    const float n2 = fmaf(alpha, alpha, sigma);
+    const float aa = fabsf(alpha);
+    const bool neg = alpha < 0.f;
+    if (n2 > 1e-30f && n2 < 1e30f) {
+      float r = rsqrtf(n2);
+      r = r * fmaf(-0.5f * n2 * r, r, 1.5f);  // one Newton step on 1/sqrt(n2)
+      const float norm = n2 * r;
+      const float ru = __frcp_rn(aa + norm);
+      h.beta = neg ? norm : -norm;
+      h.tau = fmaf(aa, r, 1.0f);
+      h.scale = neg ? -ru : ru;
+    } else {  // tiny or huge: plain IEEE square root and divisions
+      const float norm = sqrtf(n2);
+      const float beta = neg ? norm : -norm;
+      h.beta = beta;
+      h.tau = (beta - alpha) / beta;
+      h.scale = 1.0f / (alpha - beta);
+    }
   } else {
     h.beta = alpha;
     h.tau = 0.f;
@@ -64,6 +83,20 @@ int launch_larfb(const float* V, int64_t sVb, int64_t ldv, const float* T,
                  cudaStream_t stream);
 
 int panel_cluster_size(int r);
+
+// Tensor-core (tcgen05, 3xTF32) trailing update for k = 32 reflectors and
+// 16-byte aligned row-major operands; same contract as launch_larfb.
+bool larfb_tc_supported(const float* V, int64_t sVb, int64_t ldv, const float* Csrc,
+                        int64_t sCsb, int64_t ldcs, const float* Cdst, int64_t sCdb,
+                        int64_t ldcd, int k, int c);
+int launch_larfb_tc(const float* V, int64_t sVb, int64_t ldv, const float* T,
+                    int64_t sTb, int t_ld, const float* Csrc, int64_t sCsb,
+                    int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
+                    int64_t batch, int r, int c, cudaStream_t stream);
+
+// Device-side error flag set by kernels whose bounded waits timed out
+// (synchronous read; optionally reset to 0).
+int device_error_flag(int* value, bool reset);
 
 // Count of kernel launches enqueued by this library (all devices, all calls);
 // read through qrb_get_config("launches").

@@ -1,15 +1,18 @@
 // Block-reflector trailing update C <- C - V (T^T (V^T C)), FP32 FFMA.
 //
-// One CTA owns one matrix's r x TC column tile of C and runs the three
-// products of the reference's trailing update (src/qrbench/variants.py:800-804,
-// W1 = V^T C, W2 = T^T W1, C -= V W2) without writing the k x TC intermediate
-// to global memory:
-//   pass 1  W = V^T C over all r rows, 32-row chunks double-buffered into
-//           shared memory with cp.async; four row-interleaved thread groups
-//           each hold an 8 x 4 register block of W and are summed at the end;
-//   mid     W <- T^T W (T upper triangular, from shared memory);
-//   pass 2  C -= V W over 128-row chunks: V is staged transposed in shared
-//           memory, each thread updates an 8 x 4 block of C in registers.
+// One CTA (256 threads) owns one matrix's r x 64 column tile of C and runs the
+// three products of the reference's trailing update (src/qrbench/variants.py
+// :800-804, W1 = V^T C, W2 = T^T W1, C -= V W2) without writing the k x 64
+// intermediate to global memory:
+//   pass 1  W = V^T C over all r rows: 64-row chunks of V and C double-buffered
+//           into shared memory with cp.async; each warp takes every 8th row
+//           and each lane accumulates an 8 x 8 register block of W (64 FMAs
+//           per four 16-byte shared loads); the eight warp partials are summed
+//           while W <- T^T W is formed;
+//   pass 2  C -= V W over 256-row chunks: V is staged transposed in shared
+//           memory and each thread updates an 8-row x 8-column block of C in
+//           registers (columns c, c+1, c+2, c+3 and c+32..c+35, so that a
+//           warp's global loads and stores cover whole 128-byte rows).
 // V is read through its strictly lower part only: the diagonal is taken as 1
 // and everything above it as 0 (so V can point into a packed H), columns at or
 // beyond k as 0.
@@ -21,21 +24,27 @@ namespace {
 
 constexpr int K = 32;        // reflectors per block (padded)
 constexpr int TC = 64;       // columns of C per CTA
-constexpr int NT = 256;      // threads per CTA
-constexpr int RC1 = 32;      // rows per pass-1 chunk
-constexpr int RC2 = 128;     // rows per pass-2 chunk
+constexpr int NT = 256;      // threads per CTA (8 warps)
+constexpr int NW = NT / 32;
+constexpr int RC1 = 64;      // rows per pass-1 chunk
+constexpr int RC2 = 256;     // rows per pass-2 chunk
 constexpr int VS_LD = K + 4;     // pass-1 V chunk row stride (floats)
 constexpr int CS_LD = TC + 4;    // pass-1 C chunk row stride
 constexpr int VT_LD = RC2 + 4;   // pass-2 transposed V row stride
 constexpr int WS_LD = TC + 4;    // W row stride
 constexpr int T_LD = K + 1;
 
-struct __align__(16) Smem {
+struct __align__(16) Stage {
   float Vs[2][RC1 * VS_LD];
   float Cs[2][RC1 * CS_LD];
-  float Wp[4][K * TC];
+};
+struct __align__(16) Smem {
+  union {
+    Stage st;                 // pass 1 staging
+    float Wp[NW][K * TC];     // per-warp partial W (after pass 1)
+    float Vt[K * VT_LD];      // pass 2 transposed V chunk
+  } u;
   float Ws[K * WS_LD];
-  float Vt[K * VT_LD];
   float Ts[K * T_LD];
 };
 
@@ -66,7 +75,7 @@ __device__ __forceinline__ float vmask(float x, int i, int a, int k) {
 }
 
 template <bool VEC>
-__global__ void __launch_bounds__(NT)
+__global__ void __launch_bounds__(NT, 2)
 k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
         const float* __restrict__ T, int64_t sTb, int t_ld,
         const float* __restrict__ Csrc, int64_t sCsb, int64_t ldcs,
@@ -75,6 +84,8 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int64_t m = blockIdx.y;
   const int c0 = blockIdx.x * TC;
   const float* __restrict__ Vm = V + m * sVb;
@@ -87,54 +98,54 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   }
 
   // ---------------- pass 1: W = V^T C ----------------
-  const int kg = tid >> 6;            // row-interleave group 0..3
-  const int t64 = tid & 63;
-  const int wa = (t64 >> 4) << 3;     // W rows wa..wa+7
-  const int wc = (t64 & 15) << 2;     // W cols wc..wc+3
-  float acc[8][4];
+  const int wa = (lane >> 3) << 3;  // W rows wa..wa+7
+  const int wc = (lane & 7) << 2;   // W cols wc..wc+3 and wc+32..wc+35
+  float acc[8][8];
 #pragma unroll
   for (int x = 0; x < 8; ++x)
 #pragma unroll
-    for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+    for (int y = 0; y < 8; ++y) acc[x][y] = 0.f;
 
   const int nch = (r + RC1 - 1) / RC1;
   auto load_chunk = [&](int ch, int buf) {
     const int i0 = ch * RC1;
     if (VEC) {
-      {  // V: 32 rows x 32 cols = 256 float4
-        const int row = tid >> 3, c4 = (tid & 7) << 2;
+#pragma unroll
+      for (int e = 0; e < (RC1 * K) / (4 * NT); ++e) {  // V: 64 x 32 = 512 float4
+        const int idx = tid + e * NT;
+        const int row = idx >> 3, c4 = (idx & 7) << 2;
         const int i = i0 + row;
         const bool ok = i < r;
         const float* g = ok ? Vm + (int64_t)i * ldv + c4 : Vm;
-        cp_async16(&sm.Vs[buf][row * VS_LD + c4], g, ok);
+        cp_async16(&sm.u.st.Vs[buf][row * VS_LD + c4], g, ok);
       }
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {  // C: 32 rows x 64 cols = 512 float4
+      for (int e = 0; e < (RC1 * TC) / (4 * NT); ++e) {  // C: 64 x 64 = 1024 float4
         const int idx = tid + e * NT;
         const int row = idx >> 4, c4 = (idx & 15) << 2;
         const int i = i0 + row, col = c0 + c4;
         const bool ok = i < r && col < c;
         const float* g = ok ? Cm + (int64_t)i * ldcs + col : Cm;
-        cp_async16(&sm.Cs[buf][row * CS_LD + c4], g, ok);
+        cp_async16(&sm.u.st.Cs[buf][row * CS_LD + c4], g, ok);
       }
     } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
+#pragma unroll 4
+      for (int e = 0; e < (RC1 * K) / NT; ++e) {
         const int idx = tid + e * NT;
         const int row = idx >> 5, col = idx & 31;
         const int i = i0 + row;
         const bool ok = i < r && col < k;
         const float* g = ok ? Vm + (int64_t)i * ldv + col : Vm;
-        cp_async4(&sm.Vs[buf][row * VS_LD + col], g, ok);
+        cp_async4(&sm.u.st.Vs[buf][row * VS_LD + col], g, ok);
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
+#pragma unroll 4
+      for (int e = 0; e < (RC1 * TC) / NT; ++e) {
         const int idx = tid + e * NT;
         const int row = idx >> 6, cc = idx & 63;
         const int i = i0 + row, col = c0 + cc;
         const bool ok = i < r && col < c;
         const float* g = ok ? Cm + (int64_t)i * ldcs + col : Cm;
-        cp_async4(&sm.Cs[buf][row * CS_LD + cc], g, ok);
+        cp_async4(&sm.u.st.Cs[buf][row * CS_LD + cc], g, ok);
       }
     }
     cp_async_commit();
@@ -156,46 +167,52 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
         const int row = e / K, a = e % K;
         const int i = i0 + row;
         if (a >= k || i <= a) {
-          float& s = sm.Vs[buf][row * VS_LD + a];
+          float& s = sm.u.st.Vs[buf][row * VS_LD + a];
           s = vmask(s, i, a, k);
         }
       }
       __syncthreads();
     }
-    const float* vb = sm.Vs[buf];
-    const float* cb = sm.Cs[buf];
-#pragma unroll
-    for (int rr = kg; rr < RC1; rr += 4) {
+    const float* vb = sm.u.st.Vs[buf];
+    const float* cb = sm.u.st.Cs[buf];
+#pragma unroll 2
+    for (int rr = warp; rr < RC1; rr += NW) {
       const float4 v0 = *reinterpret_cast<const float4*>(vb + rr * VS_LD + wa);
       const float4 v1 = *reinterpret_cast<const float4*>(vb + rr * VS_LD + wa + 4);
-      const float4 cc = *reinterpret_cast<const float4*>(cb + rr * CS_LD + wc);
+      const float4 ca = *reinterpret_cast<const float4*>(cb + rr * CS_LD + wc);
+      const float4 cbv = *reinterpret_cast<const float4*>(cb + rr * CS_LD + wc + 32);
       const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      const float cv[4] = {cc.x, cc.y, cc.z, cc.w};
+      const float cv[8] = {ca.x, ca.y, ca.z, ca.w, cbv.x, cbv.y, cbv.z, cbv.w};
 #pragma unroll
       for (int x = 0; x < 8; ++x)
 #pragma unroll
-        for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(vv[x], cv[y], acc[x][y]);
+        for (int y = 0; y < 8; ++y) acc[x][y] = fmaf(vv[x], cv[y], acc[x][y]);
     }
     __syncthreads();
   }
 
+  // per-warp partials of W (the staging area is free now)
 #pragma unroll
-  for (int x = 0; x < 8; ++x)
-    *reinterpret_cast<float4*>(&sm.Wp[kg][(wa + x) * TC + wc]) =
-        make_float4(acc[x][0], acc[x][1], acc[x][2], acc[x][3]);
+  for (int x = 0; x < 8; ++x) {
+    float* row = &sm.u.Wp[warp][(wa + x) * TC];
+    *reinterpret_cast<float4*>(row + wc) = make_float4(acc[x][0], acc[x][1], acc[x][2], acc[x][3]);
+    *reinterpret_cast<float4*>(row + wc + 32) =
+        make_float4(acc[x][4], acc[x][5], acc[x][6], acc[x][7]);
+  }
   __syncthreads();
 
-  // ---------------- W <- T^T W ----------------
+  // ---------------- W <- T^T (sum of partials) ----------------
   {
     const int cc = tid & 63;
     const int ab = (tid >> 6) << 3;
     float o[8];
 #pragma unroll
     for (int x = 0; x < 8; ++x) o[x] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
     for (int q = 0; q < K; ++q) {
-      const float wq = sm.Wp[0][q * TC + cc] + sm.Wp[1][q * TC + cc] +
-                       sm.Wp[2][q * TC + cc] + sm.Wp[3][q * TC + cc];
+      float wq = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < NW; ++w2) wq += sm.u.Wp[w2][q * TC + cc];
 #pragma unroll
       for (int x = 0; x < 8; ++x) o[x] = fmaf(sm.Ts[q * T_LD + ab + x], wq, o[x]);
     }
@@ -204,13 +221,13 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   }
 
   // ---------------- pass 2: C -= V W ----------------
-  const int rg = (tid >> 4) << 3;    // chunk rows rg..rg+7
-  const int cg4 = (tid & 15) << 2;   // tile cols cg4..cg4+3
-  const int col = c0 + cg4;
+  const int rg = (tid >> 3) << 3;   // chunk rows rg..rg+7
+  const int cq = (tid & 7) << 2;    // tile cols cq..cq+3 and cq+32..cq+35
+  const int colA = c0 + cq, colB = c0 + cq + 32;
   for (int i0 = 0; i0 < r; i0 += RC2) {
-    __syncthreads();  // Ws ready (first iteration) / Vt free (later ones)
-    // Stage V rows i0..i0+127 transposed: Vt[a][row].
-#pragma unroll
+    __syncthreads();  // Ws ready and partials consumed (first) / Vt free (later)
+    // Stage V rows i0..i0+255 transposed: Vt[a][row].
+#pragma unroll 2
     for (int e = 0; e < (RC2 * K) / (4 * NT); ++e) {
       const int idx = tid + e * NT;
       const int row = idx & (RC2 - 1), c4 = (idx / RC2) << 2;
@@ -227,52 +244,60 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
           t.w = c4 + 3 < k ? __ldg(g + 3) : 0.f;
         }
       }
-      sm.Vt[(c4 + 0) * VT_LD + row] = vmask(t.x, i, c4 + 0, k);
-      sm.Vt[(c4 + 1) * VT_LD + row] = vmask(t.y, i, c4 + 1, k);
-      sm.Vt[(c4 + 2) * VT_LD + row] = vmask(t.z, i, c4 + 2, k);
-      sm.Vt[(c4 + 3) * VT_LD + row] = vmask(t.w, i, c4 + 3, k);
+      sm.u.Vt[(c4 + 0) * VT_LD + row] = vmask(t.x, i, c4 + 0, k);
+      sm.u.Vt[(c4 + 1) * VT_LD + row] = vmask(t.y, i, c4 + 1, k);
+      sm.u.Vt[(c4 + 2) * VT_LD + row] = vmask(t.z, i, c4 + 2, k);
+      sm.u.Vt[(c4 + 3) * VT_LD + row] = vmask(t.w, i, c4 + 3, k);
     }
-    float cv[8][4];
+    float cv[8][8];
 #pragma unroll
     for (int x = 0; x < 8; ++x) {
       const int i = i0 + rg + x;
-      const float* g = Cm + (int64_t)i * ldcs + col;
+      const float* g = Cm + (int64_t)i * ldcs;
       if (VEC) {
-        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < r && col < c) t = *reinterpret_cast<const float4*>(g);
-        cv[x][0] = t.x;
-        cv[x][1] = t.y;
-        cv[x][2] = t.z;
-        cv[x][3] = t.w;
+        float4 ta = make_float4(0.f, 0.f, 0.f, 0.f), tb = ta;
+        if (i < r && colA < c) ta = *reinterpret_cast<const float4*>(g + colA);
+        if (i < r && colB < c) tb = *reinterpret_cast<const float4*>(g + colB);
+        cv[x][0] = ta.x; cv[x][1] = ta.y; cv[x][2] = ta.z; cv[x][3] = ta.w;
+        cv[x][4] = tb.x; cv[x][5] = tb.y; cv[x][6] = tb.z; cv[x][7] = tb.w;
       } else {
 #pragma unroll
-        for (int y = 0; y < 4; ++y) cv[x][y] = (i < r && col + y < c) ? g[y] : 0.f;
+        for (int y = 0; y < 4; ++y) {
+          cv[x][y] = (i < r && colA + y < c) ? g[colA + y] : 0.f;
+          cv[x][4 + y] = (i < r && colB + y < c) ? g[colB + y] : 0.f;
+        }
       }
     }
     __syncthreads();
-#pragma unroll 8
+#pragma unroll 4
     for (int a = 0; a < K; ++a) {
-      const float4 w4 = *reinterpret_cast<const float4*>(&sm.Ws[a * WS_LD + cg4]);
-      const float4 v0 = *reinterpret_cast<const float4*>(&sm.Vt[a * VT_LD + rg]);
-      const float4 v1 = *reinterpret_cast<const float4*>(&sm.Vt[a * VT_LD + rg + 4]);
+      const float4 wA = *reinterpret_cast<const float4*>(&sm.Ws[a * WS_LD + cq]);
+      const float4 wB = *reinterpret_cast<const float4*>(&sm.Ws[a * WS_LD + cq + 32]);
+      const float4 v0 = *reinterpret_cast<const float4*>(&sm.u.Vt[a * VT_LD + rg]);
+      const float4 v1 = *reinterpret_cast<const float4*>(&sm.u.Vt[a * VT_LD + rg + 4]);
       const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      const float ww[4] = {w4.x, w4.y, w4.z, w4.w};
+      const float ww[8] = {wA.x, wA.y, wA.z, wA.w, wB.x, wB.y, wB.z, wB.w};
 #pragma unroll
       for (int x = 0; x < 8; ++x)
 #pragma unroll
-        for (int y = 0; y < 4; ++y) cv[x][y] = fmaf(-vv[x], ww[y], cv[x][y]);
+        for (int y = 0; y < 8; ++y) cv[x][y] = fmaf(-vv[x], ww[y], cv[x][y]);
     }
 #pragma unroll
     for (int x = 0; x < 8; ++x) {
       const int i = i0 + rg + x;
       if (i >= r) continue;
-      float* g = Dm + (int64_t)i * ldcd + col;
+      float* g = Dm + (int64_t)i * ldcd;
       if (VEC) {
-        if (col < c) *reinterpret_cast<float4*>(g) = make_float4(cv[x][0], cv[x][1], cv[x][2], cv[x][3]);
+        if (colA < c)
+          *reinterpret_cast<float4*>(g + colA) = make_float4(cv[x][0], cv[x][1], cv[x][2], cv[x][3]);
+        if (colB < c)
+          *reinterpret_cast<float4*>(g + colB) = make_float4(cv[x][4], cv[x][5], cv[x][6], cv[x][7]);
       } else {
 #pragma unroll
-        for (int y = 0; y < 4; ++y)
-          if (col + y < c) g[y] = cv[x][y];
+        for (int y = 0; y < 4; ++y) {
+          if (colA + y < c) g[colA + y] = cv[x][y];
+          if (colB + y < c) g[colB + y] = cv[x][4 + y];
+        }
       }
     }
   }

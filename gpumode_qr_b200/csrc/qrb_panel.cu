@@ -6,14 +6,23 @@
 // panel lives in shared memory; shared memory carries only reductions.
 //
 // One column step j is one 32-slot reduction over the rows below j:
-//     slot[m] = sum_{i>j} x_i * a_im,   x = column j (unscaled)
+//     slot[m] = sum_{i>j} x_i * a_im,   x = column j
 // which yields, at once, sigma = slot[j] (the norm below the diagonal), the
 // trailing dot products d_k = a_jk + scale * slot[k] (k > j), and the Gram
-// column G[m][j] = v_m(j) + scale * slot[m] (m < j) used by the T recurrence.
-// The reduction is a warp reduce-scatter (31 shuffles), a cross-warp sum in
-// shared memory, and for clusters a cross-CTA sum over distributed shared
-// memory with one cluster barrier per step (exchange buffers alternate by
-// step parity so no second barrier is needed).
+// column G[m][j] (m < j) used by the T recurrence. The reduction is a warp
+// reduce-scatter (31 shuffles), a cross-warp sum in shared memory, and for
+// clusters a cross-CTA sum over distributed shared memory. Every warp forms
+// the reflector coefficients itself from the summed slots, so a step costs one
+// block barrier (plus one cluster barrier for clusters); the partial-sum
+// buffers alternate by step parity so no second barrier is needed.
+//
+// The column loop is a runtime loop with a compact body (the register array is
+// indexed only by compile-time constants; the current column is picked with a
+// select tree), which keeps the kernel inside the instruction cache. Reflector
+// scaling is deferred: below the diagonal a finished column keeps its unscaled
+// values x_m during the loop and is multiplied by scale_m = 1/(alpha_m-beta_m)
+// only when the panel is written back; the Gram entries are scaled to match:
+//     G[m][j] = scale_m * (x_m(j) + scale_j * sum_{i>j} x_j(i) x_m(i)).
 //
 // Semantics follow the reference panel kernel (src/qrbench/triton_kernels.py
 // :839-871 reflectors and packing, :873-884 unit-lower V, :886-909 forward
@@ -29,7 +38,8 @@ namespace qrb {
 namespace {
 
 constexpr int W = kPanelW;
-constexpr int kMaxThreads = 512;
+constexpr int kMaxThreads = 512;        // upper bound the shared buffers are sized for
+constexpr int kPanelCtaThreads = 256;   // threads per CTA used by panel_shape
 
 // Reduce 32 per-lane slot values across a warp; afterwards lane l holds the
 // warp total of slot l in v[0]. 16+8+4+2+1 shuffles.
@@ -46,19 +56,32 @@ __device__ __forceinline__ void reduce_scatter32(float (&v)[W], int lane) {
   }
 }
 
+// v[j] for a runtime j in [0, 32): a five-level select tree (31 selects).
+__device__ __forceinline__ float pick32(const float (&v)[W], int j) {
+  float t16[16], t8[8], t4[4], t2[2];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) t16[q] = (j & 16) ? v[q + 16] : v[q];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) t8[q] = (j & 8) ? t16[q + 8] : t16[q];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) t4[q] = (j & 4) ? t8[q + 4] : t8[q];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) t2[q] = (j & 2) ? t4[q + 2] : t4[q];
+  return (j & 1) ? t2[1] : t2[0];
+}
+
 template <int RPT>
-__global__ void __launch_bounds__(kMaxThreads, 1)
+__global__ void __launch_bounds__(RPT >= 4 ? kPanelCtaThreads : kMaxThreads, 1)
 k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
         float* __restrict__ dst, int64_t sb_dst, int64_t ld_dst,
         float* __restrict__ tau_out, int64_t tau_sb, float* __restrict__ T_out,
         int64_t T_sb, int t_ld, float* __restrict__ V_out, int r, int w,
         int cs, int vec_src, int vec_dst) {
-  __shared__ float red[kMaxThreads / 32][W];
-  __shared__ float xch[2][2][W];  // [parity][0 = slot sums, 1 = row j]
-  __shared__ float fco[W];        // tau_j * d_k for trailing columns k > j
-  __shared__ float coef[4];       // beta, tau, scale
-  __shared__ float Gs[W][W + 1];  // Gram V^T V, strictly upper part
-  __shared__ float taus[W];
+  __shared__ float red[2][kMaxThreads / 32][W];  // [parity][warp][slot]
+  __shared__ float xch[2][2][W];                 // [parity][0 = CTA slot sums, 1 = row j]
+  __shared__ __align__(16) float fbuf[kMaxThreads / 32][W];  // per-warp tau_j * d_k
+  __shared__ float Gs[W][W + 1];                 // Gram V^T V, strictly upper part
+  __shared__ float taus[W], scales[W], betas[W];
 
   const int nt = blockDim.x;
   const int tid = threadIdx.x;
@@ -71,13 +94,19 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
   const int row0 = rank * nt * RPT;
 
   for (int e = tid; e < W * (W + 1); e += nt) (&Gs[0][0])[e] = 0.f;
-  if (tid < W) taus[tid] = 0.f;
+  if (tid < W) {
+    taus[tid] = 0.f;
+    scales[tid] = 0.f;
+    betas[tid] = 0.f;
+  }
 
   float a[RPT][W];
+  int rowi[RPT];
   const float* __restrict__ S = src + m * sb_src;
 #pragma unroll
   for (int p = 0; p < RPT; ++p) {
     const int i = row0 + tid + p * nt;
+    rowi[p] = i;
     const float* rowp = S + (int64_t)i * ld_src;
     if (i < r && vec_src) {
 #pragma unroll
@@ -95,104 +124,111 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
   }
   __syncthreads();
 
-#pragma unroll
-  for (int j = 0; j < W; ++j) {
-    if (j >= w) break;  // uniform across the cluster
+#pragma unroll 1
+  for (int j = 0; j < w; ++j) {  // uniform across the cluster
     const int par = j & 1;
 
     // Phase A: slot partials over this thread's rows below j.
+    float x[RPT];
     float sl[W];
 #pragma unroll
     for (int q = 0; q < W; ++q) sl[q] = 0.f;
 #pragma unroll
     for (int p = 0; p < RPT; ++p) {
-      const int i = row0 + tid + p * nt;
-      const float x = (i > j) ? a[p][j] : 0.f;
+      const float xj = pick32(a[p], j);
+      x[p] = xj;
+      const float xm = rowi[p] > j ? xj : 0.f;
 #pragma unroll
-      for (int q = 0; q < W; ++q) sl[q] = fmaf(x, a[p][q], sl[q]);
-      if (i == j) {
+      for (int q = 0; q < W; ++q) sl[q] = fmaf(xm, a[p][q], sl[q]);
+      if (rowi[p] == j) {
 #pragma unroll
         for (int q = 0; q < W; ++q) xch[par][1][q] = a[p][q];
       }
     }
     reduce_scatter32(sl, lane);
-    red[warp][lane] = sl[0];
+    red[par][warp][lane] = sl[0];
     __syncthreads();
 
-    float tot = 0.f, rowv = 0.f;
-    if (warp == 0) {
-      for (int w2 = 0; w2 < nwarps; ++w2) tot += red[w2][lane];
-      xch[par][0][lane] = tot;
-    }
+    float tot = 0.f, rowv;
     if (cs > 1) {
-      cg::this_cluster().sync();
       if (warp == 0) {
-        tot = 0.f;
-        for (int q = 0; q < cs; ++q)
-          tot += cg::this_cluster().map_shared_rank(&xch[par][0][0], q)[lane];
-        rowv = cg::this_cluster().map_shared_rank(&xch[par][1][0], 0)[lane];
+        for (int w2 = 0; w2 < nwarps; ++w2) tot += red[par][w2][lane];
+        xch[par][0][lane] = tot;
       }
-    } else if (warp == 0) {
+      cg::cluster_group cl = cg::this_cluster();
+      cl.sync();
+      tot = 0.f;
+      for (int q = 0; q < cs; ++q) tot += cl.map_shared_rank(&xch[par][0][0], q)[lane];
+      rowv = cl.map_shared_rank(&xch[par][1][0], 0)[lane];
+    } else {
+      for (int w2 = 0; w2 < nwarps; ++w2) tot += red[par][w2][lane];
       rowv = xch[par][1][lane];
     }
 
+    // Every warp forms the reflector from the summed slots (lane = column).
+    const float sigma = __shfl_sync(kFull, tot, j);
+    const float alpha = __shfl_sync(kFull, rowv, j);
+    const Reflector h = make_reflector(alpha, sigma);
+    const float d = fmaf(h.scale, tot, rowv);
+    fbuf[warp][lane] = lane > j ? h.tau * d : 0.f;
     if (warp == 0) {
-      const float sigma = __shfl_sync(kFull, tot, j);
-      const float alpha = __shfl_sync(kFull, rowv, j);
-      const Reflector h = make_reflector(alpha, sigma);
-      const float d = fmaf(h.scale, tot, rowv);
-      if (lane > j) fco[lane] = h.tau * d;
-      if (lane < j) Gs[lane][j] = d;
+      if (lane < j) Gs[lane][j] = scales[lane] * d;
       if (lane == 0) {
-        coef[0] = h.beta;
-        coef[1] = h.tau;
-        coef[2] = h.scale;
         taus[j] = h.tau;
+        scales[j] = h.scale;
+        betas[j] = h.beta;
       }
     }
-    __syncthreads();
+    __syncwarp();
 
-    // Phase B: apply H_j to this thread's rows of the trailing columns.
-    const float beta = coef[0];
-    const float scale = coef[2];
+    // Phase B: apply H_j to this thread's rows of the trailing columns
+    // (f_k = 0 for k <= j leaves the finished columns untouched).
+    float vrow[RPT];
 #pragma unroll
-    for (int p = 0; p < RPT; ++p) {
-      const int i = row0 + tid + p * nt;
-      if (i > j) {
-        const float v = a[p][j] * scale;
+    for (int p = 0; p < RPT; ++p)
+      vrow[p] = rowi[p] > j ? h.scale * x[p] : (rowi[p] == j ? 1.f : 0.f);
 #pragma unroll
-        for (int k = j + 1; k < W; ++k) a[p][k] = fmaf(-fco[k], v, a[p][k]);
-        a[p][j] = v;
-      } else if (i == j) {
+    for (int k4 = 0; k4 < W / 4; ++k4) {
+      const float4 f4 = reinterpret_cast<const float4*>(fbuf[warp])[k4];
 #pragma unroll
-        for (int k = j + 1; k < W; ++k) a[p][k] -= fco[k];
-        a[p][j] = beta;
+      for (int p = 0; p < RPT; ++p) {
+        a[p][4 * k4 + 0] = fmaf(-f4.x, vrow[p], a[p][4 * k4 + 0]);
+        a[p][4 * k4 + 1] = fmaf(-f4.y, vrow[p], a[p][4 * k4 + 1]);
+        a[p][4 * k4 + 2] = fmaf(-f4.z, vrow[p], a[p][4 * k4 + 2]);
+        a[p][4 * k4 + 3] = fmaf(-f4.w, vrow[p], a[p][4 * k4 + 3]);
       }
     }
+    __syncwarp();  // fbuf is rewritten next step
   }
+  __syncthreads();  // scales / betas / Gs from warp 0 visible to all
 
-  // Write the factored panel rows back (R on/above the diagonal, v below).
+  // Write the factored panel rows back: R above the diagonal, beta on it,
+  // v = scale * x below it.
   float* __restrict__ D = dst + m * sb_dst;
 #pragma unroll
   for (int p = 0; p < RPT; ++p) {
-    const int i = row0 + tid + p * nt;
+    const int i = rowi[p];
     if (i >= r) continue;
+#pragma unroll
+    for (int c = 0; c < W; ++c)
+      a[p][c] = i > c ? scales[c] * a[p][c] : (i == c ? betas[c] : a[p][c]);
+    const float (&o)[W] = a[p];
     float* rowp = D + (int64_t)i * ld_dst;
     if (vec_dst) {
 #pragma unroll
       for (int c4 = 0; c4 < W / 4; ++c4)
         reinterpret_cast<float4*>(rowp)[c4] =
-            make_float4(a[p][4 * c4], a[p][4 * c4 + 1], a[p][4 * c4 + 2], a[p][4 * c4 + 3]);
+            make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
     } else {
 #pragma unroll
       for (int c = 0; c < W; ++c)
-        if (c < w) rowp[c] = a[p][c];
+        if (c < w) rowp[c] = o[c];
     }
     if (V_out != nullptr) {
       float* vrow = V_out + m * (int64_t)r * w + (int64_t)i * w;
 #pragma unroll
       for (int c = 0; c < W; ++c)
-        if (c < w) vrow[c] = (i > c) ? a[p][c] : (i == c ? 1.f : 0.f);
+        if (c < w) vrow[c] = (i > c) ? o[c] : (i == c ? 1.f : 0.f);
     }
   }
 
@@ -255,12 +291,12 @@ int launch_panel_rpt(const float* src, int64_t sb_src, int64_t ld_src,
 
 }  // namespace
 
-// Rows per thread 2 above 256 rows, else 1; CTAs of up to 512 threads; a
-// cluster of cs CTAs (a power of two, <= 8 for the launch to be accepted)
-// covers the panel's rows.
+// Rows per thread: 1 up to 128 rows (one CTA of up to 128 threads), else 4:
+// one CTA of up to 256 threads up to 1024 rows, beyond that a cluster of cs
+// CTAs of 256 threads (cs a power of two, <= 8 for the launch to be accepted).
 static void panel_shape(int r, int* rpt, int* cs, int* nt) {
-  const int R = r > 256 ? 2 : 1;
-  const int per_cta_max = kMaxThreads * R;
+  const int R = r > 128 ? 4 : 1;
+  const int per_cta_max = kPanelCtaThreads * R;
   const int need = (r + per_cta_max - 1) / per_cta_max;
   int c = 1;
   while (c < need) c <<= 1;  // cluster sizes 1, 2, 4, 8
@@ -291,7 +327,7 @@ int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
     return launch_panel_rpt<1>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
                                tau_sb, T_out, T_sb, t_ld, V_out, batch, r, w, cs,
                                nt, stream);
-  return launch_panel_rpt<2>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
+  return launch_panel_rpt<4>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
                              tau_sb, T_out, T_sb, t_ld, V_out, batch, r, w, cs,
                              nt, stream);
 }

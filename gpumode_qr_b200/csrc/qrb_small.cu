@@ -1,12 +1,31 @@
-// Fused whole-matrix Householder QR for n <= 32: one warp per matrix.
+// Fused whole-matrix Householder QR for n <= 32: one half-warp per matrix,
+// two matrices per warp.
 //
-// Mapping: lane k owns column k of its matrix in 32 registers (rows 0..31,
-// zero padded beyond n). At step j lane j turns its column into the reflector
-// (slarfg, coefficients computed redundantly by every lane from two shuffles),
-// publishes v through a per-warp shared-memory line, and every lane k > j
-// applies H_j to its own column: d = v . a_k, a_k -= tau * d * v. The sum of
-// squares that step j+1 needs (rows below j+1 of column j+1) is accumulated
-// while the update is applied, so each step carries no separate reduction.
+// Mapping: in each half-warp (16 lanes) lane l owns columns l and l + 16 of its
+// matrix, each in 32 registers held as 16 row pairs (rows and columns beyond n
+// are zero). The two halves of a warp factor two matrices with the same
+// instructions, so the per-column work that does not scale with the matrix
+// (the two shuffles, the reflector coefficients, publishing the column) is
+// paid once for two matrices. The updates run on the packed FP32x2 FMA of
+// sm_100 (two IEEE FMAs per instruction).
+//
+// The column loop is unrolled (j, the owner lane j mod 16 and the owner's
+// column slot j / 16 are compile-time constants, so every row index is a
+// register name and only rows below j are touched).
+//
+// Memory: every lane loads and stores its own columns element by element
+// (a half-warp touches 64 contiguous bytes of a row per access).
+//
+// Step j: the owner lane publishes its unscaled column x through a per-half
+// shared-memory line, every lane reads it back as row pairs (once for the dot
+// product, once for the update, to keep register pressure down), and each column
+// k > j gets H_j = I - tau v v^T with v = scale * x below the diagonal:
+//     d = a_j + scale * sum_{i>j} x_i a_i,  a_j -= tau d,  a_i -= (tau d scale) x_i.
+// Column slot 0 (columns 0..15) is skipped once j >= 15, when all its columns
+// are finished. The sum of squares that step j+1 needs is accumulated during
+// the update, only for the slot that holds column j+1. A finished column keeps
+// its unscaled x below the diagonal; it is scaled once at the end (deferred
+// scaling) and beta is stored on the diagonal.
 //
 // Semantics follow the reference's fused kernel step for step
 // (src/qrbench/triton_kernels.py:676-715): slarfg coefficients (:691-700),
@@ -19,91 +38,229 @@ namespace qrb {
 namespace {
 
 constexpr int NP = kFusedMaxN;  // padded matrix size (32 rows/columns)
+constexpr int NQ = NP / 2;      // row pairs
+constexpr int kWarpsPerBlock = 4;
+constexpr int TLD = 36;                    // tile row stride (floats)
+constexpr int TMAT = NP * TLD + 16;        // tile floats per matrix (+16: bank shift)
 
-template <int WPB>
-__global__ void __launch_bounds__(WPB * 32)
-k_fused_warp(const float* __restrict__ A, int64_t sAb, int64_t sAr,
-             float* __restrict__ H, float* __restrict__ tau, int64_t batch,
-             int n) {
-  __shared__ __align__(16) float vbuf[WPB][2][NP];
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int64_t m = (int64_t)blockIdx.x * WPB + warp;
-  if (m >= batch) return;  // warp-uniform
+__device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
-  const float* __restrict__ Am = A + m * sAb;
-  const bool col_ok = lane < n;
-  float a[NP];
-#pragma unroll
-  for (int i = 0; i < NP; ++i)
-    a[i] = (col_ok && i < n) ? __ldg(Am + (int64_t)i * sAr + lane) : 0.f;
+__device__ __forceinline__ float get_row(const float2 (&a)[NQ], int i) {
+  return (i & 1) ? a[i >> 1].y : a[i >> 1].x;
+}
 
-  // Sum of squares below the diagonal for the step that consumes this column.
-  float s = 0.f;
-#pragma unroll
-  for (int i = 1; i < NP; ++i) s = fmaf(a[i], a[i], s);
+// Apply step J's reflector to one column (registers a) given the published
+// column x (in shared memory at xb, rows > J valid) and the coefficients; with
+// WANT_S, return in *s the sum of squares of rows > J+1 of the updated
+// column. x is read twice (dot product, then update) instead of being held in
+// registers across both loops.
+template <int J>
+__device__ __forceinline__ float2 xpair(const float* xb, int q) {
+  return reinterpret_cast<const float2*>(xb)[q];
+}
 
-  float my_tau = 0.f;
+template <int J, bool WANT_S>
+__device__ __forceinline__ void apply_step(float2 (&a)[NQ], const float* xb, bool active,
+                                           float tau, float scale, float* s) {
+  constexpr int qf = (J + 2) / 2;  // first full row pair strictly below row J
+  float dsum = 0.f;
+  if ((J & 1) == 0) dsum = xb[J + 1] * a[J >> 1].y;
+  float2 dA = make_float2(0.f, 0.f), dB = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int j = 0; j < NP - 1; ++j) {
-    if (j >= n - 1) break;  // uniform: the last column gets tau = 0
-    float* vb = vbuf[warp][j & 1];
-    const float alpha = __shfl_sync(kFull, a[j], j);
-    const float sigma = __shfl_sync(kFull, s, j);
-    const Reflector h = make_reflector(alpha, sigma);
-    if (lane == j) {
+  for (int q = qf; q < NQ; ++q) {
+    if (((q - qf) & 1) == 0)
+      dA = __ffma2_rn(xpair<J>(xb, q), a[q], dA);
+    else
+      dB = __ffma2_rn(xpair<J>(xb, q), a[q], dB);
+  }
+  dsum += (dA.x + dA.y) + (dB.x + dB.y);
+  const float aj = get_row(a, J);
+  const float d = fmaf(scale, dsum, aj);
+  const float f = active ? tau * d : 0.f;
+  const float g = f * scale;
+  const float2 ng = f2(-g);
+  if (J & 1) {
+    a[J >> 1].y -= f;
+  } else {
+    a[J >> 1].x -= f;
+    a[J >> 1].y = fmaf(-g, xb[J + 1], a[J >> 1].y);
+  }
+  float2 sA = make_float2(0.f, 0.f), sB = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int i = j + 1; i < NP; ++i) {
-        const float v = a[i] * h.scale;
-        vb[i] = v;
-        a[i] = v;
-      }
-      a[j] = h.beta;
-      my_tau = h.tau;
-    }
-    __syncwarp();
-    float v[NP];
-#pragma unroll
-    for (int q = (j + 1) / 4; q < NP / 4; ++q) {
-      const float4 t = reinterpret_cast<const float4*>(vb)[q];
-      v[4 * q + 0] = t.x;
-      v[4 * q + 1] = t.y;
-      v[4 * q + 2] = t.z;
-      v[4 * q + 3] = t.w;
-    }
-    float d = a[j];
-#pragma unroll
-    for (int i = j + 1; i < NP; ++i) d = fmaf(v[i], a[i], d);
-    const float f = (lane > j) ? h.tau * d : 0.f;
-    a[j] -= f;
-    s = 0.f;
-#pragma unroll
-    for (int i = j + 1; i < NP; ++i) {
-      a[i] = fmaf(-f, v[i], a[i]);
-      if (i > j + 1) s = fmaf(a[i], a[i], s);
+  for (int q = qf; q < NQ; ++q) {
+    a[q] = __ffma2_rn(ng, xpair<J>(xb, q), a[q]);
+    if (WANT_S) {
+      // rows strictly below J+1: for odd J pair qf starts at row J+1.
+      if (q == qf && (J & 1))
+        sA.y = fmaf(a[q].y, a[q].y, sA.y);
+      else if (((q - qf) & 1) == 0)
+        sA = __ffma2_rn(a[q], a[q], sA);
+      else
+        sB = __ffma2_rn(a[q], a[q], sB);
     }
   }
+  if (WANT_S) *s = (sA.x + sA.y) + (sB.x + sB.y);
+}
 
-  if (col_ok) {
-    float* __restrict__ Hm = H + m * (int64_t)n * n;
+struct PairState {
+  float2 a0[NQ], a1[NQ];  // columns l and l + 16
+  float s[2];             // sum of squares below the diagonal, per column slot
+  float mt[2], mb[2], ms[2];  // tau, beta, scale of the columns this lane owns
+};
+
+template <int J>
+__device__ __forceinline__ void step(PairState& st, float* xb0, float* xb1, int l,
+                                     int half, int n) {
+  if constexpr (J < NP - 1) {
+    if (J >= n - 1) return;  // uniform: the last column gets tau = 0
+    constexpr int owner = J & 15;
+    constexpr int slot = J >> 4;
+    float* xb = (J & 1) ? xb1 : xb0;
+    const float2(&ac)[NQ] = slot ? st.a1 : st.a0;
+    const int src = (half << 4) | owner;
+    const float alpha = __shfl_sync(kFull, get_row(ac, J), src);
+    const float sigma = __shfl_sync(kFull, st.s[slot], src);
+    const Reflector h = make_reflector(alpha, sigma);
+    if (l == owner) {
 #pragma unroll
-    for (int i = 0; i < NP; ++i)
-      if (i < n) Hm[(int64_t)i * n + lane] = a[i];
-    tau[m * n + lane] = my_tau;
+      for (int q4 = 0; q4 < NQ / 2; ++q4)
+        reinterpret_cast<float4*>(xb)[q4] =
+            make_float4(ac[2 * q4].x, ac[2 * q4].y, ac[2 * q4 + 1].x, ac[2 * q4 + 1].y);
+      st.mt[slot] = h.tau;
+      st.mb[slot] = h.beta;
+      st.ms[slot] = h.scale;
+    }
+    __syncwarp();
+    constexpr int next_slot = (J + 1) >> 4;
+    if constexpr (J < 15)
+      apply_step<J, next_slot == 0>(st.a0, xb, l > J, h.tau, h.scale, &st.s[0]);
+    apply_step<J, next_slot == 1>(st.a1, xb, l + 16 > J, h.tau, h.scale, &st.s[1]);
+    step<J + 1>(st, xb0, xb1, l, half, n);
   }
 }
 
-constexpr int kWarpsPerBlock = 4;
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  const int sz = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gmem), "r"(sz)
+               : "memory");
+}
+
+// 128 registers per thread (4 blocks of 4 warps per SM): config 2's 2048 warps
+// fit in one wave of 148 SMs. STAGED: contiguous, 16-byte aligned 32 x 32
+// matrices (see the memory note above).
+template <bool STAGED>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 4)
+k_fused_pair(const float* __restrict__ A, int64_t sAb, int64_t sAr,
+             float* __restrict__ H, float* __restrict__ tau, int64_t batch,
+             int n) {
+  __shared__ __align__(16) float tile[STAGED ? kWarpsPerBlock : 1][STAGED ? 2 * TMAT : 4];
+  __shared__ __align__(16) float xbuf[kWarpsPerBlock][2][2][NP];  // [warp][half][parity][row]
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int half = lane >> 4;
+  const int l = lane & 15;
+  const int64_t m0 = ((int64_t)blockIdx.x * kWarpsPerBlock + warp) * 2;
+  if (m0 >= batch) return;  // warp-uniform
+  const int64_t m = m0 + half;
+  const bool mat_ok = m < batch;  // the odd last matrix leaves one half idle
+  const int c0 = l, c1 = l + 16;
+
+  PairState st;
+  if constexpr (STAGED) {
+    float* tw = tile[warp];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {  // 2 matrices x 256 16-byte pieces
+      const int idx = lane + 32 * e;
+      const int mat = idx >> 8, row = (idx & 255) >> 3, c4 = (idx & 7) << 2;
+      const bool ok = m0 + mat < batch;
+      const float* g = A + (ok ? (m0 + mat) * sAb + row * NP + c4 : 0);
+      cp_async16(tw + mat * TMAT + row * TLD + c4, g, ok);
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    __syncwarp();
+    const float* tm = tw + half * TMAT;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      st.a0[q] = make_float2(tm[(2 * q) * TLD + c0], tm[(2 * q + 1) * TLD + c0]);
+      st.a1[q] = make_float2(tm[(2 * q) * TLD + c1], tm[(2 * q + 1) * TLD + c1]);
+    }
+  } else {
+    const float* __restrict__ Am = A + (mat_ok ? m : m0) * sAb;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int i = 2 * q;
+      const bool r0 = mat_ok && i < n, r1 = mat_ok && i + 1 < n;
+      st.a0[q].x = (r0 && c0 < n) ? __ldg(Am + (int64_t)i * sAr + c0) : 0.f;
+      st.a0[q].y = (r1 && c0 < n) ? __ldg(Am + (int64_t)(i + 1) * sAr + c0) : 0.f;
+      st.a1[q].x = (r0 && c1 < n) ? __ldg(Am + (int64_t)i * sAr + c1) : 0.f;
+      st.a1[q].y = (r1 && c1 < n) ? __ldg(Am + (int64_t)(i + 1) * sAr + c1) : 0.f;
+    }
+  }
+  {
+    float2 s2 = make_float2(st.a0[0].y * st.a0[0].y, 0.f);
+#pragma unroll
+    for (int q = 1; q < NQ; ++q) s2 = __ffma2_rn(st.a0[q], st.a0[q], s2);
+    st.s[0] = s2.x + s2.y;
+    st.s[1] = 0.f;
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) st.mt[e] = st.mb[e] = st.ms[e] = 0.f;
+
+  step<0>(st, xbuf[warp][half][0], xbuf[warp][half][1], l, half, n);
+
+  // Final columns: deferred scaling below the diagonal, beta on it.
+  float* tm = nullptr;
+  if constexpr (STAGED) tm = tile[warp] + half * TMAT;
+  float* __restrict__ Hm = H + (mat_ok ? m : 0) * (int64_t)n * n;
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    const int c = slot ? c1 : c0;
+    const float2(&ac)[NQ] = slot ? st.a1 : st.a0;
+    const bool refl = c < n - 1;  // columns 0 .. n-2 were factored
+    const float sc = st.ms[slot], be = st.mb[slot];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int i = 2 * q + e;
+        float v = e ? ac[q].y : ac[q].x;
+        if (refl) v = i > c ? v * sc : (i == c ? be : v);
+        if constexpr (STAGED)
+          tm[i * TLD + c] = v;
+        else if (mat_ok && c < n && i < n)
+          Hm[(int64_t)i * n + c] = v;
+      }
+    }
+    if (mat_ok && c < n) tau[m * n + c] = st.mt[slot];
+  }
+  if constexpr (STAGED) {
+    float* tw = tile[warp];
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int idx = lane + 32 * e;
+      const int mat = idx >> 8, row = (idx & 255) >> 3, c4 = (idx & 7) << 2;
+      if (m0 + mat < batch)
+        *reinterpret_cast<float4*>(H + (m0 + mat) * (int64_t)(NP * NP) + row * NP + c4) =
+            *reinterpret_cast<const float4*>(tw + mat * TMAT + row * TLD + c4);
+    }
+  }
+}
 
 }  // namespace
 
 int launch_fused_small(const float* A, int64_t sAb, int64_t sAr, float* H,
                        float* tau, int64_t batch, int n, cudaStream_t stream) {
   if (n < 1 || n > kFusedMaxN) return QRB_ERR_UNSUPPORTED;
-  const int64_t blocks = (batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  constexpr int64_t kPerBlock = 2 * kWarpsPerBlock;
+  const int64_t blocks = (batch + kPerBlock - 1) / kPerBlock;
   if (blocks > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
-  k_fused_warp<kWarpsPerBlock><<<(unsigned)blocks, kWarpsPerBlock * 32, 0, stream>>>(
-      A, sAb, sAr, H, tau, batch, n);
+  // Per-element loads and stores: staging whole matrices through shared memory
+  // with 16-byte copies measured slower here (more registers, no overlap).
+  k_fused_pair<false><<<(unsigned)blocks, kWarpsPerBlock * 32, 0, stream>>>(A, sAb, sAr, H, tau,
+                                                                          batch, n);
   note_launches(1);
   return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
 }

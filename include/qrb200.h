@@ -46,7 +46,8 @@ enum {
   QRB_ERR_WORKSPACE = 3,     /* workspace missing or smaller than required */
   QRB_ERR_LAUNCH = 4,        /* a kernel launch failed (cudaGetLastError) */
   QRB_ERR_DEVICE = 5,        /* no usable sm_100 device / device query failed */
-  QRB_ERR_INJECTED = 6       /* failure injected by qrb_set_config("fail_next") */
+  QRB_ERR_INJECTED = 6,      /* failure injected by qrb_set_config("fail_next") */
+  QRB_ERR_DEVICE_WAIT = 7    /* a kernel's bounded device-side wait timed out */
 };
 
 /* Library version as 10000*major + 100*minor + patch. */
@@ -101,8 +102,8 @@ QRB_API int qrb_geqrf_f32_noalloc(const float* A, int64_t strideA_b,
                                   int64_t batch, int32_t n, void* stream);
 
 /*
- * Fused whole-matrix QR for small n (n <= 32): one warp factors one matrix in
- * registers with a single launch. Replaces hh_fused_qr / _hh_fused_qr_kernel
+ * Fused whole-matrix QR for small n (n <= 32): one half-warp factors one
+ * matrix in registers (two matrices per warp) with a single launch. Replaces hh_fused_qr / _hh_fused_qr_kernel
  * (src/qrbench/triton_kernels.py:722-755, :641-720).
  */
 QRB_API int qrb_fused_qr_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
@@ -152,8 +153,18 @@ QRB_API int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row
  *                 return QRB_ERR_INJECTED without enqueuing work (host-side
  *                 fault injection for tests).
  *   "sync_check"  1: every compute call synchronises its stream and reports
- *                 asynchronous kernel faults as QRB_ERR_LAUNCH (debug mode).
- *   "larfb_tc"    column-tile width of the trailing update (64).
+ *                 asynchronous kernel faults as QRB_ERR_LAUNCH and device-side
+ *                 wait timeouts as QRB_ERR_DEVICE_WAIT (debug mode).
+ *   "larfb_kind"  trailing update: 0 (default) = FP32 FFMA; 1 = tcgen05
+ *                 tensor cores in 3xTF32 where it applies (32-reflector
+ *                 blocks, 16-byte aligned row-major operands), FFMA elsewhere.
+ *   "device_error" read: 1 if a kernel's bounded device-side wait timed out
+ *                 since the last reset (synchronous); set to 0 to reset.
+ *   "groups"      1..4: batches of 4 or more matrices with n > 32 are split
+ *                 into this many groups run on internal streams (forked from
+ *                 and joined back into the caller's stream) so that panel
+ *                 and trailing-update kernels of different groups overlap
+ *                 (default 2).
  *   "launches"    number of kernel launches this library has enqueued since
  *                 load or since the last qrb_set_config("launches", 0).
  * Returns QRB_ERR_INVALID_ARG for an unknown key or value.

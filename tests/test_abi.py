@@ -45,7 +45,7 @@ def test_library_exports_every_declared_symbol():
 def test_status_strings_and_constants():
     L = _lib.lib()
     assert L.qrb_version() >= 100
-    for code in range(7):
+    for code in range(8):
         s = _lib.status_string(code)
         assert s.startswith("qrb:")
     assert "unknown" in _lib.status_string(99)
@@ -107,6 +107,9 @@ def test_config_keys():
     _lib.set_config("sync_check", 0)
     _lib.set_config("launches", 0)
     assert _lib.get_config("launches") == 0
+    assert _lib.get_config("larfb_kind") in (0, 1)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("larfb_kind", 2)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("no_such_key", 1)
     with pytest.raises(_lib.QRBError):

@@ -248,3 +248,23 @@ def test_second_device_if_present():
     torch.cuda.synchronize(d1)
     assert torch.equal(H1.cpu(), H0) and torch.equal(t1.cpu(), t0)
     assert ctypes is not None
+
+
+@pytest.mark.parametrize("scale", [1e-18, 1e-12, 1e12, 1e18])
+@pytest.mark.parametrize("n", [24, 100])
+def test_tiny_and_huge_entries(scale, n):
+    # alpha^2 + sigma outside (1e-30, 1e30) takes the plain IEEE reflector
+    # formulas; inside, the reciprocal-square-root form. Both must give the
+    # same factorization up to scaling.
+    A = torch.randn(3, n, n, generator=torch.Generator().manual_seed(n)) * scale
+    H, tau = _gpu_qr(A)
+    Ho, to = oracle.geqr2(A.numpy(), f64=True)
+    par = checker.parity(H, tau, Ho, to)
+    assert par.ok(PARITY_RTOL), (scale, n, par)
+    assert checker.check(A, H, tau).passed
+
+
+def test_no_device_wait_timed_out():
+    # every bounded device-side wait in the kernels completed during this run
+    torch.cuda.synchronize()
+    assert _lib.get_config("device_error") == 0

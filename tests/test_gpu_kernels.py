@@ -82,10 +82,18 @@ def test_panel_kernel_shapes_and_clusters(r, w):
         assert R[:, w:].abs().max() < 1e-4 * Pd.abs().max()
 
 
-@pytest.mark.parametrize("r,k,c", [(64, 32, 64), (64, 32, 1), (100, 32, 37), (512, 32, 480),
-                                   (4096, 32, 200), (33, 32, 5), (50, 8, 13), (129, 31, 70),
-                                   (300, 1, 3)])
-def test_larfb_kernel_matches_fp64(r, k, c):
+@pytest.fixture(params=[0, 1], ids=["ffma", "tcgen05"])
+def larfb_kind(request):
+    old = _lib.get_config("larfb_kind")
+    _lib.set_config("larfb_kind", request.param)
+    yield request.param
+    _lib.set_config("larfb_kind", old)
+
+
+@pytest.mark.parametrize("r,k,c", [(64, 32, 64), (64, 32, 1), (100, 32, 36), (512, 32, 480),
+                                   (4096, 32, 200), (33, 32, 4), (50, 8, 13), (129, 31, 70),
+                                   (300, 1, 3), (129, 32, 260), (1000, 32, 132)])
+def test_larfb_kernel_matches_fp64(r, k, c, larfb_kind):
     g = torch.Generator().manual_seed(r * 7 + k + c)
     b = 3
     Vfull = torch.randn(b, r, k, generator=g)
@@ -96,10 +104,13 @@ def test_larfb_kernel_matches_fp64(r, k, c):
     # V is passed with garbage on and above the diagonal: only the strict lower part is read
     Cd = C.to(DEV)
     api.larfb(Vfull.to(DEV), T.to(DEV), Cd)
-    assert _rel(Cd, want) < 1e-5
+    # FFMA: FP32 rounding. Tensor cores in 3xTF32: each product carries ~2^-21
+    # relative error (the dropped lo*lo term) instead of 2^-24.
+    tol = 1e-5 if larfb_kind == 0 else 4e-5
+    assert _rel(Cd, want) < tol
 
 
-def test_larfb_strided_views_inside_a_matrix():
+def test_larfb_strided_views_inside_a_matrix(larfb_kind):
     # V and C as views into one packed matrix, as the blocked driver uses them
     g = torch.Generator().manual_seed(9)
     n, j0 = 200, 64
@@ -122,8 +133,33 @@ def test_larfb_strided_views_inside_a_matrix():
 def test_launch_counter_counts_kernels():
     A = torch.randn(4, 96, 96, device=DEV)
     torch.cuda.synchronize()
-    _lib.set_config("launches", 0)
-    api.geqrf(A)
-    torch.cuda.synchronize()
-    # 3 panels + 2 trailing updates
-    assert _lib.get_config("launches") == 5
+    groups = _lib.get_config("groups")
+    try:
+        for g in (1, 2):
+            _lib.set_config("groups", g)
+            _lib.set_config("launches", 0)
+            H, tau = api.geqrf(A)
+            torch.cuda.synchronize()
+            # per batch group: 3 panels + 2 trailing updates
+            assert _lib.get_config("launches") == 5 * g
+            assert checker.check(A, H, tau).passed
+    finally:
+        _lib.set_config("groups", groups)
+
+
+@pytest.mark.parametrize("n", [96, 200, 512, 1000])
+def test_geqrf_same_with_ffma_and_tensor_core_updates(n):
+    A = torch.randn(4, n, n, generator=torch.Generator().manual_seed(n)).to(DEV)
+    old = _lib.get_config("larfb_kind")
+    try:
+        out = {}
+        for kind in (0, 1):
+            _lib.set_config("larfb_kind", kind)
+            out[kind] = api.geqrf(A)
+            torch.cuda.synchronize()
+            assert checker.check(A, *out[kind]).passed, kind
+    finally:
+        _lib.set_config("larfb_kind", old)
+    par = checker.parity(out[1][0].cpu(), out[1][1].cpu(), out[0][0].cpu(), out[0][1].cpu())
+    assert par.ok(RTOL), par
+    assert _lib.get_config("device_error") == 0
