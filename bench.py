@@ -49,6 +49,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip CPU geqrf timings")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget")
+    ap.add_argument("--chunks", type=int, default=0,
+                    help="e2e pipeline depth for qrb_geqrf_f32_host (0 = 4; n <= 32 with pinned buffers runs direct)")
     ap.add_argument("--batch", type=int, default=None,
                     help="matrices per GPU (default: the config's batch); for small profiling cases")
     ap.add_argument("--quick", action="store_true",
@@ -405,8 +407,10 @@ def run_ours(args, info) -> int:
     tau_host = torch.empty(A_host.shape[0], cfg.n).pin_memory()
     e2e_steps = max(3, min(args.steps, 50))
 
+    e2e_ws = torch.empty(api.host_workspace_bytes(b, cfg.n), dtype=torch.uint8, device=dev)
+
     def e2e_step():
-        api.geqrf_host(A_host, H_host, tau_host, device=dev)
+        api.geqrf_host(A_host, H_host, tau_host, device=dev, chunks=args.chunks, workspace=e2e_ws)
 
     for _ in range(2):
         e2e_step()
@@ -474,7 +478,8 @@ def run_ours(args, info) -> int:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "api": "gpumode_qr_b200.api.geqrf_host (pinned host in/out)"},
+                    "api": "qrb_geqrf_f32_host via gpumode_qr_b200.api.geqrf_host (pinned host in/out)",
+                    "chunks": args.chunks},
             "gpu_launches": launches_total,
             "clocks": clk.summary(),
             "gates": {"factor": gate.factor_residual, "orth": gate.orth_residual,

@@ -137,20 +137,28 @@ def geqrf_out(A: torch.Tensor, H: torch.Tensor, tau: torch.Tensor) -> tuple[torc
     return H, tau
 
 
+def host_workspace_bytes(batch: int, n: int) -> int:
+    """Device staging bytes :func:`geqrf_host` needs (``qrb_host_workspace_bytes``)."""
+    return int(_lib.lib().qrb_host_workspace_bytes(batch, n))
+
+
 def geqrf_host(A_host: torch.Tensor, H_host: torch.Tensor, tau_host: torch.Tensor,
-               device: torch.device | int | str = "cuda", chunks: int = 8) -> None:
+               device: torch.device | int | str = "cuda", chunks: int = 0,
+               workspace: torch.Tensor | None = None) -> None:
     """Factor a host-resident batch end to end: host -> device -> QR -> host.
 
-    ``A_host`` ``[b, n, n]``, ``H_host`` ``[b, n, n]`` and ``tau_host`` ``[b, n]``
-    are contiguous float32 CPU tensors, ideally pinned (then every copy is
-    asynchronous). The batch is split into ``chunks`` pieces and run as a
-    three-stage pipeline on three streams of the device: all host-to-device
-    copies back to back on a copy-in stream, each piece's factorization on a
-    compute stream once its copy has landed, and its device-to-host copy on a
-    copy-out stream once it is factored. The two copy directions run at the
-    same time on separate copy engines. Work is ordered after, and its
-    completion joined back into, the device's current stream; synchronise that
-    stream before reading the outputs on the host.
+    ``A_host`` ``[b, n, n]``, ``H_host`` ``[b, n, n]`` (may be ``A_host``) and
+    ``tau_host`` ``[b, n]`` are contiguous float32 CPU tensors, ideally pinned
+    (then the two copy directions overlap each other and the factorization).
+    One call of ``qrb_geqrf_f32_host``. For n <= 32 with pinned (mapped) buffers
+    the fused kernel reads and writes host memory directly in one launch;
+    otherwise the batch is cut into ``chunks`` pieces (0 = 4) pipelined over
+    copy-in, compute and copy-out streams inside the library. Either way the
+    work is ordered after, and joined back into, the device's current stream;
+    synchronise that stream before reading the outputs.
+    ``workspace`` (optional) is a device uint8 tensor of at least
+    :func:`host_workspace_bytes` bytes; by default one is taken from the torch
+    caching allocator for the call.
     """
     dev = torch.device(device)
     if dev.type != "cuda":
@@ -167,52 +175,20 @@ def geqrf_host(A_host: torch.Tensor, H_host: torch.Tensor, tau_host: torch.Tenso
         raise ValueError("H_host / tau_host shapes do not match A_host")
     if b == 0 or n == 0:
         return
-    chunks = max(1, min(int(chunks), b))
-    per = (b + chunks - 1) // chunks
+    L = _lib.lib()
+    need = int(L.qrb_host_workspace_bytes(b, n))
     with torch.cuda.device(dev):
-        main = torch.cuda.current_stream(dev)
-        s_in, s_comp, s_out = _host_streams(dev)
-        A_d = torch.empty((b, n, n), dtype=torch.float32, device=dev)
-        H_d = torch.empty((b, n, n), dtype=torch.float32, device=dev)
-        t_d = torch.empty((b, n), dtype=torch.float32, device=dev)
-        ws_n = workspace_bytes(per, n)
-        ws = torch.empty(max(ws_n, 16), dtype=torch.uint8, device=dev)
-        L = _lib.lib()
-        for st in (s_in, s_comp, s_out):
-            st.wait_stream(main)
-        for s0 in range(0, b, per):
-            s1 = min(b, s0 + per)
-            landed = torch.cuda.Event()
-            factored = torch.cuda.Event()
-            with torch.cuda.stream(s_in):
-                A_d[s0:s1].copy_(A_host[s0:s1], non_blocking=True)
-                landed.record(s_in)
-            s_comp.wait_event(landed)
-            rc = L.qrb_geqrf_f32(
-                A_d[s0:s1].data_ptr(), n * n, n, H_d[s0:s1].data_ptr(), t_d[s0:s1].data_ptr(),
-                s1 - s0, n, ws.data_ptr(), ws_n, s_comp.cuda_stream,
-            )
-            _lib.check(rc)
-            factored.record(s_comp)
-            s_out.wait_event(factored)
-            with torch.cuda.stream(s_out):
-                H_host[s0:s1].copy_(H_d[s0:s1], non_blocking=True)
-                tau_host[s0:s1].copy_(t_d[s0:s1], non_blocking=True)
-        for st in (s_in, s_comp, s_out):
-            main.wait_stream(st)
-        for t in (A_d, H_d, t_d, ws):
-            for st in (main, s_in, s_comp, s_out):
-                t.record_stream(st)
-
-
-_HOST_STREAMS: dict[int, list] = {}
-
-
-def _host_streams(dev: torch.device) -> list:
-    key = dev.index
-    if key not in _HOST_STREAMS:
-        _HOST_STREAMS[key] = [torch.cuda.Stream(device=dev) for _ in range(3)]
-    return _HOST_STREAMS[key]
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        elif (not workspace.is_cuda or workspace.device != dev
+              or workspace.numel() * workspace.element_size() < need):
+            raise ValueError(f"workspace must be a device tensor of >= {need} bytes on {dev}")
+        rc = L.qrb_geqrf_f32_host(
+            A_host.data_ptr(), H_host.data_ptr(), tau_host.data_ptr(), b, n,
+            workspace.data_ptr(), workspace.numel() * workspace.element_size(), int(chunks),
+            torch.cuda.current_stream(dev).cuda_stream,
+        )
+        _lib.check(rc)
 
 
 def hh_fused_qr(A: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

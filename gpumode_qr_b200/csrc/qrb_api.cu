@@ -15,6 +15,9 @@ std::atomic<int64_t> g_sync_check{0};
 std::atomic<int64_t> g_larfb_kind{0};  // 0 = FFMA, 1 = tcgen05 3xTF32
 std::atomic<int64_t> g_launches{0};
 std::atomic<int64_t> g_groups{2};
+std::atomic<int64_t> g_host_direct{3};
+std::atomic<int64_t> g_direct_blocks{0};
+std::atomic<int64_t> g_host_ramp{0};
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -120,6 +123,51 @@ namespace qrb {
 void note_launches(int64_t count) { g_launches.fetch_add(count); }
 }  // namespace qrb
 
+namespace qrb {
+
+bool take_injected_failure_any() { return take_injected_failure(); }
+int host_direct_mode() { return (int)g_host_direct.load(); }
+bool host_ramp() { return g_host_ramp.load() != 0; }
+int64_t host_direct_blocks() {
+  const int64_t b = g_direct_blocks.load();
+  return b > 0 ? b : kHostDirectBlocks;
+}
+int finish_call(int rc, cudaStream_t stream) { return finish(rc, stream); }
+
+// The whole factorization of validated arguments, enqueued on s: the fused
+// kernel for n <= 32, the blocked loop (optionally split into batch groups on
+// internal streams) otherwise. T is the caller's workspace (n > 32 only).
+int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
+                  float* T, int64_t batch, int n, cudaStream_t s) {
+  if (n <= kFusedMaxN) return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
+  const int groups = (int)(batch >= 4 ? g_groups.load() : 1);
+  if (groups <= 1) return blocked_qr(A, strideA_b, strideA_row, H, tau, T, batch, n, s);
+  // Split the batch into groups that run the same kernel sequence on separate
+  // internal streams, forked from and joined back into the caller's stream, so
+  // that one group's (latency-bound) panel kernels overlap another group's
+  // trailing updates.
+  SideStreams* ss = side_streams();
+  if (ss == nullptr) return QRB_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(ss->mu);
+  if (cudaEventRecord(ss->fork, s) != cudaSuccess) return QRB_ERR_LAUNCH;
+  const int64_t nn = (int64_t)n * n;
+  int rc = QRB_OK;
+  for (int g = 0; g < groups && rc == QRB_OK; ++g) {
+    const int64_t b0 = batch * g / groups, b1 = batch * (g + 1) / groups;
+    if (b1 <= b0) continue;
+    cudaStream_t gs = ss->s[g];
+    if (cudaStreamWaitEvent(gs, ss->fork, 0) != cudaSuccess) return QRB_ERR_LAUNCH;
+    rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
+                    T + b0 * (int64_t)kPanelW * kPanelW, b1 - b0, n, gs);
+    if (cudaEventRecord(ss->join[g], gs) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
+    if (cudaStreamWaitEvent(s, ss->join[g], 0) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
+  }
+  return rc;
+}
+
+}  // namespace qrb
+
+
 extern "C" {
 
 int qrb_version(void) { return 100; }
@@ -202,45 +250,16 @@ int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
   if (n > qrb::kMaxN) return QRB_ERR_UNSUPPORTED;
   if (bad_matrix_strides(strideA_b, strideA_row, n, n, batch)) return QRB_ERR_INVALID_ARG;
   if (A == H && (strideA_row != n || strideA_b != (int64_t)n * n)) return QRB_ERR_INVALID_ARG;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (n <= qrb::kFusedMaxN) {
-    if (take_injected_failure()) return QRB_ERR_INJECTED;
-    return finish(qrb::launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s), s);
+  if (n > qrb::kFusedMaxN) {
+    const size_t need = qrb_workspace_bytes(batch, n);
+    if (workspace == nullptr || workspace_bytes < need) return QRB_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
   }
-  const size_t need = qrb_workspace_bytes(batch, n);
-  if (workspace == nullptr || workspace_bytes < need) return QRB_ERR_WORKSPACE;
-  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
   if (take_injected_failure()) return QRB_ERR_INJECTED;
-
-  float* T = static_cast<float*>(workspace);
-  const int groups = (int)(batch >= 4 ? g_groups.load() : 1);
-  if (groups <= 1) {
-    const int rc = blocked_qr(A, strideA_b, strideA_row, H, tau, T, batch, n, s);
-    return finish(rc, s);
-  }
-  // Split the batch into groups that run the same kernel sequence on separate
-  // internal streams, forked from and joined back into the caller's stream, so
-  // that one group's (latency-bound) panel kernels overlap another group's
-  // trailing updates.
-  int rc = QRB_OK;
-  {
-    SideStreams* ss = side_streams();
-    if (ss == nullptr) return QRB_ERR_DEVICE;
-    std::lock_guard<std::mutex> lock(ss->mu);
-    if (cudaEventRecord(ss->fork, s) != cudaSuccess) return QRB_ERR_LAUNCH;
-    const int64_t nn = (int64_t)n * n;
-    for (int g = 0; g < groups && rc == QRB_OK; ++g) {
-      const int64_t b0 = batch * g / groups, b1 = batch * (g + 1) / groups;
-      if (b1 <= b0) continue;
-      cudaStream_t gs = ss->s[g];
-      if (cudaStreamWaitEvent(gs, ss->fork, 0) != cudaSuccess) return QRB_ERR_LAUNCH;
-      rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
-                      T + b0 * (int64_t)qrb::kPanelW * qrb::kPanelW, b1 - b0, n, gs);
-      if (cudaEventRecord(ss->join[g], gs) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
-      if (cudaStreamWaitEvent(s, ss->join[g], 0) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
-    }
-  }
-  return finish(rc, s);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return finish(qrb::geqrf_enqueue(A, strideA_b, strideA_row, H, tau,
+                                   static_cast<float*>(workspace), batch, n, s),
+                s);
 }
 
 int qrb_set_config(const char* key, int64_t value) {
@@ -270,6 +289,21 @@ int qrb_set_config(const char* key, int64_t value) {
     g_groups.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "host_direct") == 0) {
+    if (value < 0 || value > 3) return QRB_ERR_INVALID_ARG;
+    g_host_direct.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "host_ramp") == 0) {
+    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    g_host_ramp.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "direct_blocks") == 0) {
+    if (value < 0 || value > (1 << 20)) return QRB_ERR_INVALID_ARG;
+    g_direct_blocks.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "launches") == 0) {
     if (value != 0) return QRB_ERR_INVALID_ARG;
     g_launches.store(0);
@@ -291,6 +325,10 @@ int qrb_get_config(const char* key, int64_t* value) {
   }
   if (std::strcmp(key, "launches") == 0) { *value = g_launches.load(); return QRB_OK; }
   if (std::strcmp(key, "groups") == 0) { *value = g_groups.load(); return QRB_OK; }
+  if (std::strcmp(key, "host_direct") == 0) { *value = g_host_direct.load(); return QRB_OK; }
+  if (std::strcmp(key, "host_ramp") == 0) { *value = g_host_ramp.load(); return QRB_OK; }
+  if (std::strcmp(key, "direct_blocks") == 0) { *value = qrb::host_direct_blocks(); return QRB_OK; }
+  if (std::strcmp(key, "host_path") == 0) { *value = qrb::host_last_path(); return QRB_OK; }
   return QRB_ERR_INVALID_ARG;
 }
 

@@ -13,6 +13,7 @@ constexpr int kPanelW = 32;        // panel / block-reflector width
 constexpr int kFusedMaxN = 32;     // largest n of the warp-per-matrix kernel
 constexpr int kMaxN = 8192;        // 4096 rows per CTA-cluster of 8 x 512 x 2
 constexpr int kMaxCluster = 8;
+constexpr int64_t kHostDirectBlocks = 148;  // direct host-memory kernel: blocks of 4 warps
 
 // Householder coefficients for one column, LAPACK slarfg convention as the
 // reference kernels state it (src/qrbench/triton_kernels.py:691-700):
@@ -60,8 +61,15 @@ __device__ __forceinline__ Reflector make_reflector(float alpha, float sigma) {
 
 // Internal launchers (one per kernel family); all return qrb status codes and
 // only enqueue work on `stream`.
+// Which operands of the fused kernel are page-locked host memory mapped into
+// the device's address space (accessed with streaming loads and stores).
+enum class HostMem { kNone, kTau, kOutputs /* H and tau */, kAll /* A, H and tau */ };
+
+// max_blocks > 0 caps the grid when A or H is host memory (each warp then
+// loops over matrix pairs).
 int launch_fused_small(const float* A, int64_t sAb, int64_t sAr, float* H,
-                       float* tau, int64_t batch, int n, cudaStream_t stream);
+                       float* tau, int64_t batch, int n, cudaStream_t stream,
+                       HostMem where = HostMem::kNone, int64_t max_blocks = 0);
 
 // Factor the r x w panel starting at (row 0, col 0) of src (row stride ld_src,
 // matrix stride sb_src) into dst; tau to tau_out[m*tau_sb + c]; T to
@@ -97,6 +105,32 @@ int launch_larfb_tc(const float* V, int64_t sVb, int64_t ldv, const float* T,
 // Device-side error flag set by kernels whose bounded waits timed out
 // (synchronous read; optionally reset to 0).
 int device_error_flag(int* value, bool reset);
+
+// Whole factorization of already validated arguments, enqueued on `stream`
+// (no fault injection, no sync check); T is the qrb_workspace_bytes scratch.
+int geqrf_enqueue(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau, float* T,
+                  int64_t batch, int n, cudaStream_t stream);
+
+// The public entry points' shared epilogue pieces: consume one injected
+// failure (fail_next), and apply the sync_check mode to a call's status.
+bool take_injected_failure_any();
+int finish_call(int rc, cudaStream_t stream);
+
+// qrb_set_config("host_direct") for qrb_geqrf_f32_host with n <= 32 and
+// mapped page-locked host buffers: 0 = copies in and out; 1 = the kernel
+// reads A and writes H and tau in host memory itself; 2 = copies in, the
+// kernel writes H and tau to host memory; 3 = copies in and out for the
+// matrices, the kernel writes tau to host memory.
+int host_direct_mode();
+// qrb_set_config("host_ramp"): 1 = chunk sizes rise and fall (1, 2, .., 2, 1)
+// so that the pipeline fills and drains on small pieces; 0 = equal chunks.
+bool host_ramp();
+// qrb_set_config("direct_blocks"): grid of the direct kernel (0 = automatic).
+int64_t host_direct_blocks();
+
+// Path taken by the last qrb_geqrf_f32_host call (the host_direct mode that
+// ran: 0..3), -1 none yet (qrb_get_config("host_path")).
+int64_t host_last_path();
 
 // Count of kernel launches enqueued by this library (all devices, all calls);
 // read through qrb_get_config("launches").

@@ -14,7 +14,10 @@
 // register name and only rows below j are touched).
 //
 // Memory: every lane loads and stores its own columns element by element
-// (a half-warp touches 64 contiguous bytes of a row per access).
+// (a half-warp touches 64 contiguous bytes of a row per access). The host
+// instantiations serve host-resident batches: A and/or H and tau are
+// page-locked host memory mapped into the device address space, read and
+// written once with streaming (evict-first) loads and stores.
 //
 // Step j: the owner lane publishes its unscaled column x through a per-half
 // shared-memory line, every lane reads it back as row pairs (once for the dot
@@ -40,8 +43,6 @@ namespace {
 constexpr int NP = kFusedMaxN;  // padded matrix size (32 rows/columns)
 constexpr int NQ = NP / 2;      // row pairs
 constexpr int kWarpsPerBlock = 4;
-constexpr int TLD = 36;                    // tile row stride (floats)
-constexpr int TMAT = NP * TLD + 16;        // tile floats per matrix (+16: bank shift)
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
@@ -139,63 +140,39 @@ __device__ __forceinline__ void step(PairState& st, float* xb0, float* xb1, int 
   }
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
-  const int sz = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gmem), "r"(sz)
-               : "memory");
+template <bool SYS>
+__device__ __forceinline__ float load_a(const float* p) {
+  if constexpr (SYS) return __ldcs(p);
+  else return __ldg(p);
 }
 
-// 128 registers per thread (4 blocks of 4 warps per SM): config 2's 2048 warps
-// fit in one wave of 148 SMs. STAGED: contiguous, 16-byte aligned 32 x 32
-// matrices (see the memory note above).
-template <bool STAGED>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32, 4)
-k_fused_pair(const float* __restrict__ A, int64_t sAb, int64_t sAr,
-             float* __restrict__ H, float* __restrict__ tau, int64_t batch,
-             int n) {
-  __shared__ __align__(16) float tile[STAGED ? kWarpsPerBlock : 1][STAGED ? 2 * TMAT : 4];
-  __shared__ __align__(16) float xbuf[kWarpsPerBlock][2][2][NP];  // [warp][half][parity][row]
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int half = lane >> 4;
-  const int l = lane & 15;
-  const int64_t m0 = ((int64_t)blockIdx.x * kWarpsPerBlock + warp) * 2;
-  if (m0 >= batch) return;  // warp-uniform
+template <bool SYS>
+__device__ __forceinline__ void store_h(float* p, float v) {
+  if constexpr (SYS) __stcs(p, v);
+  else *p = v;
+}
+
+// Factor matrices m0 and m0 + 1 (when < batch) with this warp.
+template <bool IN_SYS, bool H_SYS, bool TAU_SYS>
+__device__ __forceinline__ void factor_pair(const float* __restrict__ A, int64_t sAb, int64_t sAr,
+                                            float* __restrict__ H, float* __restrict__ tau,
+                                            int64_t batch, int n, int64_t m0, float* xb0,
+                                            float* xb1, int half, int l) {
   const int64_t m = m0 + half;
   const bool mat_ok = m < batch;  // the odd last matrix leaves one half idle
   const int c0 = l, c1 = l + 16;
 
   PairState st;
-  if constexpr (STAGED) {
-    float* tw = tile[warp];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {  // 2 matrices x 256 16-byte pieces
-      const int idx = lane + 32 * e;
-      const int mat = idx >> 8, row = (idx & 255) >> 3, c4 = (idx & 7) << 2;
-      const bool ok = m0 + mat < batch;
-      const float* g = A + (ok ? (m0 + mat) * sAb + row * NP + c4 : 0);
-      cp_async16(tw + mat * TMAT + row * TLD + c4, g, ok);
-    }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-    __syncwarp();
-    const float* tm = tw + half * TMAT;
-#pragma unroll
-    for (int q = 0; q < NQ; ++q) {
-      st.a0[q] = make_float2(tm[(2 * q) * TLD + c0], tm[(2 * q + 1) * TLD + c0]);
-      st.a1[q] = make_float2(tm[(2 * q) * TLD + c1], tm[(2 * q + 1) * TLD + c1]);
-    }
-  } else {
+  {
     const float* __restrict__ Am = A + (mat_ok ? m : m0) * sAb;
 #pragma unroll
     for (int q = 0; q < NQ; ++q) {
       const int i = 2 * q;
       const bool r0 = mat_ok && i < n, r1 = mat_ok && i + 1 < n;
-      st.a0[q].x = (r0 && c0 < n) ? __ldg(Am + (int64_t)i * sAr + c0) : 0.f;
-      st.a0[q].y = (r1 && c0 < n) ? __ldg(Am + (int64_t)(i + 1) * sAr + c0) : 0.f;
-      st.a1[q].x = (r0 && c1 < n) ? __ldg(Am + (int64_t)i * sAr + c1) : 0.f;
-      st.a1[q].y = (r1 && c1 < n) ? __ldg(Am + (int64_t)(i + 1) * sAr + c1) : 0.f;
+      st.a0[q].x = (r0 && c0 < n) ? load_a<IN_SYS>(Am + (int64_t)i * sAr + c0) : 0.f;
+      st.a0[q].y = (r1 && c0 < n) ? load_a<IN_SYS>(Am + (int64_t)(i + 1) * sAr + c0) : 0.f;
+      st.a1[q].x = (r0 && c1 < n) ? load_a<IN_SYS>(Am + (int64_t)i * sAr + c1) : 0.f;
+      st.a1[q].y = (r1 && c1 < n) ? load_a<IN_SYS>(Am + (int64_t)(i + 1) * sAr + c1) : 0.f;
     }
   }
   {
@@ -208,11 +185,9 @@ k_fused_pair(const float* __restrict__ A, int64_t sAb, int64_t sAr,
 #pragma unroll
   for (int e = 0; e < 2; ++e) st.mt[e] = st.mb[e] = st.ms[e] = 0.f;
 
-  step<0>(st, xbuf[warp][half][0], xbuf[warp][half][1], l, half, n);
+  step<0>(st, xb0, xb1, l, half, n);
 
   // Final columns: deferred scaling below the diagonal, beta on it.
-  float* tm = nullptr;
-  if constexpr (STAGED) tm = tile[warp] + half * TMAT;
   float* __restrict__ Hm = H + (mat_ok ? m : 0) * (int64_t)n * n;
 #pragma unroll
   for (int slot = 0; slot < 2; ++slot) {
@@ -227,24 +202,42 @@ k_fused_pair(const float* __restrict__ A, int64_t sAb, int64_t sAr,
         const int i = 2 * q + e;
         float v = e ? ac[q].y : ac[q].x;
         if (refl) v = i > c ? v * sc : (i == c ? be : v);
-        if constexpr (STAGED)
-          tm[i * TLD + c] = v;
-        else if (mat_ok && c < n && i < n)
-          Hm[(int64_t)i * n + c] = v;
+        if (mat_ok && c < n && i < n) store_h<H_SYS>(Hm + (int64_t)i * n + c, v);
       }
     }
-    if (mat_ok && c < n) tau[m * n + c] = st.mt[slot];
+    if (mat_ok && c < n) store_h<TAU_SYS>(tau + m * n + c, st.mt[slot]);
   }
-  if constexpr (STAGED) {
-    float* tw = tile[warp];
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int idx = lane + 32 * e;
-      const int mat = idx >> 8, row = (idx & 255) >> 3, c4 = (idx & 7) << 2;
-      if (m0 + mat < batch)
-        *reinterpret_cast<float4*>(H + (m0 + mat) * (int64_t)(NP * NP) + row * NP + c4) =
-            *reinterpret_cast<const float4*>(tw + mat * TMAT + row * TLD + c4);
+}
+
+// 128 registers per thread (4 blocks of 4 warps per SM): config 2's 2048 warps
+// fit in one wave of 148 SMs. With device memory the grid covers every pair
+// and each warp factors one. IN_SYS / H_SYS / TAU_SYS: A / H / tau are mapped
+// host memory; with IN_SYS or H_SYS each warp factors the pairs p, p + P,
+// p + 2P, ... (P = warps in the grid), and the grid is kept small on purpose so
+// that the first pairs of every warp are written back over PCIe while later
+// pairs are still being read.
+template <bool IN_SYS, bool H_SYS, bool TAU_SYS>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 4)
+k_fused_pair(const float* __restrict__ A, int64_t sAb, int64_t sAr,
+             float* __restrict__ H, float* __restrict__ tau, int64_t batch,
+             int n) {
+  __shared__ __align__(16) float xbuf[kWarpsPerBlock][2][2][NP];  // [warp][half][parity][row]
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int half = lane >> 4;
+  const int l = lane & 15;
+  const int64_t pairs = (batch + 1) / 2;
+  const int64_t first = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if constexpr (!IN_SYS && !H_SYS) {  // device matrices: the grid covers every pair
+    if (first < pairs)
+      factor_pair<false, false, TAU_SYS>(A, sAb, sAr, H, tau, batch, n, 2 * first,
+                                         xbuf[warp][half][0], xbuf[warp][half][1], half, l);
+  } else {
+    const int64_t stride = (int64_t)gridDim.x * kWarpsPerBlock;
+    for (int64_t p = first; p < pairs; p += stride) {
+      __syncwarp();  // the previous pair's readers are done with xbuf
+      factor_pair<IN_SYS, H_SYS, TAU_SYS>(A, sAb, sAr, H, tau, batch, n, 2 * p,
+                                          xbuf[warp][half][0], xbuf[warp][half][1], half, l);
     }
   }
 }
@@ -252,15 +245,32 @@ k_fused_pair(const float* __restrict__ A, int64_t sAb, int64_t sAr,
 }  // namespace
 
 int launch_fused_small(const float* A, int64_t sAb, int64_t sAr, float* H,
-                       float* tau, int64_t batch, int n, cudaStream_t stream) {
+                       float* tau, int64_t batch, int n, cudaStream_t stream, HostMem where,
+                       int64_t max_blocks) {
   if (n < 1 || n > kFusedMaxN) return QRB_ERR_UNSUPPORTED;
   constexpr int64_t kPerBlock = 2 * kWarpsPerBlock;
-  const int64_t blocks = (batch + kPerBlock - 1) / kPerBlock;
-  if (blocks > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
+  const bool looped = where == HostMem::kAll || where == HostMem::kOutputs;
+  int64_t blocks = (batch + kPerBlock - 1) / kPerBlock;
+  if (!looped && blocks > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
+  if (looped && max_blocks > 0 && blocks > max_blocks) blocks = max_blocks;
+  if (blocks > 0x7fffffffLL) blocks = 0x7fffffffLL;  // host matrices: the kernel loops
   // Per-element loads and stores: staging whole matrices through shared memory
   // with 16-byte copies measured slower here (more registers, no overlap).
-  k_fused_pair<false><<<(unsigned)blocks, kWarpsPerBlock * 32, 0, stream>>>(A, sAb, sAr, H, tau,
-                                                                          batch, n);
+  const dim3 grid((unsigned)blocks), block(kWarpsPerBlock * 32);
+  switch (where) {
+    case HostMem::kNone:
+      k_fused_pair<false, false, false><<<grid, block, 0, stream>>>(A, sAb, sAr, H, tau, batch, n);
+      break;
+    case HostMem::kTau:
+      k_fused_pair<false, false, true><<<grid, block, 0, stream>>>(A, sAb, sAr, H, tau, batch, n);
+      break;
+    case HostMem::kOutputs:
+      k_fused_pair<false, true, true><<<grid, block, 0, stream>>>(A, sAb, sAr, H, tau, batch, n);
+      break;
+    case HostMem::kAll:
+      k_fused_pair<true, true, true><<<grid, block, 0, stream>>>(A, sAb, sAr, H, tau, batch, n);
+      break;
+  }
   note_launches(1);
   return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
 }

@@ -6,7 +6,8 @@
  * Layout conventions shared by every entry point:
  *   - Matrices are batched, row-major, FP32: element (i, j) of matrix m lives at
  *     base + m * stride_b + i * stride_row + j (the column stride is 1).
- *   - All pointers are device pointers; `stream` is a cudaStream_t (NULL = the
+ *   - All pointers are device pointers (qrb_geqrf_f32_host's A_host, H_host and
+ *     tau_host excepted); `stream` is a cudaStream_t (NULL = the
  *     legacy default stream). Work is enqueued stream-ordered and the call
  *     returns without synchronising.
  *   - The library allocates no device memory per call. Scratch space, when an
@@ -102,6 +103,41 @@ QRB_API int qrb_geqrf_f32_noalloc(const float* A, int64_t strideA_b,
                                   int64_t batch, int32_t n, void* stream);
 
 /*
+ * Host memory in, host memory out: the batched QR of a host-resident batch,
+ * with the host<->device copies pipelined against the factorization. It has
+ * no single counterpart in the reference, whose impl takes device tensors; it
+ * replaces the round trip a host-side caller of the reference composes,
+ *   H, tau = impl(A.to("cuda")); H.cpu(); tau.cpu()
+ * (src/qrbench/reference.py:15 QRImpl). Results are bit-identical to
+ * qrb_geqrf_f32 on the same data.
+ *
+ *   A_host    input, batch x n x n contiguous FP32 in host memory.
+ *   H_host    output, batch x n x n contiguous (may equal A_host).
+ *   tau_host  output, batch x n contiguous.
+ *   workspace device memory of qrb_host_workspace_bytes(batch, n) bytes,
+ *             256-byte aligned (staging for A/H and tau, plus the T scratch).
+ *   chunks    pipeline depth: the batch is cut into this many pieces
+ *             (1..64; 0 = 6 for n <= 64, else 4; capped at batch).
+ * The pieces run on three internal streams of the current device (copy in,
+ * factor, copy out), forked from and joined back into `stream`: synchronise
+ * `stream` before reading H_host / tau_host. Page-locked host buffers
+ * (cudaHostAlloc / cudaHostRegister) are needed for the copies to overlap;
+ * pageable buffers give correct results with serialised copies. Calls on one
+ * device share the internal streams and are serialised on them.
+ * For n <= 32 the kernel can reach host buffers that lie in page-locked
+ * allocations mapped into the current device's address space directly
+ * (qrb_set_config("host_direct", mode)): 3 (default) = it writes tau to host
+ * memory, the matrices are copied; 1 = it reads A and writes H and tau over
+ * PCIe itself in one launch on `stream`, without copies; 2 = A is copied in,
+ * it writes H and tau; 0 = copies only. A buffer that fails the mapping check
+ * is copied. qrb_get_config("host_path") tells which mode the last call ran.
+ */
+QRB_API size_t qrb_host_workspace_bytes(int64_t batch, int32_t n);
+QRB_API int qrb_geqrf_f32_host(const float* A_host, float* H_host, float* tau_host,
+                               int64_t batch, int32_t n, void* workspace,
+                               size_t workspace_bytes, int32_t chunks, void* stream);
+
+/*
  * Fused whole-matrix QR for small n (n <= 32): one half-warp factors one
  * matrix in registers (two matrices per warp) with a single launch. Replaces hh_fused_qr / _hh_fused_qr_kernel
  * (src/qrbench/triton_kernels.py:722-755, :641-720).
@@ -165,6 +201,13 @@ QRB_API int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row
  *                 and joined back into the caller's stream) so that panel
  *                 and trailing-update kernels of different groups overlap
  *                 (default 2).
+ *   "host_direct" 0..3 (default 3): how qrb_geqrf_f32_host reaches mapped
+ *                 page-locked host buffers for n <= 32 (see there).
+ *   "direct_blocks" grid of the mode-1 kernel in blocks of 4 warps (0 = 148).
+ *   "host_ramp"   1: qrb_geqrf_f32_host cuts the batch into pieces of relative
+ *                 size 1, 2, .., 2, 1 instead of equal pieces (default 0).
+ *   "host_path"   read: the host_direct mode the last qrb_geqrf_f32_host call
+ *                 ran (0..3; -1 before the first call).
  *   "launches"    number of kernel launches this library has enqueued since
  *                 load or since the last qrb_set_config("launches", 0).
  * Returns QRB_ERR_INVALID_ARG for an unknown key or value.

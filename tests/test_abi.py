@@ -25,7 +25,7 @@ def declared_symbols() -> list[str]:
 def test_header_declares_the_expected_entry_points():
     assert set(declared_symbols()) == {
         "qrb_version", "qrb_status_string", "qrb_max_n", "qrb_workspace_bytes", "qrb_geqrf_f32",
-        "qrb_geqrf_f32_noalloc", "qrb_fused_qr_f32", "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32",
+        "qrb_geqrf_f32_noalloc", "qrb_host_workspace_bytes", "qrb_geqrf_f32_host", "qrb_fused_qr_f32", "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32",
         "qrb_set_config", "qrb_get_config",
     }
 
@@ -58,6 +58,31 @@ def test_workspace_bytes():
     assert L.qrb_workspace_bytes(4096, 32) == 0
     assert L.qrb_workspace_bytes(8, 64) == 8 * 32 * 32 * 4
     assert L.qrb_workspace_bytes(0, 512) == 0
+
+
+def test_host_entry_workspace_and_validation_without_gpu():
+    L = _lib.lib()
+    mats, taus = 8 * 64 * 64 * 4, 8 * 64 * 4
+    up = lambda x: (x + 255) // 256 * 256
+    assert L.qrb_host_workspace_bytes(8, 64) == up(mats) + up(taus) + 8 * 32 * 32 * 4
+    assert L.qrb_host_workspace_bytes(4096, 32) == up(4096 * 32 * 32 * 4) + up(4096 * 32 * 4)
+    assert L.qrb_host_workspace_bytes(0, 64) == 0
+    assert L.qrb_host_workspace_bytes(4, 8193) == 0
+    need = L.qrb_host_workspace_bytes(8, 64)
+    ws = ctypes.c_void_p(0x100000)
+    # empty problems succeed without touching memory
+    assert L.qrb_geqrf_f32_host(None, None, None, 0, 64, None, 0, 0, None) == 0
+    # null host pointers, negative sizes, chunks outside 0..64
+    assert L.qrb_geqrf_f32_host(None, FAKE, FAKE, 8, 64, ws, need, 0, None) == 1
+    assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, -1, 64, ws, need, 0, None) == 1
+    assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, ws, need, 65, None) == 1
+    assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, ws, need, -1, None) == 1
+    # too large, missing / short / misaligned workspace
+    assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 1, 8193, ws, 1 << 30, 0, None) == 2
+    assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, None, need, 0, None) == 3
+    assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, ws, need - 1, 0, None) == 3
+    assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, ctypes.c_void_p(0x100010), need, 0,
+                                None) == 1
 
 
 def test_argument_validation_without_gpu():
@@ -110,6 +135,29 @@ def test_config_keys():
     assert _lib.get_config("larfb_kind") in (0, 1)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("larfb_kind", 2)
+    assert _lib.get_config("host_direct") in (0, 1, 2, 3)
+    _lib.set_config("host_direct", 0)
+    assert _lib.get_config("host_direct") == 0
+    _lib.set_config("host_direct", 2)
+    assert _lib.get_config("host_direct") == 2
+    _lib.set_config("host_direct", 1)
+    assert _lib.get_config("host_direct") == 1
+    _lib.set_config("host_direct", 3)  # the default
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("host_direct", 4)
+    assert _lib.get_config("host_ramp") == 0
+    _lib.set_config("host_ramp", 1)
+    assert _lib.get_config("host_ramp") == 1
+    _lib.set_config("host_ramp", 0)
+    assert _lib.get_config("direct_blocks") > 0
+    _lib.set_config("direct_blocks", 7)
+    assert _lib.get_config("direct_blocks") == 7
+    _lib.set_config("direct_blocks", 0)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("direct_blocks", -1)
+    assert _lib.get_config("host_path") in (-1, 0, 1, 2, 3)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("host_path", 1)  # read-only
     with pytest.raises(_lib.QRBError):
         _lib.set_config("no_such_key", 1)
     with pytest.raises(_lib.QRBError):

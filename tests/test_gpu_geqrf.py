@@ -218,12 +218,98 @@ def test_error_paths_raise():
         api.hh_fused_qr(torch.randn(2, 33, 33, device=DEV))
 
 
-def test_host_buffer_api_matches_device_api():
-    A = torch.randn(10, 48, 48)
+@pytest.mark.parametrize("b,n,chunks", [(10, 48, 3), (4096, 32, 0), (7, 100, 64), (5, 33, 1),
+                                         (600, 64, 0), (3, 256, 2)])
+def test_host_buffer_api_matches_device_api(b, n, chunks):
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(b * 1000 + n))
     Ah = A.pin_memory()
     Hh = torch.empty_like(Ah).pin_memory()
-    th = torch.empty(10, 48).pin_memory()
-    api.geqrf_host(Ah, Hh, th, device=DEV, chunks=3)
+    th = torch.empty(b, n).pin_memory()
+    api.geqrf_host(Ah, Hh, th, device=DEV, chunks=chunks)
+    torch.cuda.synchronize()
+    H, tau = _gpu_qr(A)
+    assert torch.equal(Hh, H) and torch.equal(th, tau)
+
+
+@pytest.mark.parametrize("b,n", [(4096, 32), (9, 17), (1, 1), (3, 32)])
+def test_host_direct_path_is_taken_and_matches(b, n):
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(b + n))
+    H, tau = _gpu_qr(A)
+    Ah = A.pin_memory()
+    mode0 = _lib.get_config("host_direct")
+    for mode, blocks, ramp in ((1, 0, 1), (1, 1, 1), (1, 3, 1), (2, 0, 1), (3, 0, 0), (3, 0, 1),
+                               (0, 0, 0), (0, 0, 1)):
+        _lib.set_config("host_direct", mode)
+        _lib.set_config("direct_blocks", blocks)
+        _lib.set_config("host_ramp", ramp)
+        try:
+            Hh = torch.full_like(Ah, float("nan")).pin_memory()
+            th = torch.full((b, n), float("nan")).pin_memory()
+            api.geqrf_host(Ah, Hh, th, device=DEV, chunks=3)
+            torch.cuda.synchronize()
+            assert _lib.get_config("host_path") == mode
+            assert torch.equal(Hh, H) and torch.equal(th, tau)
+        finally:
+            _lib.set_config("host_direct", mode0)
+            _lib.set_config("direct_blocks", 0)
+            _lib.set_config("host_ramp", 0)
+    # in place, on mapped memory
+    M = A.clone().pin_memory()
+    th = torch.empty(b, n).pin_memory()
+    api.geqrf_host(M, M, th, device=DEV)
+    torch.cuda.synchronize()
+    assert _lib.get_config("host_path") == mode0
+    assert torch.equal(M, H) and torch.equal(th, tau)
+
+
+def test_host_direct_path_not_taken_for_pageable_buffers():
+    A = torch.randn(8, 32, 32)
+    H, tau = _gpu_qr(A)
+    mode0 = _lib.get_config("host_direct")
+    try:
+        for mode in (1, 2, 3):
+            _lib.set_config("host_direct", mode)
+            # pageable H: H is copied; the pinned tau is still written directly
+            Hh = torch.empty_like(A)
+            th = torch.empty(8, 32).pin_memory()
+            api.geqrf_host(A.pin_memory(), Hh, th, device=DEV)
+            torch.cuda.synchronize()
+            assert _lib.get_config("host_path") == 3
+            assert torch.equal(Hh, H) and torch.equal(th, tau)
+            # everything pageable: copies only
+            Hh = torch.empty_like(A)
+            th = torch.empty(8, 32)
+            api.geqrf_host(A, Hh, th, device=DEV)
+            torch.cuda.synchronize()
+            assert _lib.get_config("host_path") == 0
+            assert torch.equal(Hh, H) and torch.equal(th, tau)
+    finally:
+        _lib.set_config("host_direct", mode0)
+
+
+def test_host_buffer_api_in_place_pageable_and_caller_workspace():
+    A = torch.randn(9, 40, 40, generator=torch.Generator().manual_seed(5))
+    H, tau = _gpu_qr(A)
+    M = A.clone()  # pageable, factored in place
+    th = torch.empty(9, 40)
+    ws = torch.empty(api.host_workspace_bytes(9, 40), dtype=torch.uint8, device=DEV)
+    api.geqrf_host(M, M, th, device=DEV, chunks=4, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(M, H) and torch.equal(th, tau)
+    with pytest.raises(ValueError):
+        api.geqrf_host(M, M, th, device=DEV, workspace=ws[:100])
+
+
+def test_host_buffer_api_injected_failure_enqueues_nothing():
+    A = torch.randn(4, 64, 64).pin_memory()
+    Hh = torch.full_like(A, 7.0).pin_memory()
+    th = torch.full((4, 64), 7.0).pin_memory()
+    _lib.set_config("fail_next", 1)
+    with pytest.raises(_lib.QRBError):
+        api.geqrf_host(A, Hh, th, device=DEV)
+    torch.cuda.synchronize()
+    assert bool((Hh == 7.0).all()) and bool((th == 7.0).all())
+    api.geqrf_host(A, Hh, th, device=DEV)
     torch.cuda.synchronize()
     H, tau = _gpu_qr(A)
     assert torch.equal(Hh, H) and torch.equal(th, tau)
