@@ -472,7 +472,7 @@ def run_ours(args, info) -> int:
                 "frac": ach / peaks["hbm_gbs"],
                 "traffic": traffic,
                 "peak_source": peaks["source"],
-                "kernel": "k_fused_pair (one launch per step)" if cfg.n <= 32 else "whole step",
+                "kernel": "k_fused (one launch per step)" if cfg.n <= 32 else "whole step",
                 "algorithmic_bytes_per_launch": alg_bytes,
             },
             "cpu_baseline": cpu,

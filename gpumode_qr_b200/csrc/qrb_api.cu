@@ -18,6 +18,7 @@ std::atomic<int64_t> g_groups{2};
 std::atomic<int64_t> g_host_direct{3};
 std::atomic<int64_t> g_direct_blocks{0};
 std::atomic<int64_t> g_host_ramp{0};
+std::atomic<int64_t> g_fused_cpl{0};
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -128,6 +129,7 @@ namespace qrb {
 bool take_injected_failure_any() { return take_injected_failure(); }
 int host_direct_mode() { return (int)g_host_direct.load(); }
 bool host_ramp() { return g_host_ramp.load() != 0; }
+int fused_cpl() { return (int)g_fused_cpl.load(); }
 int64_t host_direct_blocks() {
   const int64_t b = g_direct_blocks.load();
   return b > 0 ? b : kHostDirectBlocks;
@@ -294,6 +296,11 @@ int qrb_set_config(const char* key, int64_t value) {
     g_host_direct.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "fused_cpl") == 0) {
+    if (value != 0 && value != 2 && value != 4) return QRB_ERR_INVALID_ARG;
+    g_fused_cpl.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "host_ramp") == 0) {
     if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
     g_host_ramp.store(value);
@@ -327,6 +334,7 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "groups") == 0) { *value = g_groups.load(); return QRB_OK; }
   if (std::strcmp(key, "host_direct") == 0) { *value = g_host_direct.load(); return QRB_OK; }
   if (std::strcmp(key, "host_ramp") == 0) { *value = g_host_ramp.load(); return QRB_OK; }
+  if (std::strcmp(key, "fused_cpl") == 0) { *value = g_fused_cpl.load(); return QRB_OK; }
   if (std::strcmp(key, "direct_blocks") == 0) { *value = qrb::host_direct_blocks(); return QRB_OK; }
   if (std::strcmp(key, "host_path") == 0) { *value = qrb::host_last_path(); return QRB_OK; }
   return QRB_ERR_INVALID_ARG;

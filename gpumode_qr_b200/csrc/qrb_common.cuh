@@ -22,13 +22,22 @@ constexpr int64_t kHostDirectBlocks = 148;  // direct host-memory kernel: blocks
 //   v = x / (alpha - beta); sigma <= 0 -> tau = 0, beta = alpha (identity).
 // Evaluated without divisions by the identities (u = |alpha| + norm > 0)
 //   alpha - beta = sign(alpha) * u,   tau = u / norm = 1 + |alpha| / norm,
-// with 1/norm from the hardware reciprocal square root refined by one Newton
-// step (r <- r (3 - n2 r^2) / 2) and 1/u from the IEEE reciprocal. Both forms
-// are exact in real arithmetic; in FP32 they agree to a few ulp. Outside
+// with 1/norm from the hardware reciprocal square root and 1/u from the
+// hardware reciprocal, each refined by one Newton-Raphson step
+// (r <- r (3 - n2 r^2) / 2 and r <- r + r (1 - u r)). Both forms are exact in
+// real arithmetic; in FP32 they agree to a few ulp. Outside
 // 1e-30 < alpha^2 + sigma < 1e30 the plain IEEE formulas are used.
 struct Reflector {
   float beta, tau, scale;
 };
+
+// 1/x for normal x of moderate size (1e-16 < |x| < 1e16 here): hardware
+// approximation plus one Newton-Raphson step.
+__device__ __forceinline__ float recip_nr(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return fmaf(r, fmaf(-x, r, 1.0f), r);
+}
 
 __device__ __forceinline__ Reflector make_reflector(float alpha, float sigma) {
   Reflector h;
@@ -40,7 +49,7 @@ __device__ __forceinline__ Reflector make_reflector(float alpha, float sigma) {
       float r = rsqrtf(n2);
       r = r * fmaf(-0.5f * n2 * r, r, 1.5f);  // one Newton step on 1/sqrt(n2)
       const float norm = n2 * r;
-      const float ru = __frcp_rn(aa + norm);
+      const float ru = recip_nr(aa + norm);
       h.beta = neg ? norm : -norm;
       h.tau = fmaf(aa, r, 1.0f);
       h.scale = neg ? -ru : ru;
@@ -127,6 +136,10 @@ int host_direct_mode();
 bool host_ramp();
 // qrb_set_config("direct_blocks"): grid of the direct kernel (0 = automatic).
 int64_t host_direct_blocks();
+
+// qrb_set_config("fused_cpl"): columns per lane of the n <= 32 kernel, 2 (two
+// matrices per warp), 4 (four matrices per warp) or 0 (by batch size).
+int fused_cpl();
 
 // Path taken by the last qrb_geqrf_f32_host call (the host_direct mode that
 // ran: 0..3), -1 none yet (qrb_get_config("host_path")).

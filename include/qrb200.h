@@ -138,8 +138,8 @@ QRB_API int qrb_geqrf_f32_host(const float* A_host, float* H_host, float* tau_ho
                                size_t workspace_bytes, int32_t chunks, void* stream);
 
 /*
- * Fused whole-matrix QR for small n (n <= 32): one half-warp factors one
- * matrix in registers (two matrices per warp) with a single launch. Replaces hh_fused_qr / _hh_fused_qr_kernel
+ * Fused whole-matrix QR for small n (n <= 32): 16 (or 8) lanes factor one
+ * matrix in registers, two (or four) matrices per warp, in a single launch. Replaces hh_fused_qr / _hh_fused_qr_kernel
  * (src/qrbench/triton_kernels.py:722-755, :641-720).
  */
 QRB_API int qrb_fused_qr_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
@@ -204,6 +204,8 @@ QRB_API int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row
  *   "host_direct" 0..3 (default 3): how qrb_geqrf_f32_host reaches mapped
  *                 page-locked host buffers for n <= 32 (see there).
  *   "direct_blocks" grid of the mode-1 kernel in blocks of 4 warps (0 = 148).
+ *   "fused_cpl"   n <= 32 kernel: 2 or 4 matrices per warp, 0 (default) = 4 up
+ *                 to 4736 matrices, else 2. Results are identical either way.
  *   "host_ramp"   1: qrb_geqrf_f32_host cuts the batch into pieces of relative
  *                 size 1, 2, .., 2, 1 instead of equal pieces (default 0).
  *   "host_path"   read: the host_direct mode the last qrb_geqrf_f32_host call

@@ -52,6 +52,23 @@ def test_fused_kernel_every_small_n(n):
     assert (tau[:, -1] == 0).all()
 
 
+@pytest.mark.parametrize("n", [1, 5, 8, 9, 16, 17, 31, 32])
+@pytest.mark.parametrize("b", [1, 3, 5, 6, 7, 37, 4736, 4737])
+def test_fused_kernel_two_and_four_matrices_per_warp_agree(n, b):
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(b * 33 + n)).to(DEV)
+    outs = {}
+    try:
+        for cpl in (2, 4, 0):
+            _lib.set_config("fused_cpl", cpl)
+            outs[cpl] = api.hh_fused_qr(A)
+    finally:
+        _lib.set_config("fused_cpl", 0)
+    for cpl in (4, 0):
+        assert torch.equal(outs[cpl][0], outs[2][0]) and torch.equal(outs[cpl][1], outs[2][1])
+    if b <= 37:
+        assert checker.check(A.cpu(), outs[2][0].cpu(), outs[2][1].cpu()).passed
+
+
 def test_panel_kernel_matches_reference_kernel(ref_panel):
     for case in golden_cases(ref_panel):
         P = torch.from_numpy(ref_panel[f"{case}_P"])
