@@ -6,13 +6,14 @@
 // intermediate to global memory:
 //   pass 1  W = V^T C over all r rows: 64-row chunks of V and C double-buffered
 //           into shared memory with cp.async; each warp takes every 8th row
-//           and each lane accumulates an 8 x 8 register block of W (64 FMAs
-//           per four 16-byte shared loads); the eight warp partials are summed
-//           while W <- T^T W is formed;
+//           and each lane accumulates an 8 x 8 register block of W (32 packed
+//           FP32x2 FMAs per four 16-byte shared loads); the eight warp
+//           partials are summed, then W <- T^T W is formed;
 //   pass 2  C -= V W over 256-row chunks: V is staged transposed in shared
-//           memory and each thread updates an 8-row x 8-column block of C in
-//           registers (columns c, c+1, c+2, c+3 and c+32..c+35, so that a
-//           warp's global loads and stores cover whole 128-byte rows).
+//           memory (negated) and each thread updates an 8-row x 8-column block
+//           of C in registers with packed FMAs (columns c, c+1, c+2, c+3 and
+//           c+32..c+35, so that a warp's global loads and stores cover whole
+//           128-byte rows).
 // V is read through its strictly lower part only: the diagonal is taken as 1
 // and everything above it as 0 (so V can point into a packed H), columns at or
 // beyond k as 0.
@@ -100,11 +101,13 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   // ---------------- pass 1: W = V^T C ----------------
   const int wa = (lane >> 3) << 3;  // W rows wa..wa+7
   const int wc = (lane & 7) << 2;   // W cols wc..wc+3 and wc+32..wc+35
-  float acc[8][8];
+  // acc[x][j]: W(wa + x, column pair j) with pairs (wc, wc+1), (wc+2, wc+3),
+  // (wc+32, wc+33), (wc+34, wc+35), updated with the packed FP32x2 FMA.
+  float2 acc[8][4];
 #pragma unroll
   for (int x = 0; x < 8; ++x)
 #pragma unroll
-    for (int y = 0; y < 8; ++y) acc[x][y] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[x][j] = make_float2(0.f, 0.f);
 
   const int nch = (r + RC1 - 1) / RC1;
   auto load_chunk = [&](int ch, int buf) {
@@ -182,11 +185,14 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
       const float4 ca = *reinterpret_cast<const float4*>(cb + rr * CS_LD + wc);
       const float4 cbv = *reinterpret_cast<const float4*>(cb + rr * CS_LD + wc + 32);
       const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      const float cv[8] = {ca.x, ca.y, ca.z, ca.w, cbv.x, cbv.y, cbv.z, cbv.w};
+      const float2 cp[4] = {make_float2(ca.x, ca.y), make_float2(ca.z, ca.w),
+                            make_float2(cbv.x, cbv.y), make_float2(cbv.z, cbv.w)};
 #pragma unroll
-      for (int x = 0; x < 8; ++x)
+      for (int x = 0; x < 8; ++x) {
+        const float2 vx = make_float2(vv[x], vv[x]);
 #pragma unroll
-        for (int y = 0; y < 8; ++y) acc[x][y] = fmaf(vv[x], cv[y], acc[x][y]);
+        for (int j = 0; j < 4; ++j) acc[x][j] = __ffma2_rn(vx, cp[j], acc[x][j]);
+      }
     }
     __syncthreads();
   }
@@ -195,27 +201,44 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
 #pragma unroll
   for (int x = 0; x < 8; ++x) {
     float* row = &sm.u.Wp[warp][(wa + x) * TC];
-    *reinterpret_cast<float4*>(row + wc) = make_float4(acc[x][0], acc[x][1], acc[x][2], acc[x][3]);
+    *reinterpret_cast<float4*>(row + wc) =
+        make_float4(acc[x][0].x, acc[x][0].y, acc[x][1].x, acc[x][1].y);
     *reinterpret_cast<float4*>(row + wc + 32) =
-        make_float4(acc[x][4], acc[x][5], acc[x][6], acc[x][7]);
+        make_float4(acc[x][2].x, acc[x][2].y, acc[x][3].x, acc[x][3].y);
   }
   __syncthreads();
 
   // ---------------- W <- T^T (sum of partials) ----------------
+  // Sum the eight warp partials (8 consecutive W entries per thread, 16-byte
+  // loads), into Ws; then each thread forms 8 rows of one column of T^T W.
+  {
+    const int e0 = tid * 8;  // W entries e0..e0+7 (row e0 / TC)
+    float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+#pragma unroll
+    for (int w2 = 0; w2 < NW; ++w2) {
+      const float4 p0 = *reinterpret_cast<const float4*>(&sm.u.Wp[w2][e0]);
+      const float4 p1 = *reinterpret_cast<const float4*>(&sm.u.Wp[w2][e0 + 4]);
+      s0.x += p0.x; s0.y += p0.y; s0.z += p0.z; s0.w += p0.w;
+      s1.x += p1.x; s1.y += p1.y; s1.z += p1.z; s1.w += p1.w;
+    }
+    float* ws = &sm.Ws[(e0 / TC) * WS_LD + (e0 % TC)];
+    *reinterpret_cast<float4*>(ws) = s0;
+    *reinterpret_cast<float4*>(ws + 4) = s1;
+  }
+  __syncthreads();
   {
     const int cc = tid & 63;
     const int ab = (tid >> 6) << 3;
     float o[8];
 #pragma unroll
     for (int x = 0; x < 8; ++x) o[x] = 0.f;
-#pragma unroll 2
+#pragma unroll 4
     for (int q = 0; q < K; ++q) {
-      float wq = 0.f;
-#pragma unroll
-      for (int w2 = 0; w2 < NW; ++w2) wq += sm.u.Wp[w2][q * TC + cc];
+      const float wq = sm.Ws[q * WS_LD + cc];
 #pragma unroll
       for (int x = 0; x < 8; ++x) o[x] = fmaf(sm.Ts[q * T_LD + ab + x], wq, o[x]);
     }
+    __syncthreads();  // every thread has read the sums in Ws
 #pragma unroll
     for (int x = 0; x < 8; ++x) sm.Ws[(ab + x) * WS_LD + cc] = o[x];
   }
@@ -244,12 +267,14 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
           t.w = c4 + 3 < k ? __ldg(g + 3) : 0.f;
         }
       }
-      sm.u.Vt[(c4 + 0) * VT_LD + row] = vmask(t.x, i, c4 + 0, k);
-      sm.u.Vt[(c4 + 1) * VT_LD + row] = vmask(t.y, i, c4 + 1, k);
-      sm.u.Vt[(c4 + 2) * VT_LD + row] = vmask(t.z, i, c4 + 2, k);
-      sm.u.Vt[(c4 + 3) * VT_LD + row] = vmask(t.w, i, c4 + 3, k);
+      // stored negated: the update below is then a plain FMA
+      sm.u.Vt[(c4 + 0) * VT_LD + row] = -vmask(t.x, i, c4 + 0, k);
+      sm.u.Vt[(c4 + 1) * VT_LD + row] = -vmask(t.y, i, c4 + 1, k);
+      sm.u.Vt[(c4 + 2) * VT_LD + row] = -vmask(t.z, i, c4 + 2, k);
+      sm.u.Vt[(c4 + 3) * VT_LD + row] = -vmask(t.w, i, c4 + 3, k);
     }
-    float cv[8][8];
+    // cv[x][j]: C(i0 + rg + x, column pair j), pairs as for pass 1
+    float2 cv[8][4];
 #pragma unroll
     for (int x = 0; x < 8; ++x) {
       const int i = i0 + rg + x;
@@ -258,14 +283,17 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
         float4 ta = make_float4(0.f, 0.f, 0.f, 0.f), tb = ta;
         if (i < r && colA < c) ta = *reinterpret_cast<const float4*>(g + colA);
         if (i < r && colB < c) tb = *reinterpret_cast<const float4*>(g + colB);
-        cv[x][0] = ta.x; cv[x][1] = ta.y; cv[x][2] = ta.z; cv[x][3] = ta.w;
-        cv[x][4] = tb.x; cv[x][5] = tb.y; cv[x][6] = tb.z; cv[x][7] = tb.w;
+        cv[x][0] = make_float2(ta.x, ta.y); cv[x][1] = make_float2(ta.z, ta.w);
+        cv[x][2] = make_float2(tb.x, tb.y); cv[x][3] = make_float2(tb.z, tb.w);
       } else {
+        float t8[8];
 #pragma unroll
         for (int y = 0; y < 4; ++y) {
-          cv[x][y] = (i < r && colA + y < c) ? g[colA + y] : 0.f;
-          cv[x][4 + y] = (i < r && colB + y < c) ? g[colB + y] : 0.f;
+          t8[y] = (i < r && colA + y < c) ? g[colA + y] : 0.f;
+          t8[4 + y] = (i < r && colB + y < c) ? g[colB + y] : 0.f;
         }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) cv[x][j] = make_float2(t8[2 * j], t8[2 * j + 1]);
       }
     }
     __syncthreads();
@@ -275,12 +303,15 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
       const float4 wB = *reinterpret_cast<const float4*>(&sm.Ws[a * WS_LD + cq + 32]);
       const float4 v0 = *reinterpret_cast<const float4*>(&sm.u.Vt[a * VT_LD + rg]);
       const float4 v1 = *reinterpret_cast<const float4*>(&sm.u.Vt[a * VT_LD + rg + 4]);
-      const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      const float ww[8] = {wA.x, wA.y, wA.z, wA.w, wB.x, wB.y, wB.z, wB.w};
+      const float nv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      const float2 wp[4] = {make_float2(wA.x, wA.y), make_float2(wA.z, wA.w),
+                            make_float2(wB.x, wB.y), make_float2(wB.z, wB.w)};
 #pragma unroll
-      for (int x = 0; x < 8; ++x)
+      for (int x = 0; x < 8; ++x) {
+        const float2 vx = make_float2(nv[x], nv[x]);
 #pragma unroll
-        for (int y = 0; y < 8; ++y) cv[x][y] = fmaf(-vv[x], ww[y], cv[x][y]);
+        for (int j = 0; j < 4; ++j) cv[x][j] = __ffma2_rn(vx, wp[j], cv[x][j]);
+      }
     }
 #pragma unroll
     for (int x = 0; x < 8; ++x) {
@@ -289,14 +320,18 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
       float* g = Dm + (int64_t)i * ldcd;
       if (VEC) {
         if (colA < c)
-          *reinterpret_cast<float4*>(g + colA) = make_float4(cv[x][0], cv[x][1], cv[x][2], cv[x][3]);
+          *reinterpret_cast<float4*>(g + colA) =
+              make_float4(cv[x][0].x, cv[x][0].y, cv[x][1].x, cv[x][1].y);
         if (colB < c)
-          *reinterpret_cast<float4*>(g + colB) = make_float4(cv[x][4], cv[x][5], cv[x][6], cv[x][7]);
+          *reinterpret_cast<float4*>(g + colB) =
+              make_float4(cv[x][2].x, cv[x][2].y, cv[x][3].x, cv[x][3].y);
       } else {
+        const float t8[8] = {cv[x][0].x, cv[x][0].y, cv[x][1].x, cv[x][1].y,
+                             cv[x][2].x, cv[x][2].y, cv[x][3].x, cv[x][3].y};
 #pragma unroll
         for (int y = 0; y < 4; ++y) {
-          if (colA + y < c) g[colA + y] = cv[x][y];
-          if (colB + y < c) g[colB + y] = cv[x][4 + y];
+          if (colA + y < c) g[colA + y] = t8[y];
+          if (colB + y < c) g[colB + y] = t8[4 + y];
         }
       }
     }
