@@ -14,7 +14,7 @@ std::atomic<int64_t> g_fail_next{0};
 std::atomic<int64_t> g_sync_check{0};
 std::atomic<int64_t> g_larfb_kind{0};  // 0 = FFMA, 1 = tcgen05 3xTF32
 std::atomic<int64_t> g_launches{0};
-std::atomic<int64_t> g_groups{2};
+std::atomic<int64_t> g_groups{0};  // 0 = automatic
 std::atomic<int64_t> g_host_direct{3};
 std::atomic<int64_t> g_direct_blocks{0};
 std::atomic<int64_t> g_host_ramp{0};
@@ -142,7 +142,12 @@ int finish_call(int rc, cudaStream_t stream) { return finish(rc, stream); }
 int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
                   float* T, int64_t batch, int n, cudaStream_t s) {
   if (n <= kFusedMaxN) return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
-  const int groups = (int)(batch >= 4 ? g_groups.load() : 1);
+  // Automatic: 4 groups from n = 1024 on (measured on B200: 30.6 vs 32.8 ms for
+  // 8 x 4096^2), else 2; at most half the batch.
+  int groups = (int)g_groups.load();
+  if (groups == 0) groups = n >= 1024 ? 4 : 2;
+  if (groups > batch / 2) groups = (int)(batch / 2);
+  if (batch < 4) groups = 1;
   if (groups <= 1) return blocked_qr(A, strideA_b, strideA_row, H, tau, T, batch, n, s);
   // Split the batch into groups that run the same kernel sequence on separate
   // internal streams, forked from and joined back into the caller's stream, so
@@ -287,7 +292,7 @@ int qrb_set_config(const char* key, int64_t value) {
     return qrb::device_error_flag(&v, true);
   }
   if (std::strcmp(key, "groups") == 0) {
-    if (value < 1 || value > kMaxGroups) return QRB_ERR_INVALID_ARG;
+    if (value < 0 || value > kMaxGroups) return QRB_ERR_INVALID_ARG;
     g_groups.store(value);
     return QRB_OK;
   }

@@ -197,10 +197,11 @@ QRB_API int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row
  *   "device_error" read: 1 if a kernel's bounded device-side wait timed out
  *                 since the last reset (synchronous); set to 0 to reset.
  *   "groups"      1..4: batches of 4 or more matrices with n > 32 are split
- *                 into this many groups run on internal streams (forked from
- *                 and joined back into the caller's stream) so that panel
- *                 and trailing-update kernels of different groups overlap
- *                 (default 2).
+ *                 into this many groups (at most batch / 2) run on internal
+ *                 streams (forked from and joined back into the caller's
+ *                 stream) so that panel and trailing-update kernels of
+ *                 different groups overlap; 0 (default) = 4 for n >= 1024,
+ *                 else 2.
  *   "host_direct" 0..3 (default 3): how qrb_geqrf_f32_host reaches mapped
  *                 page-locked host buffers for n <= 32 (see there).
  *   "direct_blocks" grid of the mode-1 kernel in blocks of 4 warps (0 = 148).

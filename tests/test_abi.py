@@ -149,6 +149,12 @@ def test_config_keys():
     _lib.set_config("host_ramp", 1)
     assert _lib.get_config("host_ramp") == 1
     _lib.set_config("host_ramp", 0)
+    assert _lib.get_config("groups") == 0
+    _lib.set_config("groups", 3)
+    assert _lib.get_config("groups") == 3
+    _lib.set_config("groups", 0)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("groups", 5)
     assert _lib.get_config("fused_cpl") == 0
     _lib.set_config("fused_cpl", 4)
     assert _lib.get_config("fused_cpl") == 4

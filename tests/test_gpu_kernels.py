@@ -152,13 +152,14 @@ def test_launch_counter_counts_kernels():
     torch.cuda.synchronize()
     groups = _lib.get_config("groups")
     try:
-        for g in (1, 2):
+        # (setting, groups used): 0 = automatic (2 below n = 1024); at most batch / 2
+        for g, used in ((1, 1), (2, 2), (0, 2), (4, 2)):
             _lib.set_config("groups", g)
             _lib.set_config("launches", 0)
             H, tau = api.geqrf(A)
             torch.cuda.synchronize()
             # per batch group: 3 panels + 2 trailing updates
-            assert _lib.get_config("launches") == 5 * g
+            assert _lib.get_config("launches") == 5 * used
             assert checker.check(A, H, tau).passed
     finally:
         _lib.set_config("groups", groups)
