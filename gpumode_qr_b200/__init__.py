@@ -14,6 +14,9 @@ __all__ = [
     "hh_fused_qr",
     "hh_panel_qr",
     "larfb",
+    "householder_product",
+    "ormqr",
+    "geqrf_host",
     "VARIANTS",
     "VARIANT_INFO",
     "CHAMPION",
@@ -26,7 +29,8 @@ from .variants import CHAMPION, VARIANT_INFO, VARIANTS  # noqa: E402
 
 
 def __getattr__(name):  # lazy: keep `import gpumode_qr_b200` torch-free
-    if name in ("geqrf", "impl", "hh_fused_qr", "hh_panel_qr", "larfb"):
+    if name in ("geqrf", "impl", "hh_fused_qr", "hh_panel_qr", "larfb", "householder_product",
+                "ormqr", "geqrf_host"):
         from . import api
 
         return getattr(api, name)

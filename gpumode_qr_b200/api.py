@@ -245,6 +245,69 @@ def hh_panel_qr(panel: torch.Tensor, num_warps: int | None = None, num_stages: i
     return H, V, tau, T
 
 
+def _reflectors(H: torch.Tensor, tau: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda_f32("H", H)
+    _require_cuda_f32("tau", tau)
+    if H.dim() != 3 or H.shape[1] != H.shape[2]:
+        raise ValueError(f"H must be (B, n, n), got {tuple(H.shape)}")
+    b, n, _ = H.shape
+    if tau.dim() != 2 or tau.shape[0] != b or tau.shape[1] > n:
+        raise ValueError(f"tau must be (B, k) with k <= n, got {tuple(tau.shape)}")
+    if tau.device != H.device:
+        raise ValueError("H and tau must be on the same device")
+    return _as_rowmajor_batch(H, n, n), tau.contiguous()
+
+
+def householder_product(H: torch.Tensor, tau: torch.Tensor) -> torch.Tensor:
+    """Q = H_0 H_1 ... H_{k-1} from a factorization, as
+    ``torch.linalg.householder_product(H, tau)`` for square ``H [B,n,n]`` and
+    ``tau [B,k]`` (k <= n); the reference's checker forms Q this way
+    (src/qrbench/checker.py:129). One call of ``qrb_orgqr_f32``."""
+    H3, t = _reflectors(H, tau)
+    b, n, _ = H3.shape
+    k = t.shape[1]
+    Q = torch.empty((b, n, n), dtype=torch.float32, device=H.device)
+    if Q.numel() == 0:
+        return Q
+    L = _lib.lib()
+    ws_n = int(L.qrb_orgqr_workspace_bytes(b, n))
+    ws = torch.empty(max(ws_n, 16), dtype=torch.uint8, device=H.device)
+    with torch.cuda.device(H.device):
+        rc = L.qrb_orgqr_f32(H3.data_ptr(), H3.stride(0), H3.stride(1), t.data_ptr(), k,
+                             Q.data_ptr(), b, n, ws.data_ptr(), ws_n, _stream(H.device))
+    _lib.check(rc)
+    return Q
+
+
+def ormqr(H: torch.Tensor, tau: torch.Tensor, C: torch.Tensor, left: bool = True,
+          transpose: bool = False) -> torch.Tensor:
+    """``Q C`` (or ``Q^T C`` with ``transpose``) as ``torch.ormqr(H, tau, C,
+    left=True, transpose=...)`` for square ``H [B,n,n]``, ``tau [B,k]`` and
+    ``C [B,n,m]``; returns a new tensor. Only ``left=True`` is supported.
+    One call of ``qrb_ormqr_f32`` (src/qrbench/variants.py:165 is the
+    reference's use of torch.ormqr)."""
+    if not left:
+        raise NotImplementedError("ormqr: only left=True (Q applied from the left) is supported")
+    H3, t = _reflectors(H, tau)
+    _require_cuda_f32("C", C)
+    b, n, _ = H3.shape
+    if C.dim() != 3 or C.shape[0] != b or C.shape[1] != n:
+        raise ValueError(f"C must be (B, n, m) = ({b}, {n}, m), got {tuple(C.shape)}")
+    out = C.contiguous().clone()
+    if out.numel() == 0 or t.shape[1] == 0:
+        return out
+    L = _lib.lib()
+    ws_n = int(L.qrb_orgqr_workspace_bytes(b, n))
+    ws = torch.empty(max(ws_n, 16), dtype=torch.uint8, device=H.device)
+    m = out.shape[2]
+    with torch.cuda.device(H.device):
+        rc = L.qrb_ormqr_f32(H3.data_ptr(), H3.stride(0), H3.stride(1), t.data_ptr(), t.shape[1],
+                             out.data_ptr(), out.stride(0), out.stride(1), b, n, m,
+                             1 if transpose else 0, ws.data_ptr(), ws_n, _stream(H.device))
+    _lib.check(rc)
+    return out
+
+
 def larfb(V: torch.Tensor, T: torch.Tensor, C: torch.Tensor) -> torch.Tensor:
     """In-place ``C -= V (T^T (V^T C))`` for ``V [B,r,k]``, ``T [B,k,k]``, ``C [B,r,c]``.
 

@@ -1,0 +1,224 @@
+// Consumers of a factorization (H, tau): forming Q (householder_product /
+// sorgqr) and applying Q or Q^T to a matrix from the left (ormqr), the step the
+// reference's checker takes next (src/qrbench/checker.py:129 forms Q with
+// torch.linalg.householder_product; src/qrbench/variants.py:165 applies it
+// with torch.ormqr).
+//
+// Both run block by block over the 32-column reflector blocks of H:
+//   k_larft  T of one block from its packed reflectors and tau: the Gram
+//            matrix V^T V accumulated over the block's rows through shared
+//            memory (thread (g, a) sums row a of the Gram over rows g, g + 8,
+//            ... of each staged 64-row chunk), then the forward recurrence
+//            T[i][i] = tau_i, T[0:i][i] = -tau_i T[0:i][0:i] (V^T V)[0:i][i]
+//            (the reference panel kernel's, triton_kernels.py:886-909) by one
+//            warp, lane = row of T. It can write T transposed.
+//   larfb    the trailing-update kernel of the factorization, which applies
+//            C <- C - V X^T V^T C for the X it is given: X = T applies the
+//            block's H^T = I - V T^T V^T, X = T^T applies H = I - V T V^T.
+// Q = H_0 H_1 ... H_{k-1}: start from the identity and apply the blocks in
+// reverse order to Q[j0:, j0:] (columns left of j0 are still unit vectors that
+// a block starting at row j0 does not touch). Q^T C applies the blocks in
+// order with T, Q C in reverse order with T^T.
+#include "qrb_common.cuh"
+
+namespace qrb {
+
+namespace {
+
+constexpr int W = kPanelW;
+constexpr int NT = 256;
+constexpr int NG = NT / W;   // row groups (8)
+constexpr int RCH = 64;      // rows per staged chunk
+
+// One CTA per matrix. H points at the block's top-left element (row j0,
+// column j0) of matrix 0; the block has r rows and k <= 32 reflectors. T is
+// written as a zero-padded 32 x 32 block per matrix.
+__global__ void __launch_bounds__(NT)
+k_larft(const float* __restrict__ H, int64_t sb, int64_t ld, const float* __restrict__ tau,
+        int64_t tau_sb, int r, int k, float* __restrict__ T_out, int64_t T_sb, int transpose) {
+  __shared__ __align__(16) float Vs[RCH][W];
+  __shared__ float Gp[NG][W][W + 1];  // per-row-group partial Gram, [group][a][b]
+  __shared__ float taus[W];
+  const int tid = threadIdx.x;
+  const int a = tid & (W - 1);
+  const int g = tid >> 5;
+  const int64_t m = blockIdx.x;
+  const float* __restrict__ Hm = H + m * sb;
+  if (tid < W) taus[tid] = tid < k ? __ldg(tau + m * tau_sb + tid) : 0.f;
+
+  float acc[W];
+#pragma unroll
+  for (int b = 0; b < W; ++b) acc[b] = 0.f;
+  for (int i0 = 0; i0 < r; i0 += RCH) {
+    __syncthreads();  // the previous chunk has been consumed
+#pragma unroll
+    for (int e = 0; e < (RCH * W) / NT; ++e) {  // a warp loads one 128-byte row
+      const int idx = tid + e * NT;
+      const int row = idx / W, col = idx % W;
+      const int i = i0 + row;
+      float v = 0.f;
+      if (i < r && col < k)
+        v = i > col ? __ldg(Hm + (int64_t)i * ld + col) : (i == col ? 1.f : 0.f);
+      Vs[row][col] = v;
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int row = g; row < RCH; row += NG) {
+      const float xa = Vs[row][a];
+#pragma unroll
+      for (int b4 = 0; b4 < W / 4; ++b4) {
+        const float4 xb = reinterpret_cast<const float4*>(Vs[row])[b4];
+        acc[4 * b4 + 0] = fmaf(xa, xb.x, acc[4 * b4 + 0]);
+        acc[4 * b4 + 1] = fmaf(xa, xb.y, acc[4 * b4 + 1]);
+        acc[4 * b4 + 2] = fmaf(xa, xb.z, acc[4 * b4 + 2]);
+        acc[4 * b4 + 3] = fmaf(xa, xb.w, acc[4 * b4 + 3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < W; ++b) Gp[g][a][b] = acc[b];
+  __syncthreads();
+  // Sum the eight partials into Gp[0]; every entry is summed by one thread.
+  for (int e = tid; e < W * W; e += NT) {
+    const int q = e / W, i = e % W;
+    float s = 0.f;
+#pragma unroll
+    for (int gg = 0; gg < NG; ++gg) s += Gp[gg][q][i];
+    Gp[0][q][i] = s;
+  }
+  __syncthreads();
+  if (g == 0) {
+    const int row = a;
+    float trow[W];
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      float t = 0.f;
+#pragma unroll
+      for (int q = 0; q < i; ++q) t = fmaf(trow[q], Gp[0][q][i], t);
+      trow[i] = row < i ? -taus[i] * t : (row == i ? taus[i] : 0.f);
+    }
+    float* Tm = T_out + m * T_sb;
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      const float v = (row < k && i < k) ? trow[i] : 0.f;
+      if (transpose)
+        Tm[(int64_t)i * W + row] = v;
+      else
+        Tm[(int64_t)row * W + i] = v;
+    }
+  }
+}
+
+// Q <- I for batch contiguous n x n matrices.
+__global__ void k_identity(float* __restrict__ Q, int64_t total, int n) {
+  const int64_t nn = (int64_t)n * n;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t w = e % nn;
+    Q[e] = (w / n == w % n) ? 1.f : 0.f;
+  }
+}
+
+int launch_larft(const float* H, int64_t sb, int64_t ld, const float* tau, int64_t tau_sb,
+                 int64_t batch, int r, int k, float* T, int transpose, cudaStream_t s) {
+  if (batch > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
+  k_larft<<<(unsigned)batch, NT, 0, s>>>(H, sb, ld, tau, tau_sb, r, k, T, (int64_t)W * W,
+                                         transpose);
+  note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
+}
+
+// Apply the reflector blocks of (H, tau) (k reflectors, H n x ? with row
+// stride sHr) to C (n x c, strides sCb / sCr) from the left: Q^T when
+// transpose, else Q. Blocks whose columns start at or beyond `first_col` of C
+// are applied only to C's columns from their own start on (orgqr's triangle).
+int apply_blocks(const float* H, int64_t sHb, int64_t sHr, const float* tau, int64_t tau_sb,
+                 float* C, int64_t sCb, int64_t sCr, int64_t batch, int n, int k, int c,
+                 bool transpose, bool triangle, float* T, cudaStream_t s) {
+  const int nblk = (k + W - 1) / W;
+  for (int q = 0; q < nblk; ++q) {
+    const int blk = transpose ? q : nblk - 1 - q;
+    const int j0 = blk * W;
+    const int w = k - j0 < W ? k - j0 : W;
+    const int r = n - j0;
+    const float* Vb = H + (int64_t)j0 * sHr + j0;
+    int rc = launch_larft(Vb, sHb, sHr, tau + j0, tau_sb, batch, r, w, T, transpose ? 0 : 1, s);
+    if (rc != QRB_OK) return rc;
+    const int c0 = triangle ? j0 : 0;
+    float* Cb = C + (int64_t)j0 * sCr + c0;
+    rc = launch_larfb(Vb, sHb, sHr, T, (int64_t)W * W, W, Cb, sCb, sCr, Cb, sCb, sCr, batch, r, w,
+                      c - c0, 64, s);
+    if (rc != QRB_OK) return rc;
+  }
+  return QRB_OK;
+}
+
+bool bad_strides(int64_t sb, int64_t srow, int64_t rows, int64_t cols, int64_t batch) {
+  if (srow < cols) return true;
+  if (batch > 1 && sb < (rows - 1) * srow + cols) return true;
+  return false;
+}
+
+}  // namespace
+
+}  // namespace qrb
+
+extern "C" {
+
+size_t qrb_orgqr_workspace_bytes(int64_t batch, int32_t n) {
+  if (batch <= 0 || n <= 0) return 0;
+  return (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float);
+}
+
+int qrb_orgqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row, const float* tau,
+                  int32_t k, float* Q, int64_t batch, int32_t n, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (batch < 0 || n < 0 || k < 0) return QRB_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0) return QRB_OK;
+  if (!H || !tau || !Q) return QRB_ERR_INVALID_ARG;
+  if (k > n) return QRB_ERR_INVALID_ARG;
+  if (n > qrb::kMaxN) return QRB_ERR_UNSUPPORTED;
+  if (qrb::bad_strides(strideH_b, strideH_row, n, k > 0 ? k : 1, batch)) return QRB_ERR_INVALID_ARG;
+  if (k > 0) {
+    if (workspace == nullptr || workspace_bytes < qrb_orgqr_workspace_bytes(batch, n))
+      return QRB_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
+  }
+  if (qrb::take_injected_failure_any()) return QRB_ERR_INJECTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t total = batch * (int64_t)n * n;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  qrb::k_identity<<<(unsigned)blocks, 256, 0, s>>>(Q, total, n);
+  qrb::note_launches(1);
+  int rc = cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
+  if (rc == QRB_OK && k > 0)
+    rc = qrb::apply_blocks(H, strideH_b, strideH_row, tau, k, Q, (int64_t)n * n, n, batch, n, k,
+                           n, /*transpose=*/false, /*triangle=*/true,
+                           static_cast<float*>(workspace), s);
+  return qrb::finish_call(rc, s);
+}
+
+int qrb_ormqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row, const float* tau,
+                  int32_t k, float* C, int64_t strideC_b, int64_t strideC_row, int64_t batch,
+                  int32_t n, int32_t ncols, int32_t transpose, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (batch < 0 || n < 0 || k < 0 || ncols < 0) return QRB_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0 || ncols == 0 || k == 0) return QRB_OK;
+  if (!H || !tau || !C) return QRB_ERR_INVALID_ARG;
+  if (k > n) return QRB_ERR_INVALID_ARG;
+  if (n > qrb::kMaxN) return QRB_ERR_UNSUPPORTED;
+  if (qrb::bad_strides(strideH_b, strideH_row, n, k, batch)) return QRB_ERR_INVALID_ARG;
+  if (qrb::bad_strides(strideC_b, strideC_row, n, ncols, batch)) return QRB_ERR_INVALID_ARG;
+  if (workspace == nullptr || workspace_bytes < qrb_orgqr_workspace_bytes(batch, n))
+    return QRB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
+  if (qrb::take_injected_failure_any()) return QRB_ERR_INJECTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rc = qrb::apply_blocks(H, strideH_b, strideH_row, tau, k, C, strideC_b, strideC_row,
+                                   batch, n, k, ncols, transpose != 0, /*triangle=*/false,
+                                   static_cast<float*>(workspace), s);
+  return qrb::finish_call(rc, s);
+}
+
+}  // extern "C"

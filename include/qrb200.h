@@ -184,6 +184,31 @@ QRB_API int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row
                   int32_t c, void* stream);
 
 /*
+ * Consumers of a factorization: form Q, or apply Q / Q^T to a matrix. H and
+ * tau are as qrb_geqrf_f32 writes them; the first k columns of H hold the
+ * reflectors (strictly lower part, unit diagonal implied) and tau is
+ * batch x k contiguous (k <= n). Both need qrb_orgqr_workspace_bytes(batch, n)
+ * bytes of 16-byte aligned device scratch (one 32 x 32 T factor per matrix).
+ *
+ * qrb_orgqr_f32: Q (batch x n x n contiguous, must not overlap H) =
+ * H_0 H_1 ... H_{k-1}. Replaces torch.linalg.householder_product(H, tau) as
+ * the reference's checker calls it (src/qrbench/checker.py:129).
+ *
+ * qrb_ormqr_f32: C (batch x n x ncols, strides (strideC_b, strideC_row)) is
+ * overwritten with Q^T C (transpose != 0) or Q C (transpose == 0). Replaces
+ * torch.ormqr(H, tau, C, left=True, transpose=...) (src/qrbench/variants.py:165).
+ */
+QRB_API size_t qrb_orgqr_workspace_bytes(int64_t batch, int32_t n);
+QRB_API int qrb_orgqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row,
+                          const float* tau, int32_t k, float* Q, int64_t batch, int32_t n,
+                          void* workspace, size_t workspace_bytes, void* stream);
+QRB_API int qrb_ormqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row,
+                          const float* tau, int32_t k, float* C, int64_t strideC_b,
+                          int64_t strideC_row, int64_t batch, int32_t n, int32_t ncols,
+                          int32_t transpose, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/*
  * Tuning and test hooks (never needed for correct use). Keys:
  *   "fail_next"   value v > 0: the next v calls of any compute entry point
  *                 return QRB_ERR_INJECTED without enqueuing work (host-side

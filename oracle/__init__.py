@@ -62,7 +62,9 @@ def _load():
         lib.oracle_panel.argtypes = [i64, i32, i32, fp, fp, fp, fp, fp, i32]
         lib.oracle_larfb.argtypes = [i64, i32, i32, i32, fp, fp, fp, i32]
         lib.oracle_blocked_geqrf.argtypes = [i64, i32, fp, i64, i64, fp, fp, i32, i32]
-        for f in ("oracle_geqr2", "oracle_panel", "oracle_larfb", "oracle_blocked_geqrf"):
+        lib.oracle_larft.argtypes = [i64, i32, i32, fp, i64, i64, fp, i64, fp, i32]
+        for f in ("oracle_geqr2", "oracle_panel", "oracle_larfb", "oracle_blocked_geqrf",
+                  "oracle_larft"):
             getattr(lib, f).restype = None
         _lib = lib
     return _lib
@@ -112,6 +114,17 @@ def larfb(V, T, C, f64: bool = True) -> np.ndarray:
     return c
 
 
+def larft(H, tau, f64: bool = True) -> np.ndarray:
+    """T ``[b,k,k]`` of the packed reflector block ``H [b,r,k]`` (strictly lower
+    part, unit diagonal) with coefficients ``tau [b,k]``."""
+    h = _f32(H)
+    t = _f32(tau)
+    b, r, k = h.shape
+    T = np.empty((b, k, k), np.float32)
+    _load().oracle_larft(b, r, k, _ptr(h), r * k, k, _ptr(t), k, _ptr(T), int(f64))
+    return T
+
+
 def blocked_geqrf(A, w: int = 32, f64: bool = True):
     """Blocked Householder QR with panel width ``w`` -> (H, tau)."""
     a = _f32(A)
@@ -129,6 +142,22 @@ def lapack_geqrf(A):
     t = torch.as_tensor(_f32(A))
     H, tau = torch.geqrf(t)
     return H.numpy(), tau.numpy()
+
+
+def lapack_householder_product(H, tau):
+    """Q from (H, tau) with CPU ``torch.linalg.householder_product`` (LAPACK
+    sorgqr), as the reference's checker forms it (src/qrbench/checker.py:129)."""
+    import torch
+
+    return torch.linalg.householder_product(torch.as_tensor(_f32(H)), torch.as_tensor(_f32(tau))).numpy()
+
+
+def lapack_ormqr(H, tau, C, transpose: bool = False):
+    """Q C (or Q^T C) with CPU ``torch.ormqr`` (LAPACK sormqr), left side."""
+    import torch
+
+    return torch.ormqr(torch.as_tensor(_f32(H)), torch.as_tensor(_f32(tau)), torch.as_tensor(_f32(C)),
+                       left=True, transpose=transpose).numpy()
 
 
 def lapack_provenance() -> dict:

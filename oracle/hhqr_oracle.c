@@ -26,6 +26,8 @@
  *     (src/qrbench/variants.py:800-804): C -= V (T^T (V^T C)).
  *   - oracle_blocked_geqrf: the blocked driver (variants.py:761-805) built
  *     from the three pieces above.
+ *   - oracle_larft: the LARFT recurrence alone, from a packed (H, tau) block
+ *     (the T factor an apply-Q / form-Q step needs).
  * Every routine takes `f64`: 0 computes in float (the reference's FP32
  * arithmetic, sequential sums), 1 computes in double and rounds the outputs to
  * float (a high-accuracy answer for parity checks).
@@ -234,6 +236,41 @@ ORACLE_API void oracle_larfb(int64_t batch, int r, int k, int c, const float* V,
       free(cd);
     } else {
       larfb_f(r, k, c, v, t, cm);
+    }
+  }
+}
+
+/* Forward LARFT from a packed block: V is the strictly lower part of the
+ * r x k block at H (unit diagonal implied, zero above), tau its k
+ * coefficients; T is k x k row-major. Follows the reference panel kernel's
+ * recurrence (src/qrbench/triton_kernels.py:886-909). */
+ORACLE_API void oracle_larft(int64_t batch, int r, int k, const float* H, int64_t sb, int64_t ld,
+                             const float* tau, int64_t tau_sb, float* T, int f64) {
+#pragma omp parallel for schedule(dynamic)
+  for (int64_t m = 0; m < batch; ++m) {
+    const float* h = H + m * sb;
+    const float* tm = tau + m * tau_sb;
+    float* tt = T + m * (int64_t)k * k;
+    if (f64) {
+      double* vd = (double*)malloc(sizeof(double) * (size_t)r * k);
+      double* td = (double*)malloc(sizeof(double) * (size_t)k);
+      double* out = (double*)malloc(sizeof(double) * (size_t)k * k);
+      for (int i = 0; i < r; ++i)
+        for (int j = 0; j < k; ++j)
+          vd[(int64_t)i * k + j] = i > j ? h[(int64_t)i * ld + j] : (i == j ? 1.0 : 0.0);
+      for (int j = 0; j < k; ++j) td[j] = tm[j];
+      larft_d(r, k, vd, td, out);
+      for (int64_t e = 0; e < (int64_t)k * k; ++e) tt[e] = (float)out[e];
+      free(vd);
+      free(td);
+      free(out);
+    } else {
+      float* vf = (float*)malloc(sizeof(float) * (size_t)r * k);
+      for (int i = 0; i < r; ++i)
+        for (int j = 0; j < k; ++j)
+          vf[(int64_t)i * k + j] = i > j ? h[(int64_t)i * ld + j] : (i == j ? 1.f : 0.f);
+      larft_f(r, k, vf, tm, tt);
+      free(vf);
     }
   }
 }

@@ -25,7 +25,9 @@ def declared_symbols() -> list[str]:
 def test_header_declares_the_expected_entry_points():
     assert set(declared_symbols()) == {
         "qrb_version", "qrb_status_string", "qrb_max_n", "qrb_workspace_bytes", "qrb_geqrf_f32",
-        "qrb_geqrf_f32_noalloc", "qrb_host_workspace_bytes", "qrb_geqrf_f32_host", "qrb_fused_qr_f32", "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32",
+        "qrb_geqrf_f32_noalloc", "qrb_host_workspace_bytes", "qrb_geqrf_f32_host", "qrb_fused_qr_f32",
+        "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32", "qrb_orgqr_workspace_bytes",
+        "qrb_orgqr_f32", "qrb_ormqr_f32",
         "qrb_set_config", "qrb_get_config",
     }
 
@@ -83,6 +85,29 @@ def test_host_entry_workspace_and_validation_without_gpu():
     assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, ws, need - 1, 0, None) == 3
     assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, ctypes.c_void_p(0x100010), need, 0,
                                 None) == 1
+
+
+def test_orgqr_ormqr_validation_without_gpu():
+    L = _lib.lib()
+    assert L.qrb_orgqr_workspace_bytes(8, 64) == 8 * 32 * 32 * 4
+    assert L.qrb_orgqr_workspace_bytes(8, 16) == 8 * 32 * 32 * 4
+    assert L.qrb_orgqr_workspace_bytes(0, 16) == 0
+    ws = ctypes.c_void_p(0x100000)
+    need = L.qrb_orgqr_workspace_bytes(2, 64)
+    # empty problems
+    assert L.qrb_orgqr_f32(None, 0, 0, None, 0, None, 0, 64, None, 0, None) == 0
+    assert L.qrb_ormqr_f32(None, 0, 0, None, 0, None, 0, 0, 2, 64, 0, 1, None, 0, None) == 0
+    # bad arguments: k > n, null pointers, overlapping rows, short workspace, too large
+    assert L.qrb_orgqr_f32(FAKE, 4096, 64, FAKE, 65, FAKE, 2, 64, ws, need, None) == 1
+    assert L.qrb_orgqr_f32(None, 4096, 64, FAKE, 64, FAKE, 2, 64, ws, need, None) == 1
+    assert L.qrb_orgqr_f32(FAKE, 4096, 32, FAKE, 64, FAKE, 2, 64, ws, need, None) == 1
+    assert L.qrb_orgqr_f32(FAKE, 4096, 64, FAKE, 64, FAKE, 2, 64, ws, need - 1, None) == 3
+    assert L.qrb_orgqr_f32(FAKE, 8193 * 8193, 8193, FAKE, 8193, FAKE, 1, 8193, ws, 1 << 30,
+                           None) == 2
+    assert L.qrb_ormqr_f32(FAKE, 4096, 64, FAKE, 64, FAKE, 640, 9, 2, 64, 10, 1, ws, need,
+                           None) == 1
+    assert L.qrb_ormqr_f32(FAKE, 4096, 64, FAKE, 64, FAKE, 640, 10, 2, 64, 10, 1, None, 0,
+                           None) == 3
 
 
 def test_argument_validation_without_gpu():
