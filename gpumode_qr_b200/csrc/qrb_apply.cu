@@ -128,10 +128,10 @@ int launch_larft(const float* H, int64_t sb, int64_t ld, const float* tau, int64
   return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
 }
 
-// Apply the reflector blocks of (H, tau) (k reflectors, H n x ? with row
-// stride sHr) to C (n x c, strides sCb / sCr) from the left: Q^T when
-// transpose, else Q. Blocks whose columns start at or beyond `first_col` of C
-// are applied only to C's columns from their own start on (orgqr's triangle).
+// Apply the reflector blocks of (H, tau) (k reflectors in the first k
+// columns of the n-row H, row stride sHr) to C (n x c, strides sCb / sCr) from
+// the left: Q^T when transpose, else Q. With triangle, the block starting at
+// column j0 is applied to C's columns j0.. only (forming Q from the identity).
 int apply_blocks(const float* H, int64_t sHb, int64_t sHr, const float* tau, int64_t tau_sb,
                  float* C, int64_t sCb, int64_t sCr, int64_t batch, int n, int k, int c,
                  bool transpose, bool triangle, float* T, cudaStream_t s) {
@@ -175,7 +175,7 @@ int qrb_orgqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row, const 
                   size_t workspace_bytes, void* stream) {
   if (batch < 0 || n < 0 || k < 0) return QRB_ERR_INVALID_ARG;
   if (batch == 0 || n == 0) return QRB_OK;
-  if (!H || !tau || !Q) return QRB_ERR_INVALID_ARG;
+  if (!H || !Q || (k > 0 && !tau)) return QRB_ERR_INVALID_ARG;  // k = 0: tau may be empty
   if (k > n) return QRB_ERR_INVALID_ARG;
   if (n > qrb::kMaxN) return QRB_ERR_UNSUPPORTED;
   if (qrb::bad_strides(strideH_b, strideH_row, n, k > 0 ? k : 1, batch)) return QRB_ERR_INVALID_ARG;
