@@ -338,6 +338,58 @@ def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
     return res
 
 
+def pcie_probe(A_host, H_host, A_dev, H_dev, dev, reps: int = 10) -> dict:
+    """Copy-engine bandwidth of this box for the e2e step's buffers: one
+    host-to-device copy, one device-to-host copy, and both at once on two
+    streams (GB/s, median of ``reps``). Outside every timed region."""
+    import torch
+
+    s1 = torch.cuda.Stream(device=dev)
+    s2 = torch.cuda.Stream(device=dev)
+
+    def timed(fn):
+        out = []
+        for _ in range(reps + 2):
+            cur = torch.cuda.current_stream(dev)
+            a = torch.cuda.Event(enable_timing=True)
+            z = torch.cuda.Event(enable_timing=True)
+            a.record(cur)
+            fn(cur)
+            z.record(cur)
+            torch.cuda.synchronize(dev)
+            out.append(a.elapsed_time(z))
+        return statistics.median(out[2:])
+
+    def h2d(cur):
+        s1.wait_stream(cur)
+        with torch.cuda.stream(s1):
+            A_dev.copy_(A_host, non_blocking=True)
+        cur.wait_stream(s1)
+
+    def d2h(cur):
+        s2.wait_stream(cur)
+        with torch.cuda.stream(s2):
+            H_host.copy_(H_dev, non_blocking=True)
+        cur.wait_stream(s2)
+
+    nb = A_host.numel() * 4
+    t_h, t_d = timed(h2d), timed(d2h)
+
+    def both(cur):  # both directions in flight together
+        s1.wait_stream(cur)
+        s2.wait_stream(cur)
+        with torch.cuda.stream(s1):
+            A_dev.copy_(A_host, non_blocking=True)
+        with torch.cuda.stream(s2):
+            H_host.copy_(H_dev, non_blocking=True)
+        cur.wait_stream(s1)
+        cur.wait_stream(s2)
+
+    t_b = timed(both)
+    return {"h2d_gbs": nb / t_h / 1e6, "d2h_gbs": nb / t_d / 1e6, "both_gbs": 2 * nb / t_b / 1e6,
+            "method": "pinned cudaMemcpyAsync of the step's A / H buffers, median of %d" % reps}
+
+
 def run_ours(args, info) -> int:
     import torch
 
@@ -428,6 +480,9 @@ def run_ours(args, info) -> int:
     e2e_value = b * world * e2e_steps / (e2e_ms / 1e3)
     h2d = A_host.numel() * 4
     d2h = H_host.numel() * 4 + tau_host.numel() * 4
+    pcie = pcie_probe(A_host, H_host, A, H, dev)
+    pcie["bound_ms"] = max(h2d / (pcie["h2d_gbs"] * 1e6), d2h / (pcie["d2h_gbs"] * 1e6))
+    pcie["e2e_frac"] = pcie["bound_ms"] / (e2e_ms / e2e_steps)
 
     peaks = measured_peaks()
     extra = {}
@@ -479,7 +534,8 @@ def run_ours(args, info) -> int:
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "api": "qrb_geqrf_f32_host via gpumode_qr_b200.api.geqrf_host (pinned host in/out)",
-                    "chunks": args.chunks},
+                    "chunks": args.chunks,
+                    "pcie": pcie},
             "gpu_launches": launches_total,
             "clocks": clk.summary(),
             "gates": {"factor": gate.factor_residual, "orth": gate.orth_residual,
