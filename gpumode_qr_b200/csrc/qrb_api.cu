@@ -19,6 +19,7 @@ std::atomic<int64_t> g_host_direct{3};
 std::atomic<int64_t> g_direct_blocks{0};
 std::atomic<int64_t> g_host_ramp{0};
 std::atomic<int64_t> g_fused_cpl{0};
+std::atomic<int64_t> g_mid_fused{1};
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -130,6 +131,7 @@ bool take_injected_failure_any() { return take_injected_failure(); }
 int host_direct_mode() { return (int)g_host_direct.load(); }
 bool host_ramp() { return g_host_ramp.load() != 0; }
 int fused_cpl() { return (int)g_fused_cpl.load(); }
+bool mid_fused_enabled() { return g_mid_fused.load() != 0; }
 int64_t host_direct_blocks() {
   const int64_t b = g_direct_blocks.load();
   return b > 0 ? b : kHostDirectBlocks;
@@ -142,6 +144,12 @@ int finish_call(int rc, cudaStream_t stream) { return finish(rc, stream); }
 int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
                   float* T, int64_t batch, int n, cudaStream_t s) {
   if (n <= kFusedMaxN) return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
+  // The CTA-per-matrix kernel is latency-friendly (one launch) but does about
+  // twice the blocked route's arithmetic: measured on B200 it wins at n <= 64
+  // for every batch (2x) and above n = 64 while the batch fits about two waves
+  // (1.2-1.4x at 8-200 matrices), and loses at 1024 x 96 (436 vs 271 us).
+  if (n <= kFusedMidMaxN && mid_fused_enabled() && (n <= 64 || batch <= kFusedMidMaxBatch))
+    return launch_fused_mid(A, strideA_b, strideA_row, H, tau, batch, n, s);
   // Automatic: 4 groups from n = 1024 on (measured on B200: 30.6 vs 32.8 ms for
   // 8 x 4096^2), else 2; at most half the batch.
   int groups = (int)g_groups.load();
@@ -301,6 +309,11 @@ int qrb_set_config(const char* key, int64_t value) {
     g_host_direct.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "mid_fused") == 0) {
+    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    g_mid_fused.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "fused_cpl") == 0) {
     if (value != 0 && value != 2 && value != 4) return QRB_ERR_INVALID_ARG;
     g_fused_cpl.store(value);
@@ -340,6 +353,7 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "host_direct") == 0) { *value = g_host_direct.load(); return QRB_OK; }
   if (std::strcmp(key, "host_ramp") == 0) { *value = g_host_ramp.load(); return QRB_OK; }
   if (std::strcmp(key, "fused_cpl") == 0) { *value = g_fused_cpl.load(); return QRB_OK; }
+  if (std::strcmp(key, "mid_fused") == 0) { *value = g_mid_fused.load(); return QRB_OK; }
   if (std::strcmp(key, "direct_blocks") == 0) { *value = qrb::host_direct_blocks(); return QRB_OK; }
   if (std::strcmp(key, "host_path") == 0) { *value = qrb::host_last_path(); return QRB_OK; }
   return QRB_ERR_INVALID_ARG;

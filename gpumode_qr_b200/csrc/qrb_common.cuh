@@ -11,6 +11,8 @@ namespace qrb {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kPanelW = 32;        // panel / block-reflector width
 constexpr int kFusedMaxN = 32;     // largest n of the warp-per-matrix kernel
+constexpr int kFusedMidMaxN = 128; // largest n of the CTA-per-matrix fused kernel
+constexpr int64_t kFusedMidMaxBatch = 592;  // above n = 64: about two waves of 2 CTAs per SM
 constexpr int kMaxN = 8192;        // 4096 rows per CTA-cluster of 8 x 512 x 2
 constexpr int kMaxCluster = 8;
 constexpr int64_t kHostDirectBlocks = 148;  // direct host-memory kernel: blocks of 4 warps
@@ -79,6 +81,14 @@ enum class HostMem { kNone, kTau, kOutputs /* H and tau */, kAll /* A, H and tau
 int launch_fused_small(const float* A, int64_t sAb, int64_t sAr, float* H,
                        float* tau, int64_t batch, int n, cudaStream_t stream,
                        HostMem where = HostMem::kNone, int64_t max_blocks = 0);
+
+// CTA-per-matrix fused QR for kFusedMaxN < n <= kFusedMidMaxN (one launch).
+int launch_fused_mid(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau,
+                     int64_t batch, int n, cudaStream_t stream);
+// qrb_set_config("mid_fused"): 1 (default) = 32 < n <= 64, and 64 < n <= 128
+// up to kFusedMidMaxBatch matrices, run the CTA-per-matrix fused kernel;
+// 0 = always the blocked panel route.
+bool mid_fused_enabled();
 
 // Factor the r x w panel starting at (row 0, col 0) of src (row stride ld_src,
 // matrix stride sb_src) into dst; tau to tau_out[m*tau_sb + c]; T to

@@ -70,7 +70,9 @@ QRB_API size_t qrb_workspace_bytes(int64_t batch, int32_t n);
  *   impl(A: [b, n, n] fp32) -> (H, tau)
  * (src/qrbench/reference.py:15 QRImpl; src/qrbench/variants.py:876-917
  * make_hh_panel_tuned(...).impl, the CHAMPION at variants.py:106), including
- * its dispatch between the fused small-n kernel and the blocked panel route.
+ * its dispatch between fused whole-matrix kernels (n <= 32: lanes of a warp
+ * per matrix; 32 < n <= 128: one CTA per matrix, see "mid_fused") and the
+ * blocked panel route.
  *
  *   A      input, batch x n x n, strides (strideA_b, strideA_row), read only.
  *   H      output, batch x n x n contiguous (stride n*n, row stride n).
@@ -230,6 +232,9 @@ QRB_API int qrb_ormqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row
  *   "host_direct" 0..3 (default 3): how qrb_geqrf_f32_host reaches mapped
  *                 page-locked host buffers for n <= 32 (see there).
  *   "direct_blocks" grid of the mode-1 kernel in blocks of 4 warps (0 = 148).
+ *   "mid_fused"   1 (default): 32 < n <= 64, and 64 < n <= 128 up to 592
+ *                 matrices, are factored by one CTA per matrix in one launch;
+ *                 0: always the blocked panel route above n = 32.
  *   "fused_cpl"   n <= 32 kernel: 2 or 4 matrices per warp, 0 (default) = 4 up
  *                 to 4736 matrices, else 2. Results are identical either way.
  *   "host_ramp"   1: qrb_geqrf_f32_host cuts the batch into pieces of relative

@@ -147,7 +147,16 @@ def test_larfb_strided_views_inside_a_matrix(larfb_kind):
     assert torch.equal(Hd.cpu()[mask], Hm[mask])
 
 
-def test_launch_counter_counts_kernels():
+@pytest.fixture
+def blocked_route():
+    """Run n <= 128 through the blocked panel route instead of the fused CTA kernel."""
+    old = _lib.get_config("mid_fused")
+    _lib.set_config("mid_fused", 0)
+    yield
+    _lib.set_config("mid_fused", old)
+
+
+def test_launch_counter_counts_kernels(blocked_route):
     A = torch.randn(4, 96, 96, device=DEV)
     torch.cuda.synchronize()
     groups = _lib.get_config("groups")
@@ -166,7 +175,7 @@ def test_launch_counter_counts_kernels():
 
 
 @pytest.mark.parametrize("n", [96, 200, 512, 1000])
-def test_geqrf_same_with_ffma_and_tensor_core_updates(n):
+def test_geqrf_same_with_ffma_and_tensor_core_updates(n, blocked_route):
     A = torch.randn(4, n, n, generator=torch.Generator().manual_seed(n)).to(DEV)
     old = _lib.get_config("larfb_kind")
     try:
@@ -181,3 +190,45 @@ def test_geqrf_same_with_ffma_and_tensor_core_updates(n):
     par = checker.parity(out[1][0].cpu(), out[1][1].cpu(), out[0][0].cpu(), out[0][1].cpu())
     assert par.ok(RTOL), par
     assert _lib.get_config("device_error") == 0
+
+
+@pytest.mark.parametrize("n", [33, 40, 47, 63, 64, 65, 80, 96, 100, 127, 128])
+@pytest.mark.parametrize("b", [1, 3, 200, 593])
+def test_fused_cta_kernel_mid_n(n, b):
+    # 32 < n <= 128: one launch of the CTA-per-matrix kernel; parity with the
+    # FP64 oracle, FP64 gates, and agreement with the blocked route.
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(b * 131 + n))
+    Ad = A.to(DEV)
+    _lib.set_config("launches", 0)
+    H, tau = api.geqrf(Ad)
+    torch.cuda.synchronize()
+    fused = n <= 64 or b <= 592  # the dispatch rule for the CTA kernel
+    assert (_lib.get_config("launches") == 1) == fused
+    k = min(b, 16)
+    Ho, to = oracle.geqr2(A[:k].numpy(), f64=True)
+    assert checker.parity(H[:k].cpu(), tau[:k].cpu(), Ho, to).ok(RTOL), n
+    assert checker.check(A[:k], H[:k].cpu(), tau[:k].cpu()).passed
+    assert (tau[:, -1] == 0).all()
+    old = _lib.get_config("mid_fused")
+    try:
+        _lib.set_config("mid_fused", 0)
+        Hb, tb = api.geqrf(Ad)
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_config("mid_fused", old)
+    assert _rel(H, Hb.cpu().numpy()) < RTOL
+    assert (tau - tb).abs().max() < RTOL
+
+
+def test_fused_cta_kernel_in_place_and_strided():
+    n = 72
+    A = torch.randn(6, n, n, generator=torch.Generator().manual_seed(3)).to(DEV)
+    H, tau = api.geqrf(A)
+    big = torch.zeros(6, n, n + 8, device=DEV)
+    big[:, :, :n] = A
+    H2, tau2 = api.geqrf(big[:, :, :n])  # row stride n + 8
+    M = A.clone()
+    t3 = api.geqrf_out(M, M, torch.empty(6, n, device=DEV))[1]
+    torch.cuda.synchronize()
+    assert torch.equal(H, H2) and torch.equal(tau, tau2)
+    assert torch.equal(M, H) and torch.equal(t3, tau)
