@@ -49,6 +49,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip CPU geqrf timings")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget")
+    ap.add_argument("--larfb-kind", type=int, default=None, choices=(0, 1, 2),
+                    help="trailing update: 0 FFMA (default), 1 tcgen05 3xTF32, 2 FFMA + tcgen05")
     ap.add_argument("--chunks", type=int, default=0,
                     help="e2e pipeline depth for qrb_geqrf_f32_host (0 = 4; n <= 32 with pinned buffers runs direct)")
     ap.add_argument("--batch", type=int, default=None,
@@ -273,7 +275,7 @@ def time_device_steps(step, steps: int, warmup: int, flush_buf, stream):
 def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
     import torch
 
-    from gpumode_qr_b200 import api, checker, inputs
+    from gpumode_qr_b200 import _lib, api, checker, inputs
 
     out = {}
     gpu_ms, cpu_ms = [], []
@@ -324,6 +326,18 @@ def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
                 par = checker.parity(H.cpu(), tau.cpu(), Hr, tr)
                 rec["parity_vs_geqrf"] = {"h_rel": par.h_rel, "tau_rel": par.tau_rel,
                                           "col_rel": par.col_rel, "ok": par.ok()}
+        if cfg.n >= 512:
+            # the trailing-update pipe per n: FFMA (default), tcgen05 3xTF32 for
+            # both products, FFMA + tcgen05 for the second (median of 3 each)
+            kinds = {}
+            old_kind = _lib.get_config("larfb_kind")
+            try:
+                for kind, name in ((0, "ffma"), (1, "tcgen05_3xtf32"), (2, "ffma_then_tcgen05")):
+                    _lib.set_config("larfb_kind", kind)
+                    kinds[name] = statistics.median(time_device_steps(fn, 3, 1, flush_buf, stream))
+            finally:
+                _lib.set_config("larfb_kind", old_kind)
+            rec["trailing_update_pipe_ms"] = kinds
         out[cfg.name] = rec
         del A, H, tau, A_cpu
         torch.cuda.empty_cache()
@@ -397,6 +411,8 @@ def run_ours(args, info) -> int:
 
     dev = torch.device("cuda", info.local_rank if info.initialized else 0)
     torch.cuda.set_device(dev)
+    if args.larfb_kind is not None:
+        _lib.set_config("larfb_kind", args.larfb_kind)
     cfg = inputs.config(args.config)
     if args.batch is not None:
         cfg = inputs.Config(cfg.index, args.batch, cfg.n, cfg.kind, cfg.seed, cfg.log10_cond, cfg.parity)

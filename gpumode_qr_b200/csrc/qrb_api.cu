@@ -47,12 +47,13 @@ int finish(int rc, cudaStream_t stream) {
 int larfb_any(const float* V, int64_t sVb, int64_t ldv, const float* T, int64_t sTb, int t_ld,
               const float* Csrc, int64_t sCsb, int64_t ldcs, float* Cdst, int64_t sCdb,
               int64_t ldcd, int64_t batch, int r, int k, int c, cudaStream_t s) {
-  if (g_larfb_kind.load() == 1 &&
+  const int64_t kind = g_larfb_kind.load();
+  if (kind == 1 &&
       qrb::larfb_tc_supported(V, sVb, ldv, Csrc, sCsb, ldcs, Cdst, sCdb, ldcd, k, c))
     return qrb::launch_larfb_tc(V, sVb, ldv, T, sTb, t_ld, Csrc, sCsb, ldcs, Cdst, sCdb, ldcd,
                                 batch, r, c, s);
   return qrb::launch_larfb(V, sVb, ldv, T, sTb, t_ld, Csrc, sCsb, ldcs, Cdst, sCdb, ldcd, batch,
-                           r, k, c, 64, s);
+                           r, k, c, /*tc_pass2=*/kind == 2, s);
 }
 
 bool bad_matrix_strides(int64_t sb, int64_t srow, int64_t rows, int64_t cols,
@@ -290,7 +291,7 @@ int qrb_set_config(const char* key, int64_t value) {
     return QRB_OK;
   }
   if (std::strcmp(key, "larfb_kind") == 0) {
-    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
     g_larfb_kind.store(value);
     return QRB_OK;
   }

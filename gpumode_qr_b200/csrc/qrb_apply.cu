@@ -147,7 +147,7 @@ int apply_blocks(const float* H, int64_t sHb, int64_t sHr, const float* tau, int
     const int c0 = triangle ? j0 : 0;
     float* Cb = C + (int64_t)j0 * sCr + c0;
     rc = launch_larfb(Vb, sHb, sHr, T, (int64_t)W * W, W, Cb, sCb, sCr, Cb, sCb, sCr, batch, r, w,
-                      c - c0, 64, s);
+                      c - c0, /*tc_pass2=*/false, s);
     if (rc != QRB_OK) return rc;
   }
   return QRB_OK;

@@ -103,10 +103,12 @@ int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
 // C_dst <- C_src - V T^T V^T C_src for r x c blocks, k <= 32 reflectors whose
 // strictly-lower part is read from V (unit diagonal implied). T is 32 x 32 per
 // matrix (leading k x k used) when t_ld == 32, else k x k (t_ld = k).
+// tc_pass2: the second product (C -= V W') on the tensor cores (tcgen05,
+// 3xTF32) where the operands allow 16-byte vector access and k == 32.
 int launch_larfb(const float* V, int64_t sVb, int64_t ldv, const float* T,
                  int64_t sTb, int t_ld, const float* Csrc, int64_t sCsb,
                  int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
-                 int64_t batch, int r, int k, int c, int tile_c,
+                 int64_t batch, int r, int k, int c, bool tc_pass2,
                  cudaStream_t stream);
 
 int panel_cluster_size(int r);
@@ -122,8 +124,9 @@ int launch_larfb_tc(const float* V, int64_t sVb, int64_t ldv, const float* T,
                     int64_t batch, int r, int c, cudaStream_t stream);
 
 // Device-side error flag set by kernels whose bounded waits timed out
-// (synchronous read; optionally reset to 0).
+// (synchronous read; optionally reset to 0), and its device address.
 int device_error_flag(int* value, bool reset);
+int device_error_ptr(int** p);
 
 // Whole factorization of already validated arguments, enqueued on `stream`
 // (no fault injection, no sync check); T is the qrb_workspace_bytes scratch.

@@ -18,6 +18,9 @@
 // and everything above it as 0 (so V can point into a packed H), columns at or
 // beyond k as 0.
 #include "qrb_common.cuh"
+#include "qrb_tc.cuh"
+
+#include <type_traits>
 
 namespace qrb {
 
@@ -49,6 +52,28 @@ struct __align__(16) Smem {
   float Ts[K * T_LD];
 };
 
+// Tensor-core pass 2 (TCP2): D (128 rows x 64 columns, TMEM) = V_chunk W' as
+// kind::tf32 MMAs in 3xTF32, both operands K-major without swizzle: A = the
+// V chunk, 16-byte units (k-quad kq, row m) at kq * 2048 + m * 16; B = W'^T,
+// units (kq, column n) at kq * 1024 + n * 16.
+constexpr int R2T = 128;                    // rows per tensor-core chunk (MMA M)
+constexpr int A2T_BYTES = R2T * K * 4;      // 16 KiB per hi / lo part
+constexpr int B2T_BYTES = TC * K * 4;       // 8 KiB per hi / lo part
+constexpr uint32_t IDESC_P2 = tc::idesc(R2T, TC, false, false);
+constexpr uint32_t TM_COLS_P2 = 2 * TC;     // two 64-column accumulators
+struct __align__(1024) SmemTc {
+  union {
+    Stage st;
+    float Wp[NW][K * TC];
+    unsigned char A[2][2][A2T_BYTES];       // [buffer][hi, lo]
+  } u;
+  unsigned char B[2][B2T_BYTES];            // [hi, lo]
+  float Ws[K * WS_LD];
+  float Ts[K * T_LD];
+  uint64_t bar[2];
+  uint32_t tmem;
+};
+
 __device__ __forceinline__ void cp_async16(void* s, const void* g, bool valid) {
   const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
   const int sz = valid ? 16 : 0;
@@ -75,15 +100,126 @@ __device__ __forceinline__ float vmask(float x, int i, int a, int k) {
   return (a >= k || i < a) ? 0.f : (i == a ? 1.f : x);
 }
 
-template <bool VEC>
+// Pass 2 on the tensor cores: W' (in Ws, 32 x 64) becomes the B operand; per
+// 128-row chunk of V (staged, masked, split) one elected thread issues 4
+// k-steps x 3 MMAs into one of two TMEM accumulators and commits them to an
+// mbarrier; the previous chunk's accumulator is read back (warp w: TMEM lanes
+// 32 (w % 4) .., columns 32 (w / 4) ..) and subtracted from C.
+__device__ __forceinline__ void pass2_tc(SmemTc& sm, const float* __restrict__ Vm, int64_t ldv,
+                                         const float* __restrict__ Cm, int64_t ldcs,
+                                         float* __restrict__ Dm, int64_t ldcd, int r, int c,
+                                         int c0, int tid, int warp, int lane,
+                                         int* __restrict__ err) {
+  __syncthreads();  // W' complete in Ws; the pass-1 partials (aliased by A) consumed
+  // B = W'^T, K-major, split
+#pragma unroll
+  for (int e = 0; e < (K / 4) * TC / NT; ++e) {
+    const int u = tid + e * NT;
+    const int kq = u / TC, n = u % TC;
+    const float4 w = make_float4(sm.Ws[(4 * kq + 0) * WS_LD + n], sm.Ws[(4 * kq + 1) * WS_LD + n],
+                                 sm.Ws[(4 * kq + 2) * WS_LD + n], sm.Ws[(4 * kq + 3) * WS_LD + n]);
+    float4 hi, lo;
+    tc::split4(w, hi, lo);
+    *reinterpret_cast<float4*>(sm.B[0] + u * 16) = hi;
+    *reinterpret_cast<float4*>(sm.B[1] + u * 16) = lo;
+  }
+  const uint32_t tmem = sm.tmem;
+  uint32_t ph[2] = {0u, 0u};
+  const uint32_t bar0 = tc::smem_u32(&sm.bar[0]);
+  const int nch = (r + R2T - 1) / R2T;
+
+  auto epilogue = [&](int cp) {
+    const int s = cp & 1;
+    tc::mbar_wait(bar0 + 8 * s, ph[s], err);
+    ph[s] ^= 1u;
+    tc::fence_after();
+    const int q = warp & 3, h = warp >> 2;
+    float d[32];
+    tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + s * TC + 32 * h, d);
+    const int i = cp * R2T + 32 * q + lane;
+    if (i < r) {
+      const float* src = Cm + (int64_t)i * ldcs + c0 + 32 * h;
+      float* dst = Dm + (int64_t)i * ldcd + c0 + 32 * h;
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        if (c0 + 32 * h + 4 * j4 < c) {
+          float4 v = *reinterpret_cast<const float4*>(src + 4 * j4);
+          v.x -= d[4 * j4 + 0];
+          v.y -= d[4 * j4 + 1];
+          v.z -= d[4 * j4 + 2];
+          v.w -= d[4 * j4 + 3];
+          *reinterpret_cast<float4*>(dst + 4 * j4) = v;
+        }
+      }
+    }
+    tc::fence_before();
+  };
+
+  for (int ch = 0; ch < nch; ++ch) {
+    const int s = ch & 1;
+    // A = V rows ch*128 .., masked (unit diagonal, zero above) and split. The
+    // buffer was last read by the MMAs of chunk ch - 2, which the epilogue of
+    // the previous iteration waited for.
+    const int i0 = ch * R2T;
+#pragma unroll
+    for (int e = 0; e < (R2T * K / 4) / NT; ++e) {
+      const int u = tid + e * NT;
+      const int row = u & (R2T - 1), kq = u >> 7;
+      const int i = i0 + row;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < r) v = __ldg(reinterpret_cast<const float4*>(Vm + (int64_t)i * ldv + 4 * kq));
+      v.x = tc::vmask(v.x, i, 4 * kq + 0);
+      v.y = tc::vmask(v.y, i, 4 * kq + 1);
+      v.z = tc::vmask(v.z, i, 4 * kq + 2);
+      v.w = tc::vmask(v.w, i, 4 * kq + 3);
+      float4 hi, lo;
+      tc::split4(v, hi, lo);
+      *reinterpret_cast<float4*>(sm.u.A[s][0] + u * 16) = hi;
+      *reinterpret_cast<float4*>(sm.u.A[s][1] + u * 16) = lo;
+    }
+    tc::fence_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after();
+      const uint32_t a_hi = tc::smem_u32(sm.u.A[s][0]), a_lo = tc::smem_u32(sm.u.A[s][1]);
+      const uint32_t b_hi = tc::smem_u32(sm.B[0]), b_lo = tc::smem_u32(sm.B[1]);
+      const uint32_t dacc = tmem + s * TC;
+#pragma unroll
+      for (int ks = 0; ks < K / 8; ++ks) {
+        const uint64_t ah = tc::sdesc(a_hi + ks * 4096, 2048, 128);
+        const uint64_t al = tc::sdesc(a_lo + ks * 4096, 2048, 128);
+        const uint64_t bh = tc::sdesc(b_hi + ks * 2048, 1024, 128);
+        const uint64_t bl = tc::sdesc(b_lo + ks * 2048, 1024, 128);
+        tc::mma_tf32(dacc, ah, bh, IDESC_P2, ks != 0 ? 1u : 0u);
+        tc::mma_tf32(dacc, ah, bl, IDESC_P2, 1u);
+        tc::mma_tf32(dacc, al, bh, IDESC_P2, 1u);
+      }
+      tc::mma_commit(bar0 + 8 * s);
+    }
+    if (ch >= 1) epilogue(ch - 1);
+  }
+  epilogue(nch - 1);
+  __syncthreads();
+  tc::fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TM_COLS_P2)
+                 : "memory");
+}
+
+// TCP2 (with VEC): pass 2 on the tensor cores (tcgen05, 3xTF32) instead of
+// FFMA; err receives a bounded mbarrier wait's timeout.
+template <bool VEC, bool TCP2>
 __global__ void __launch_bounds__(NT, 2)
 k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
         const float* __restrict__ T, int64_t sTb, int t_ld,
         const float* __restrict__ Csrc, int64_t sCsb, int64_t ldcs,
         float* __restrict__ Cdst, int64_t sCdb, int64_t ldcd, int r, int k,
-        int c) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+        int c, int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  using SM = typename std::conditional<TCP2, SmemTc, Smem>::type;
+  SM& sm = *reinterpret_cast<SM*>(smem_raw);
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -96,6 +232,22 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   for (int e = tid; e < K * K; e += NT) {
     const int i = e / K, a = e % K;
     sm.Ts[i * T_LD + a] = (i < k && a < k) ? __ldg(T + m * sTb + (int64_t)i * t_ld + a) : 0.f;
+  }
+  if constexpr (TCP2) {
+    if (warp == 0) {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       tc::smem_u32(&sm.tmem)),
+                   "r"(TM_COLS_P2)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+      for (int b = 0; b < 2; ++b)
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc::smem_u32(&sm.bar[b])),
+                     "r"(1)
+                     : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
   }
 
   // ---------------- pass 1: W = V^T C ----------------
@@ -243,6 +395,9 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
     for (int x = 0; x < 8; ++x) sm.Ws[(ab + x) * WS_LD + cc] = o[x];
   }
 
+  if constexpr (TCP2) {
+    pass2_tc(sm, Vm, ldv, Cm, ldcs, Dm, ldcd, r, c, c0, tid, warp, lane, err);
+  } else {
   // ---------------- pass 2: C -= V W ----------------
   const int rg = (tid >> 3) << 3;   // chunk rows rg..rg+7
   const int cq = (tid & 7) << 2;    // tile cols cq..cq+3 and cq+32..cq+35
@@ -336,26 +491,29 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
       }
     }
   }
+  }  // FFMA pass 2
 }
 
-template <bool VEC>
+template <bool VEC, bool TCP2>
 int launch_larfb_t(const float* V, int64_t sVb, int64_t ldv, const float* T,
                    int64_t sTb, int t_ld, const float* Csrc, int64_t sCsb,
                    int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
                    int64_t batch, int r, int k, int c, cudaStream_t stream) {
   static bool attr_set[64] = {};  // per device ordinal
+  static int* err_ptr[64] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
-  const size_t smem = sizeof(Smem);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(k_larfb<VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;
+  const size_t smem = TCP2 ? sizeof(SmemTc) : sizeof(Smem);
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(k_larfb<VEC, TCP2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return QRB_ERR_LAUNCH;
+    if (TCP2 && device_error_ptr(&err_ptr[dev]) != QRB_OK) return QRB_ERR_DEVICE;
     attr_set[dev] = true;
   }
   const dim3 grid((unsigned)((c + TC - 1) / TC), (unsigned)batch, 1);
-  k_larfb<VEC><<<grid, NT, smem, stream>>>(V, sVb, ldv, T, sTb, t_ld, Csrc, sCsb, ldcs,
-                                           Cdst, sCdb, ldcd, r, k, c);
+  k_larfb<VEC, TCP2><<<grid, NT, smem, stream>>>(V, sVb, ldv, T, sTb, t_ld, Csrc, sCsb, ldcs,
+                                                 Cdst, sCdb, ldcd, r, k, c, err_ptr[dev]);
   note_launches(1);
   return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
 }
@@ -367,9 +525,8 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 int launch_larfb(const float* V, int64_t sVb, int64_t ldv, const float* T,
                  int64_t sTb, int t_ld, const float* Csrc, int64_t sCsb,
                  int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
-                 int64_t batch, int r, int k, int c, int tile_c,
+                 int64_t batch, int r, int k, int c, bool tc_pass2,
                  cudaStream_t stream) {
-  (void)tile_c;
   if (r < 1 || k < 1 || k > K || c < 1) return QRB_ERR_UNSUPPORTED;
   const bool vec = k == K && c % 4 == 0 && ldv % 4 == 0 && sVb % 4 == 0 &&
                    ldcs % 4 == 0 && sCsb % 4 == 0 && ldcd % 4 == 0 &&
@@ -377,10 +534,15 @@ int launch_larfb(const float* V, int64_t sVb, int64_t ldv, const float* T,
   constexpr int64_t kMaxGridY = 65535;
   for (int64_t b0 = 0; b0 < batch; b0 += kMaxGridY) {
     const int64_t nb = batch - b0 < kMaxGridY ? batch - b0 : kMaxGridY;
-    const int rc = vec ? launch_larfb_t<true>(V + b0 * sVb, sVb, ldv, T + b0 * sTb, sTb, t_ld,
+    const int rc = vec && tc_pass2
+                       ? launch_larfb_t<true, true>(V + b0 * sVb, sVb, ldv, T + b0 * sTb, sTb,
+                                                    t_ld, Csrc + b0 * sCsb, sCsb, ldcs,
+                                                    Cdst + b0 * sCdb, sCdb, ldcd, nb, r, k, c,
+                                                    stream)
+                   : vec ? launch_larfb_t<true, false>(V + b0 * sVb, sVb, ldv, T + b0 * sTb, sTb, t_ld,
                                               Csrc + b0 * sCsb, sCsb, ldcs, Cdst + b0 * sCdb,
                                               sCdb, ldcd, nb, r, k, c, stream)
-                       : launch_larfb_t<false>(V + b0 * sVb, sVb, ldv, T + b0 * sTb, sTb, t_ld,
+                       : launch_larfb_t<false, false>(V + b0 * sVb, sVb, ldv, T + b0 * sTb, sTb, t_ld,
                                                Csrc + b0 * sCsb, sCsb, ldcs, Cdst + b0 * sCdb,
                                                sCdb, ldcd, nb, r, k, c, stream);
     if (rc != QRB_OK) return rc;

@@ -219,8 +219,10 @@ QRB_API int qrb_ormqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row
  *                 asynchronous kernel faults as QRB_ERR_LAUNCH and device-side
  *                 wait timeouts as QRB_ERR_DEVICE_WAIT (debug mode).
  *   "larfb_kind"  trailing update: 0 (default) = FP32 FFMA; 1 = tcgen05
- *                 tensor cores in 3xTF32 where it applies (32-reflector
- *                 blocks, 16-byte aligned row-major operands), FFMA elsewhere.
+ *                 tensor cores in 3xTF32 for both products; 2 = FFMA for
+ *                 V^T C and tcgen05 3xTF32 for C -= V W'. Kinds 1 and 2 apply
+ *                 to 32-reflector blocks with 16-byte aligned row-major
+ *                 operands; FFMA elsewhere.
  *   "device_error" read: 1 if a kernel's bounded device-side wait timed out
  *                 since the last reset (synchronous); set to 0 to reset.
  *   "groups"      1..4: batches of 4 or more matrices with n > 32 are split

@@ -157,9 +157,12 @@ def test_config_keys():
     _lib.set_config("sync_check", 0)
     _lib.set_config("launches", 0)
     assert _lib.get_config("launches") == 0
-    assert _lib.get_config("larfb_kind") in (0, 1)
+    assert _lib.get_config("larfb_kind") in (0, 1, 2)
+    _lib.set_config("larfb_kind", 2)
+    assert _lib.get_config("larfb_kind") == 2
+    _lib.set_config("larfb_kind", 0)
     with pytest.raises(_lib.QRBError):
-        _lib.set_config("larfb_kind", 2)
+        _lib.set_config("larfb_kind", 3)
     assert _lib.get_config("host_direct") in (0, 1, 2, 3)
     _lib.set_config("host_direct", 0)
     assert _lib.get_config("host_direct") == 0

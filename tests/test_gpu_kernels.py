@@ -99,7 +99,7 @@ def test_panel_kernel_shapes_and_clusters(r, w):
         assert R[:, w:].abs().max() < 1e-4 * Pd.abs().max()
 
 
-@pytest.fixture(params=[0, 1], ids=["ffma", "tcgen05"])
+@pytest.fixture(params=[0, 1, 2], ids=["ffma", "tcgen05", "ffma_tcgen05"])
 def larfb_kind(request):
     old = _lib.get_config("larfb_kind")
     _lib.set_config("larfb_kind", request.param)
@@ -180,15 +180,17 @@ def test_geqrf_same_with_ffma_and_tensor_core_updates(n, blocked_route):
     old = _lib.get_config("larfb_kind")
     try:
         out = {}
-        for kind in (0, 1):
+        for kind in (0, 1, 2):
             _lib.set_config("larfb_kind", kind)
             out[kind] = api.geqrf(A)
             torch.cuda.synchronize()
             assert checker.check(A, *out[kind]).passed, kind
     finally:
         _lib.set_config("larfb_kind", old)
-    par = checker.parity(out[1][0].cpu(), out[1][1].cpu(), out[0][0].cpu(), out[0][1].cpu())
-    assert par.ok(RTOL), par
+    for kind in (1, 2):
+        par = checker.parity(out[kind][0].cpu(), out[kind][1].cpu(), out[0][0].cpu(),
+                             out[0][1].cpu())
+        assert par.ok(RTOL), (kind, par)
     assert _lib.get_config("device_error") == 0
 
 
