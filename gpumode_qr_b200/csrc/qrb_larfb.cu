@@ -128,22 +128,30 @@ __device__ __forceinline__ void pass2_tc(SmemTc& sm, const float* __restrict__ V
   const uint32_t bar0 = tc::smem_u32(&sm.bar[0]);
   const int nch = (r + R2T - 1) / R2T;
 
+  // The previous chunk's C rows are loaded before waiting for its MMAs, and
+  // the next chunk's V rows while the epilogue runs (register prefetch).
   auto epilogue = [&](int cp) {
     const int s = cp & 1;
+    const int q = warp & 3, h = warp >> 2;
+    const int i = cp * R2T + 32 * q + lane;
+    const bool row_ok = i < r;
+    const float* src = Cm + (int64_t)(row_ok ? i : 0) * ldcs + c0 + 32 * h;
+    float4 cv[8];
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4)
+      cv[j4] = (row_ok && c0 + 32 * h + 4 * j4 < c) ? *reinterpret_cast<const float4*>(src + 4 * j4)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
     tc::mbar_wait(bar0 + 8 * s, ph[s], err);
     ph[s] ^= 1u;
     tc::fence_after();
-    const int q = warp & 3, h = warp >> 2;
     float d[32];
     tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + s * TC + 32 * h, d);
-    const int i = cp * R2T + 32 * q + lane;
-    if (i < r) {
-      const float* src = Cm + (int64_t)i * ldcs + c0 + 32 * h;
+    if (row_ok) {
       float* dst = Dm + (int64_t)i * ldcd + c0 + 32 * h;
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
         if (c0 + 32 * h + 4 * j4 < c) {
-          float4 v = *reinterpret_cast<const float4*>(src + 4 * j4);
+          float4 v = cv[j4];
           v.x -= d[4 * j4 + 0];
           v.y -= d[4 * j4 + 1];
           v.z -= d[4 * j4 + 2];
@@ -155,19 +163,28 @@ __device__ __forceinline__ void pass2_tc(SmemTc& sm, const float* __restrict__ V
     tc::fence_before();
   };
 
+  constexpr int kUnits = (R2T * K / 4) / NT;  // 16-byte V units per thread per chunk
+  float4 vpre[kUnits];
+  auto load_v = [&](int ch) {
+#pragma unroll
+    for (int e = 0; e < kUnits; ++e) {
+      const int u = tid + e * NT;
+      const int i = ch * R2T + (u & (R2T - 1));
+      vpre[e] = i < r ? __ldg(reinterpret_cast<const float4*>(Vm + (int64_t)i * ldv + 4 * (u >> 7)))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  load_v(0);
   for (int ch = 0; ch < nch; ++ch) {
     const int s = ch & 1;
     // A = V rows ch*128 .., masked (unit diagonal, zero above) and split. The
     // buffer was last read by the MMAs of chunk ch - 2, which the epilogue of
     // the previous iteration waited for.
-    const int i0 = ch * R2T;
 #pragma unroll
-    for (int e = 0; e < (R2T * K / 4) / NT; ++e) {
+    for (int e = 0; e < kUnits; ++e) {
       const int u = tid + e * NT;
-      const int row = u & (R2T - 1), kq = u >> 7;
-      const int i = i0 + row;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (i < r) v = __ldg(reinterpret_cast<const float4*>(Vm + (int64_t)i * ldv + 4 * kq));
+      const int i = ch * R2T + (u & (R2T - 1)), kq = u >> 7;
+      float4 v = vpre[e];
       v.x = tc::vmask(v.x, i, 4 * kq + 0);
       v.y = tc::vmask(v.y, i, 4 * kq + 1);
       v.z = tc::vmask(v.z, i, 4 * kq + 2);
@@ -197,6 +214,7 @@ __device__ __forceinline__ void pass2_tc(SmemTc& sm, const float* __restrict__ V
       }
       tc::mma_commit(bar0 + 8 * s);
     }
+    if (ch + 1 < nch) load_v(ch + 1);
     if (ch >= 1) epilogue(ch - 1);
   }
   epilogue(nch - 1);
