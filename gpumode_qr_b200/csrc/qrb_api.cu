@@ -20,6 +20,7 @@ std::atomic<int64_t> g_direct_blocks{0};
 std::atomic<int64_t> g_host_ramp{0};
 std::atomic<int64_t> g_fused_cpl{0};
 std::atomic<int64_t> g_mid_fused{1};
+std::atomic<int64_t> g_lookahead{2};  // 0 off, 1 on, 2 from kLookaheadMinN
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -91,6 +92,59 @@ int blocked_qr(const float* A, int64_t strideA_b, int64_t strideA_row, float* H,
   return QRB_OK;
 }
 
+// The blocked factorization with a look-ahead of one panel, on two streams:
+// sp runs panel j and the update of panel j + 1's 32 columns (part a), sb the
+// update of everything right of them (part b). Panel j + 1 then runs while
+// part b of step j does, instead of after it. Part a of step j waits for part
+// b of step j - 1 (which last touched those columns), part b of step j for
+// panel j. T alternates between T0 and T1 so that panel j + 1 can write its
+// factor while part b of step j still reads panel j's. The update is column by
+// column, so the split changes no result. Both streams end joined into sb.
+int blocked_qr_lookahead(const float* A, int64_t strideA_b, int64_t strideA_row, float* H,
+                         float* tau, float* T0, float* T1, int64_t batch, int n,
+                         cudaStream_t sb, cudaStream_t sp, cudaEvent_t evP, cudaEvent_t evB,
+                         cudaEvent_t joinP) {
+  const int64_t nn = (int64_t)n * n;
+  const int W = qrb::kPanelW;
+  if (cudaEventRecord(evB, sb) != cudaSuccess || cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess)
+    return QRB_ERR_LAUNCH;
+  int rc = QRB_OK;
+  for (int j0 = 0, step = 0; j0 < n && rc == QRB_OK; j0 += W, ++step) {
+    float* T = (step & 1) ? T1 : T0;
+    const int w = n - j0 < W ? n - j0 : W;
+    const int r = n - j0;
+    const float* src = (j0 == 0) ? A : H;
+    const int64_t sbt = (j0 == 0) ? strideA_b : nn;
+    const int64_t ld = (j0 == 0) ? strideA_row : n;
+    float* Hp = H + (int64_t)j0 * n + j0;
+    rc = qrb::launch_panel(src + (int64_t)j0 * ld + j0, sbt, ld, Hp, nn, n, tau + j0, n, T,
+                           (int64_t)W * W, W, nullptr, batch, r, w, sp);
+    if (rc != QRB_OK) break;
+    if (cudaEventRecord(evP, sp) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+    const int c = n - j0 - w;
+    if (c <= 0) break;
+    const int ca = c < W ? c : W, cbw = c - ca;
+    const float* ca_src = src + (int64_t)j0 * ld + j0 + w;
+    // part a on sp, after part b of the previous step
+    if (cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+    rc = larfb_any(Hp, nn, n, T, (int64_t)W * W, W, ca_src, sbt, ld, Hp + w, nn, n, batch, r, w,
+                   ca, sp);
+    if (rc != QRB_OK) break;
+    // part b on sb, after panel j
+    if (cudaStreamWaitEvent(sb, evP, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+    if (cbw > 0) {
+      rc = larfb_any(Hp, nn, n, T, (int64_t)W * W, W, ca_src + ca, sbt, ld, Hp + w + ca, nn, n,
+                     batch, r, w, cbw, sb);
+      if (rc != QRB_OK) break;
+    }
+    if (cudaEventRecord(evB, sb) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+  }
+  // join sp into sb (also after an error)
+  if (cudaEventRecord(joinP, sp) != cudaSuccess || cudaStreamWaitEvent(sb, joinP, 0) != cudaSuccess)
+    if (rc == QRB_OK) rc = QRB_ERR_LAUNCH;
+  return rc;
+}
+
 // Internal streams for batch groups, created once per device and kept for the
 // life of the process (streams and events, no device memory).
 constexpr int kMaxGroups = 4;
@@ -99,6 +153,9 @@ struct SideStreams {
   cudaStream_t s[kMaxGroups] = {};
   cudaEvent_t fork = nullptr;
   cudaEvent_t join[kMaxGroups] = {};
+  // look-ahead: per group a panel stream and its events
+  cudaStream_t sp[kMaxGroups] = {};
+  cudaEvent_t evP[kMaxGroups] = {}, evB[kMaxGroups] = {}, joinP[kMaxGroups] = {};
   bool ok = false;
 };
 constexpr int kMaxDevices = 64;
@@ -111,9 +168,14 @@ SideStreams* side_streams() {
   SideStreams* ss = &g_side[dev];
   std::call_once(g_side_once[dev], [ss] {
     bool ok = cudaEventCreateWithFlags(&ss->fork, cudaEventDisableTiming) == cudaSuccess;
+    const unsigned ef = cudaEventDisableTiming;
     for (int g = 0; g < kMaxGroups && ok; ++g) {
       ok = cudaStreamCreateWithFlags(&ss->s[g], cudaStreamNonBlocking) == cudaSuccess &&
-           cudaEventCreateWithFlags(&ss->join[g], cudaEventDisableTiming) == cudaSuccess;
+           cudaEventCreateWithFlags(&ss->join[g], ef) == cudaSuccess &&
+           cudaStreamCreateWithFlags(&ss->sp[g], cudaStreamNonBlocking) == cudaSuccess &&
+           cudaEventCreateWithFlags(&ss->evP[g], ef) == cudaSuccess &&
+           cudaEventCreateWithFlags(&ss->evB[g], ef) == cudaSuccess &&
+           cudaEventCreateWithFlags(&ss->joinP[g], ef) == cudaSuccess;
     }
     ss->ok = ok;
   });
@@ -143,7 +205,7 @@ int finish_call(int rc, cudaStream_t stream) { return finish(rc, stream); }
 // kernel for n <= 32, the blocked loop (optionally split into batch groups on
 // internal streams) otherwise. T is the caller's workspace (n > 32 only).
 int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
-                  float* T, int64_t batch, int n, cudaStream_t s) {
+                  float* T, float* T2, int64_t batch, int n, cudaStream_t s) {
   if (n <= kFusedMaxN) return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
   // The CTA-per-matrix kernel is latency-friendly (one launch) but does about
   // twice the blocked route's arithmetic: measured on B200 it wins at n <= 64
@@ -157,24 +219,36 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
   if (groups == 0) groups = n >= 1024 ? 4 : 2;
   if (groups > batch / 2) groups = (int)(batch / 2);
   if (batch < 4) groups = 1;
-  if (groups <= 1) return blocked_qr(A, strideA_b, strideA_row, H, tau, T, batch, n, s);
+  // Look-ahead needs the second T buffer (a workspace of 2 factors per matrix).
+  const int64_t la_mode = g_lookahead.load();
+  const bool la = T2 != nullptr && (la_mode == 1 || (la_mode == 2 && n >= kLookaheadMinN));
+  if (groups <= 1 && !la) return blocked_qr(A, strideA_b, strideA_row, H, tau, T, batch, n, s);
+  SideStreams* ss = side_streams();
+  if (ss == nullptr) return QRB_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(ss->mu);
+  if (groups <= 1)
+    return blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, T, T2, batch, n, s, ss->sp[0],
+                                ss->evP[0], ss->evB[0], ss->joinP[0]);
   // Split the batch into groups that run the same kernel sequence on separate
   // internal streams, forked from and joined back into the caller's stream, so
   // that one group's (latency-bound) panel kernels overlap another group's
   // trailing updates.
-  SideStreams* ss = side_streams();
-  if (ss == nullptr) return QRB_ERR_DEVICE;
-  std::lock_guard<std::mutex> lock(ss->mu);
   if (cudaEventRecord(ss->fork, s) != cudaSuccess) return QRB_ERR_LAUNCH;
   const int64_t nn = (int64_t)n * n;
+  const int64_t tper = (int64_t)kPanelW * kPanelW;
   int rc = QRB_OK;
   for (int g = 0; g < groups && rc == QRB_OK; ++g) {
     const int64_t b0 = batch * g / groups, b1 = batch * (g + 1) / groups;
     if (b1 <= b0) continue;
     cudaStream_t gs = ss->s[g];
     if (cudaStreamWaitEvent(gs, ss->fork, 0) != cudaSuccess) return QRB_ERR_LAUNCH;
-    rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
-                    T + b0 * (int64_t)kPanelW * kPanelW, b1 - b0, n, gs);
+    if (la)
+      rc = blocked_qr_lookahead(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn,
+                                tau + b0 * n, T + b0 * tper, T2 + b0 * tper, b1 - b0, n, gs,
+                                ss->sp[g], ss->evP[g], ss->evB[g], ss->joinP[g]);
+    else
+      rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
+                      T + b0 * tper, b1 - b0, n, gs);
     if (cudaEventRecord(ss->join[g], gs) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
     if (cudaStreamWaitEvent(s, ss->join[g], 0) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
   }
@@ -207,8 +281,9 @@ int32_t qrb_fused_max_n(void) { return qrb::kFusedMaxN; }
 
 size_t qrb_workspace_bytes(int64_t batch, int32_t n) {
   if (batch <= 0 || n <= qrb::kFusedMaxN) return 0;
-  // One 32 x 32 compact-WY factor T per matrix.
-  return (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float);
+  // Two 32 x 32 compact-WY factors T per matrix (the second for the panel
+  // look-ahead; one suffices without it).
+  return 2 * (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float);
 }
 
 int qrb_fused_qr_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
@@ -266,15 +341,17 @@ int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
   if (n > qrb::kMaxN) return QRB_ERR_UNSUPPORTED;
   if (bad_matrix_strides(strideA_b, strideA_row, n, n, batch)) return QRB_ERR_INVALID_ARG;
   if (A == H && (strideA_row != n || strideA_b != (int64_t)n * n)) return QRB_ERR_INVALID_ARG;
+  float* T2 = nullptr;
   if (n > qrb::kFusedMaxN) {
-    const size_t need = qrb_workspace_bytes(batch, n);
-    if (workspace == nullptr || workspace_bytes < need) return QRB_ERR_WORKSPACE;
+    const size_t one = qrb_workspace_bytes(batch, n) / 2;  // the minimum: one factor each
+    if (workspace == nullptr || workspace_bytes < one) return QRB_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
+    if (workspace_bytes >= 2 * one) T2 = static_cast<float*>(workspace) + one / sizeof(float);
   }
   if (take_injected_failure()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return finish(qrb::geqrf_enqueue(A, strideA_b, strideA_row, H, tau,
-                                   static_cast<float*>(workspace), batch, n, s),
+                                   static_cast<float*>(workspace), T2, batch, n, s),
                 s);
 }
 
@@ -308,6 +385,11 @@ int qrb_set_config(const char* key, int64_t value) {
   if (std::strcmp(key, "host_direct") == 0) {
     if (value < 0 || value > 3) return QRB_ERR_INVALID_ARG;
     g_host_direct.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "lookahead") == 0) {
+    if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
+    g_lookahead.store(value);
     return QRB_OK;
   }
   if (std::strcmp(key, "mid_fused") == 0) {
@@ -355,6 +437,7 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "host_ramp") == 0) { *value = g_host_ramp.load(); return QRB_OK; }
   if (std::strcmp(key, "fused_cpl") == 0) { *value = g_fused_cpl.load(); return QRB_OK; }
   if (std::strcmp(key, "mid_fused") == 0) { *value = g_mid_fused.load(); return QRB_OK; }
+  if (std::strcmp(key, "lookahead") == 0) { *value = g_lookahead.load(); return QRB_OK; }
   if (std::strcmp(key, "direct_blocks") == 0) { *value = qrb::host_direct_blocks(); return QRB_OK; }
   if (std::strcmp(key, "host_path") == 0) { *value = qrb::host_last_path(); return QRB_OK; }
   return QRB_ERR_INVALID_ARG;

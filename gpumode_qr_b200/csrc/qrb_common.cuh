@@ -13,6 +13,8 @@ constexpr int kPanelW = 32;        // panel / block-reflector width
 constexpr int kFusedMaxN = 32;     // largest n of the warp-per-matrix kernel
 constexpr int kFusedMidMaxN = 128; // largest n of the CTA-per-matrix fused kernel
 constexpr int64_t kFusedMidMaxBatch = 592;  // above n = 64: about two waves of 2 CTAs per SM
+constexpr int kLookaheadMinN = 4096;  // automatic panel look-ahead from this n (measured on B200:
+                                      // 29.7 vs 30.5 ms at 8 x 4096, slower at n = 512 and 1024)
 constexpr int kMaxN = 8192;        // 4096 rows per CTA-cluster of 8 x 512 x 2
 constexpr int kMaxCluster = 8;
 constexpr int64_t kHostDirectBlocks = 148;  // direct host-memory kernel: blocks of 4 warps
@@ -129,9 +131,10 @@ int device_error_flag(int* value, bool reset);
 int device_error_ptr(int** p);
 
 // Whole factorization of already validated arguments, enqueued on `stream`
-// (no fault injection, no sync check); T is the qrb_workspace_bytes scratch.
+// (no fault injection, no sync check); T is one T factor per matrix of the
+// qrb_workspace_bytes scratch, T2 (or nullptr) a second one for the look-ahead.
 int geqrf_enqueue(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau, float* T,
-                  int64_t batch, int n, cudaStream_t stream);
+                  float* T2, int64_t batch, int n, cudaStream_t stream);
 
 // The public entry points' shared epilogue pieces: consume one injected
 // failure (fail_next), and apply the sync_check mode to a call's status.

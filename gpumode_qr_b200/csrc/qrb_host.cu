@@ -224,7 +224,8 @@ int qrb_geqrf_f32_host(const float* A_host, float* H_host, float* tau_host, int6
       }
       rc = where == qrb::HostMem::kTau
                ? qrb::launch_fused_small(Mc, nn, n, Mc, dt + b0 * n, cnt, n, p->comp, where)
-               : qrb::geqrf_enqueue(Mc, nn, n, Mc, tc, T, cnt, n, p->comp);
+               : qrb::geqrf_enqueue(Mc, nn, n, Mc, tc, T, T + batch * qrb::kPanelW * qrb::kPanelW,
+                                    cnt, n, p->comp);
       if (rc != QRB_OK) break;
       if (cudaEventRecord(p->factored[c], p->comp) != cudaSuccess ||
           cudaStreamWaitEvent(p->out, p->factored[c], 0) != cudaSuccess ||

@@ -60,8 +60,10 @@ QRB_API const char* qrb_status_string(int status);
 /* Largest n that qrb_geqrf_f32 accepts. */
 QRB_API int32_t qrb_max_n(void);
 
-/* Bytes of device workspace qrb_geqrf_f32 needs for (batch, n); 0 when the
- * size is handled without scratch memory. */
+/* Bytes of device workspace to give qrb_geqrf_f32 for (batch, n): two 32 x 32
+ * T factors per matrix when n > 32, 0 otherwise. Half of it (one factor per
+ * matrix) is the minimum accepted; the second half enables the panel
+ * look-ahead ("lookahead" below). */
 QRB_API size_t qrb_workspace_bytes(int64_t batch, int32_t n);
 
 /*
@@ -234,6 +236,10 @@ QRB_API int qrb_ormqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row
  *   "host_direct" 0..3 (default 3): how qrb_geqrf_f32_host reaches mapped
  *                 page-locked host buffers for n <= 32 (see there).
  *   "direct_blocks" grid of the mode-1 kernel in blocks of 4 warps (0 = 148).
+ *   "lookahead"   blocked route: 0 = off, 1 = on, 2 (default) = from n = 4096;
+ *                 needs the full qrb_workspace_bytes. Panel j + 1 and the
+ *                 update of its columns run on a second stream while the rest
+ *                 of step j's update runs; results are unchanged.
  *   "mid_fused"   1 (default): 32 < n <= 64, and 64 < n <= 128 up to 592
  *                 matrices, are factored by one CTA per matrix in one launch;
  *                 0: always the blocked panel route above n = 32.

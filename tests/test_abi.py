@@ -58,7 +58,7 @@ def test_status_strings_and_constants():
 def test_workspace_bytes():
     L = _lib.lib()
     assert L.qrb_workspace_bytes(4096, 32) == 0
-    assert L.qrb_workspace_bytes(8, 64) == 8 * 32 * 32 * 4
+    assert L.qrb_workspace_bytes(8, 64) == 2 * 8 * 32 * 32 * 4
     assert L.qrb_workspace_bytes(0, 512) == 0
 
 
@@ -66,7 +66,7 @@ def test_host_entry_workspace_and_validation_without_gpu():
     L = _lib.lib()
     mats, taus = 8 * 64 * 64 * 4, 8 * 64 * 4
     up = lambda x: (x + 255) // 256 * 256
-    assert L.qrb_host_workspace_bytes(8, 64) == up(mats) + up(taus) + 8 * 32 * 32 * 4
+    assert L.qrb_host_workspace_bytes(8, 64) == up(mats) + up(taus) + 2 * 8 * 32 * 32 * 4
     assert L.qrb_host_workspace_bytes(4096, 32) == up(4096 * 32 * 32 * 4) + up(4096 * 32 * 4)
     assert L.qrb_host_workspace_bytes(0, 64) == 0
     assert L.qrb_host_workspace_bytes(4, 8193) == 0
@@ -183,6 +183,12 @@ def test_config_keys():
     _lib.set_config("groups", 0)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("groups", 5)
+    assert _lib.get_config("lookahead") == 2
+    _lib.set_config("lookahead", 1)
+    assert _lib.get_config("lookahead") == 1
+    _lib.set_config("lookahead", 2)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("lookahead", 3)
     assert _lib.get_config("mid_fused") == 1
     _lib.set_config("mid_fused", 0)
     assert _lib.get_config("mid_fused") == 0

@@ -234,3 +234,36 @@ def test_fused_cta_kernel_in_place_and_strided():
     torch.cuda.synchronize()
     assert torch.equal(H, H2) and torch.equal(tau, tau2)
     assert torch.equal(M, H) and torch.equal(t3, tau)
+
+
+@pytest.mark.parametrize("n", [129, 200, 512, 1000, 1100])
+@pytest.mark.parametrize("groups", [1, 2])
+def test_panel_lookahead_gives_identical_results(n, groups):
+    # the look-ahead only reorders independent column updates across two
+    # streams: H and tau must be bit-identical; a one-factor workspace runs
+    # without it.
+    b = 4
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(n + groups)).to(DEV)
+    old = {k: _lib.get_config(k) for k in ("lookahead", "groups")}
+    outs = {}
+    try:
+        _lib.set_config("groups", groups)
+        for la in (0, 1):
+            _lib.set_config("lookahead", la)
+            outs[la] = api.geqrf(A)
+        torch.cuda.synchronize()
+        # minimal workspace: one factor per matrix, look-ahead requested but unavailable
+        ws_one = api.workspace_bytes(b, n) // 2
+        ws = torch.empty(ws_one, dtype=torch.uint8, device=DEV)
+        H = torch.empty_like(A)
+        tau = torch.empty(b, n, device=DEV)
+        rc = _lib.lib().qrb_geqrf_f32(A.data_ptr(), n * n, n, H.data_ptr(), tau.data_ptr(), b, n,
+                                      ws.data_ptr(), ws_one, torch.cuda.current_stream().cuda_stream)
+        _lib.check(rc)
+        torch.cuda.synchronize()
+    finally:
+        for k, v in old.items():
+            _lib.set_config(k, v)
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert torch.equal(H, outs[0][0]) and torch.equal(tau, outs[0][1])
+    assert checker.check(A.cpu(), outs[1][0].cpu(), outs[1][1].cpu()).passed
