@@ -354,3 +354,31 @@ def test_no_device_wait_timed_out():
     # every bounded device-side wait in the kernels completed during this run
     torch.cuda.synchronize()
     assert _lib.get_config("device_error") == 0
+
+
+@pytest.mark.parametrize("b,n", [(4096, 32), (8, 64), (200, 100), (64, 512), (8, 4096)])
+def test_cuda_graph_capture_and_replay(b, n):
+    # The whole call (including the batch-group streams and the panel
+    # look-ahead, which fork from and join back into the capturing stream)
+    # captures into one CUDA graph; replays give the eager results bit for bit.
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(b + n)).to(DEV)
+    H = torch.empty_like(A)
+    tau = torch.empty(b, n, device=DEV)
+    step = api.geqrf_into_fn(A, H, tau)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()  # warm-up outside capture (first-call attribute setup)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for seed in (1, 2):
+        A.copy_(torch.randn(b, n, n, generator=torch.Generator().manual_seed(seed)).to(DEV))
+        g.replay()
+        torch.cuda.synchronize()
+        He, te = api.geqrf(A)
+        torch.cuda.synchronize()
+        assert torch.equal(H, He) and torch.equal(tau, te)
+    del g
