@@ -52,7 +52,7 @@ def parse_args(argv=None):
     ap.add_argument("--larfb-kind", type=int, default=None, choices=(0, 1, 2),
                     help="trailing update: 0 FFMA (default), 1 tcgen05 3xTF32, 2 FFMA + tcgen05")
     ap.add_argument("--chunks", type=int, default=0,
-                    help="e2e pipeline depth for qrb_geqrf_f32_host (0 = 4; n <= 32 with pinned buffers runs direct)")
+                    help="e2e pipeline depth for qrb_geqrf_f32_host (0 = 6 for n <= 64, else 4)")
     ap.add_argument("--batch", type=int, default=None,
                     help="matrices per GPU (default: the config's batch); for small profiling cases")
     ap.add_argument("--quick", action="store_true",
@@ -543,7 +543,8 @@ def run_ours(args, info) -> int:
                 "frac": ach / peaks["hbm_gbs"],
                 "traffic": traffic,
                 "peak_source": peaks["source"],
-                "kernel": "k_fused (one launch per step)" if cfg.n <= 32 else "whole step",
+                "kernel": ("k_fused (one launch per step)" if cfg.n <= 32 else
+                           "k_fused_cta (one launch per step)" if cfg.n <= 64 else "whole step"),
                 "algorithmic_bytes_per_launch": alg_bytes,
             },
             "cpu_baseline": cpu,

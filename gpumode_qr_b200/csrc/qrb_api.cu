@@ -202,8 +202,10 @@ int64_t host_direct_blocks() {
 int finish_call(int rc, cudaStream_t stream) { return finish(rc, stream); }
 
 // The whole factorization of validated arguments, enqueued on s: the fused
-// kernel for n <= 32, the blocked loop (optionally split into batch groups on
-// internal streams) otherwise. T is the caller's workspace (n > 32 only).
+// warp kernel for n <= 32, the fused CTA kernel for 32 < n <= 128 where it
+// wins, the blocked loop otherwise (optionally split into batch groups on
+// internal streams, optionally with the panel look-ahead). T (and T2, the
+// look-ahead's second factor buffer, or nullptr) is the caller's workspace.
 int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
                   float* T, float* T2, int64_t batch, int n, cudaStream_t s) {
   if (n <= kFusedMaxN) return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);

@@ -6,7 +6,8 @@ problem with cond = 1 (src/qrbench/inputs.py:52-60, restated in
 ``inputs.make_benchmark_problem``), gated with the FP64 checker, then timed for
 this library's ``impl`` and for the library baseline ``torch.geqrf`` on the
 same GPU (cuSOLVER). Each point also records its regime: the path that runs
-(the fused n <= 32 kernel or the blocked panel / trailing-update route), the
+(the fused warp kernel for n <= 32, the fused CTA kernel for 32 < n <= 128 at the
+sizes it is dispatched for, or the blocked panel / trailing-update route), the
 bound (HBM traffic 2 b n^2 4 bytes against the measured copy bandwidth, or
 (4/3) n^3 b FLOPs against the FP32 FFMA peak, whichever takes longer) and the
 achieved fraction of that roofline.
@@ -46,7 +47,8 @@ def regime(batch: int, n: int, ms: float, peaks: dict) -> dict:
     bound = "hbm" if t_hbm >= t_flop else "flop"
     floor_ms = max(t_hbm, t_flop) * 1e3
     return {
-        "path": "fused" if n <= 32 else "blocked",
+        "path": ("fused" if n <= 32 else
+                 "fused_cta" if n <= 128 and (n <= 64 or batch <= 592) else "blocked"),
         "bound": bound,
         "floor_ms": floor_ms,
         "roofline_frac": floor_ms / ms if ms > 0 else None,

@@ -48,11 +48,12 @@ class VariantInfo:
 
 VARIANT_INFO: dict[str, VariantInfo] = {
     "b200_geqrf": VariantInfo(
-        "B200 sm_100a: fused warp kernel (n<=32), else cluster panel + larft + FFMA larfb",
+        "B200 sm_100a: fused warp kernel (n<=32), fused CTA kernel (n<=128, size permitting), "
+        "else cluster panel + larft + FFMA larfb",
         "active",
     ),
     "b200_fused_smalln": VariantInfo(
-        "B200 sm_100a fused one-warp-per-matrix QR (n<=32 only)",
+        "B200 sm_100a fused whole-matrix QR, 2 or 4 matrices per warp (n<=32 only)",
         "experimental",
     ),
 }

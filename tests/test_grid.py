@@ -17,6 +17,8 @@ def test_regime_bounds_follow_the_roofline_crossover():
     assert 0.2 < small["roofline_frac"] < 0.25 and small["achieved_unit"] == "GB/s"
     big = grid.regime(8, 4096, 30.0, PEAKS)
     assert big["path"] == "blocked" and big["bound"] == "flop"
+    assert grid.regime(8, 64, 0.035, PEAKS)["path"] == "fused_cta"
+    assert grid.regime(1024, 96, 0.27, PEAKS)["path"] == "blocked"
     flops = 4 / 3 * 4096**3 * 8
     assert math.isclose(big["achieved"], flops / 0.030 / 1e12)
     assert math.isclose(big["roofline_frac"], flops / (grid.FP32_FFMA_TFLOPS * 1e12) * 1e3 / 30.0)
