@@ -21,6 +21,8 @@ std::atomic<int64_t> g_host_ramp{0};
 std::atomic<int64_t> g_fused_cpl{0};
 std::atomic<int64_t> g_mid_fused{1};
 std::atomic<int64_t> g_lookahead{2};  // 0 off, 1 on, 2 from kLookaheadMinN
+std::atomic<int64_t> g_two_level{0};  // 0 off, 1 on
+std::atomic<int64_t> g_panel_rpt{0};
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -145,6 +147,60 @@ int blocked_qr_lookahead(const float* A, int64_t strideA_b, int64_t strideA_row,
   return rc;
 }
 
+// Two-level blocking: per 64 columns two 32-column panels and one trailing
+// update with the combined 64-reflector block, so that each trailing column
+// is read and written once per 64 reflectors instead of once per 32.
+//   panel 1           columns j0 .. j0+31 (T1 on the diagonal of T64)
+//   update (k = 32)   panel 1's reflectors on columns j0+32 .. j0+63
+//   panel 2           rows and columns from j0+32 (T2 on the diagonal of T64)
+//   t64               the cross block of T64 from V1^T V2
+//   update (k = 64)   both panels' reflectors on the columns from j0+64.
+// Where the 64-wide update's operands are not 16-byte aligned, the two panels
+// are applied one after the other instead (the same product).
+int blocked_qr2(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
+                float* T64, int64_t batch, int n, cudaStream_t s) {
+  const int64_t nn = (int64_t)n * n;
+  constexpr int W = qrb::kPanelW;
+  constexpr int K2 = 2 * W;
+  constexpr int64_t tsb = (int64_t)K2 * K2;
+  float* T1 = T64;
+  float* T2 = T64 + W * K2 + W;
+  for (int j0 = 0; j0 < n; j0 += K2) {
+    const int r = n - j0;
+    const float* src = (j0 == 0) ? A : H;
+    const int64_t sb = (j0 == 0) ? strideA_b : nn;
+    const int64_t ld = (j0 == 0) ? strideA_row : n;
+    float* Hp = H + (int64_t)j0 * n + j0;
+    const float* Sp = src + (int64_t)j0 * ld + j0;
+    const int w1 = r < W ? r : W;
+    int rc = qrb::launch_panel(Sp, sb, ld, Hp, nn, n, tau + j0, n, T1, tsb, K2, nullptr, batch,
+                               r, w1, s);
+    if (rc != QRB_OK || r <= W) return rc;
+    const int w2 = r - W < W ? r - W : W;
+    rc = larfb_any(Hp, nn, n, T1, tsb, K2, Sp + W, sb, ld, Hp + W, nn, n, batch, r, W, w2, s);
+    if (rc != QRB_OK) return rc;
+    float* Hq = Hp + (int64_t)W * n + W;
+    rc = qrb::launch_panel(Hq, nn, n, Hq, nn, n, tau + j0 + W, n, T2, tsb, K2, nullptr, batch,
+                           r - W, w2, s);
+    if (rc != QRB_OK) return rc;
+    const int c = r - K2;
+    if (c <= 0) continue;
+    if (qrb::larfb64_supported(Hp, nn, n, Sp + K2, sb, ld, Hp + K2, nn, n, c)) {
+      rc = qrb::launch_t64(Hp, nn, n, T64, tsb, batch, r, s);
+      if (rc != QRB_OK) return rc;
+      rc = qrb::launch_larfb64(Hp, nn, n, T64, tsb, Sp + K2, sb, ld, Hp + K2, nn, n, batch, r,
+                               c, s);
+    } else {
+      rc = larfb_any(Hp, nn, n, T1, tsb, K2, Sp + K2, sb, ld, Hp + K2, nn, n, batch, r, W, c, s);
+      if (rc == QRB_OK)
+        rc = larfb_any(Hq, nn, n, T2, tsb, K2, Hq + W, nn, n, Hq + W, nn, n, batch, r - W, W, c,
+                       s);
+    }
+    if (rc != QRB_OK) return rc;
+  }
+  return QRB_OK;
+}
+
 // Internal streams for batch groups, created once per device and kept for the
 // life of the process (streams and events, no device memory).
 constexpr int kMaxGroups = 4;
@@ -195,19 +251,31 @@ int host_direct_mode() { return (int)g_host_direct.load(); }
 bool host_ramp() { return g_host_ramp.load() != 0; }
 int fused_cpl() { return (int)g_fused_cpl.load(); }
 bool mid_fused_enabled() { return g_mid_fused.load() != 0; }
+int panel_rpt() { return (int)g_panel_rpt.load(); }
 int64_t host_direct_blocks() {
   const int64_t b = g_direct_blocks.load();
   return b > 0 ? b : kHostDirectBlocks;
 }
 int finish_call(int rc, cudaStream_t stream) { return finish(rc, stream); }
 
+FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch) {
+  FactorScratch f;
+  const size_t unit = (size_t)batch * kPanelW * kPanelW * sizeof(float);
+  float* base = static_cast<float*>(workspace);
+  if (base == nullptr || batch <= 0 || bytes < unit) return f;
+  f.T = base;
+  if (bytes >= 2 * unit) f.T2 = base + unit / sizeof(float);
+  if (bytes >= 4 * unit) f.T64 = base;
+  return f;
+}
+
 // The whole factorization of validated arguments, enqueued on s: the fused
 // warp kernel for n <= 32, the fused CTA kernel for 32 < n <= 128 where it
 // wins, the blocked loop otherwise (optionally split into batch groups on
-// internal streams, optionally with the panel look-ahead). T (and T2, the
-// look-ahead's second factor buffer, or nullptr) is the caller's workspace.
+// internal streams, with the panel look-ahead or two-level blocking where
+// selected and the workspace holds their factors).
 int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
-                  float* T, float* T2, int64_t batch, int n, cudaStream_t s) {
+                  const FactorScratch& ws, int64_t batch, int n, cudaStream_t s) {
   if (n <= kFusedMaxN) return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
   // The CTA-per-matrix kernel is latency-friendly (one launch) but does about
   // twice the blocked route's arithmetic: measured on B200 it wins at n <= 64
@@ -215,22 +283,31 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
   // (1.2-1.4x at 8-200 matrices), and loses at 1024 x 96 (436 vs 271 us).
   if (n <= kFusedMidMaxN && mid_fused_enabled() && (n <= 64 || batch <= kFusedMidMaxBatch))
     return launch_fused_mid(A, strideA_b, strideA_row, H, tau, batch, n, s);
+  if (ws.T == nullptr) return QRB_ERR_WORKSPACE;
   // Automatic: 4 groups from n = 1024 on (measured on B200: 30.6 vs 32.8 ms for
   // 8 x 4096^2), else 2; at most half the batch.
   int groups = (int)g_groups.load();
   if (groups == 0) groups = n >= 1024 ? 4 : 2;
   if (groups > batch / 2) groups = (int)(batch / 2);
   if (batch < 4) groups = 1;
-  // Look-ahead needs the second T buffer (a workspace of 2 factors per matrix).
+  // Two-level blocking (opt-in: measured on B200 it is slower at every size,
+  // 5.58 vs 5.22 ms at 640 x 512^2, 35.0 vs 29.6 ms at 8 x 4096^2) needs a
+  // 64 x 64 factor per matrix, the look-ahead a second 32 x 32 one; two-level
+  // takes precedence.
+  const bool tl = ws.T64 != nullptr && g_two_level.load() == 1;
   const int64_t la_mode = g_lookahead.load();
-  const bool la = T2 != nullptr && (la_mode == 1 || (la_mode == 2 && n >= kLookaheadMinN));
-  if (groups <= 1 && !la) return blocked_qr(A, strideA_b, strideA_row, H, tau, T, batch, n, s);
+  const bool la = !tl && ws.T2 != nullptr &&
+                  (la_mode == 1 || (la_mode == 2 && n >= kLookaheadMinN));
+  if (groups <= 1 && !la) {
+    if (tl) return blocked_qr2(A, strideA_b, strideA_row, H, tau, ws.T64, batch, n, s);
+    return blocked_qr(A, strideA_b, strideA_row, H, tau, ws.T, batch, n, s);
+  }
   SideStreams* ss = side_streams();
   if (ss == nullptr) return QRB_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(ss->mu);
   if (groups <= 1)
-    return blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, T, T2, batch, n, s, ss->sp[0],
-                                ss->evP[0], ss->evB[0], ss->joinP[0]);
+    return blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, ws.T, ws.T2, batch, n, s,
+                                ss->sp[0], ss->evP[0], ss->evB[0], ss->joinP[0]);
   // Split the batch into groups that run the same kernel sequence on separate
   // internal streams, forked from and joined back into the caller's stream, so
   // that one group's (latency-bound) panel kernels overlap another group's
@@ -244,13 +321,16 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     if (b1 <= b0) continue;
     cudaStream_t gs = ss->s[g];
     if (cudaStreamWaitEvent(gs, ss->fork, 0) != cudaSuccess) return QRB_ERR_LAUNCH;
-    if (la)
+    if (tl)
+      rc = blocked_qr2(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
+                       ws.T64 + b0 * 4 * tper, b1 - b0, n, gs);
+    else if (la)
       rc = blocked_qr_lookahead(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn,
-                                tau + b0 * n, T + b0 * tper, T2 + b0 * tper, b1 - b0, n, gs,
-                                ss->sp[g], ss->evP[g], ss->evB[g], ss->joinP[g]);
+                                tau + b0 * n, ws.T + b0 * tper, ws.T2 + b0 * tper, b1 - b0, n,
+                                gs, ss->sp[g], ss->evP[g], ss->evB[g], ss->joinP[g]);
     else
       rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
-                      T + b0 * tper, b1 - b0, n, gs);
+                      ws.T + b0 * tper, b1 - b0, n, gs);
     if (cudaEventRecord(ss->join[g], gs) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
     if (cudaStreamWaitEvent(s, ss->join[g], 0) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
   }
@@ -283,9 +363,10 @@ int32_t qrb_fused_max_n(void) { return qrb::kFusedMaxN; }
 
 size_t qrb_workspace_bytes(int64_t batch, int32_t n) {
   if (batch <= 0 || n <= qrb::kFusedMaxN) return 0;
-  // Two 32 x 32 compact-WY factors T per matrix (the second for the panel
-  // look-ahead; one suffices without it).
-  return 2 * (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float);
+  // Four 32 x 32 units per matrix: one compact-WY factor T is the minimum, a
+  // second enables the panel look-ahead, all four (one 64 x 64 factor) the
+  // two-level blocking.
+  return 4 * (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float);
 }
 
 int qrb_fused_qr_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
@@ -324,11 +405,19 @@ int qrb_larfb_f32(const float* V, int64_t strideV_b, int64_t strideV_row,
   if (batch < 0 || r < 0 || k < 0 || c < 0) return QRB_ERR_INVALID_ARG;
   if (batch == 0 || r == 0 || k == 0 || c == 0) return QRB_OK;
   if (!V || !T || !C) return QRB_ERR_INVALID_ARG;
-  if (k > qrb::kPanelW || r < k) return QRB_ERR_UNSUPPORTED;
+  const bool k64 = k == 2 * qrb::kPanelW;
+  if ((k > qrb::kPanelW && !k64) || r < k) return QRB_ERR_UNSUPPORTED;
   if (bad_matrix_strides(strideV_b, strideV_row, r, k, batch)) return QRB_ERR_INVALID_ARG;
   if (bad_matrix_strides(strideC_b, strideC_row, r, c, batch)) return QRB_ERR_INVALID_ARG;
+  if (k64 && !qrb::larfb64_supported(V, strideV_b, strideV_row, C, strideC_b, strideC_row, C,
+                                     strideC_b, strideC_row, c))
+    return QRB_ERR_UNSUPPORTED;
   if (take_injected_failure()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (k64)
+    return finish(qrb::launch_larfb64(V, strideV_b, strideV_row, T, (int64_t)k * k, C, strideC_b,
+                                      strideC_row, C, strideC_b, strideC_row, batch, r, c, s),
+                  s);
   const int rc = larfb_any(V, strideV_b, strideV_row, T, (int64_t)k * k, k, C, strideC_b,
                            strideC_row, C, strideC_b, strideC_row, batch, r, k, c, s);
   return finish(rc, s);
@@ -343,18 +432,16 @@ int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
   if (n > qrb::kMaxN) return QRB_ERR_UNSUPPORTED;
   if (bad_matrix_strides(strideA_b, strideA_row, n, n, batch)) return QRB_ERR_INVALID_ARG;
   if (A == H && (strideA_row != n || strideA_b != (int64_t)n * n)) return QRB_ERR_INVALID_ARG;
-  float* T2 = nullptr;
+  qrb::FactorScratch fs;
   if (n > qrb::kFusedMaxN) {
-    const size_t one = qrb_workspace_bytes(batch, n) / 2;  // the minimum: one factor each
+    const size_t one = qrb_workspace_bytes(batch, n) / 4;  // the minimum: one factor each
     if (workspace == nullptr || workspace_bytes < one) return QRB_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
-    if (workspace_bytes >= 2 * one) T2 = static_cast<float*>(workspace) + one / sizeof(float);
+    fs = qrb::factor_scratch(workspace, workspace_bytes, batch);
   }
   if (take_injected_failure()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return finish(qrb::geqrf_enqueue(A, strideA_b, strideA_row, H, tau,
-                                   static_cast<float*>(workspace), T2, batch, n, s),
-                s);
+  return finish(qrb::geqrf_enqueue(A, strideA_b, strideA_row, H, tau, fs, batch, n, s), s);
 }
 
 int qrb_set_config(const char* key, int64_t value) {
@@ -392,6 +479,16 @@ int qrb_set_config(const char* key, int64_t value) {
   if (std::strcmp(key, "lookahead") == 0) {
     if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
     g_lookahead.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "two_level") == 0) {
+    if (value < 0 || value > 1) return QRB_ERR_INVALID_ARG;
+    g_two_level.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "panel_rpt") == 0) {
+    if (value != 0 && value != 1 && value != 2 && value != 4) return QRB_ERR_INVALID_ARG;
+    g_panel_rpt.store(value);
     return QRB_OK;
   }
   if (std::strcmp(key, "mid_fused") == 0) {
@@ -440,6 +537,8 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "fused_cpl") == 0) { *value = g_fused_cpl.load(); return QRB_OK; }
   if (std::strcmp(key, "mid_fused") == 0) { *value = g_mid_fused.load(); return QRB_OK; }
   if (std::strcmp(key, "lookahead") == 0) { *value = g_lookahead.load(); return QRB_OK; }
+  if (std::strcmp(key, "two_level") == 0) { *value = g_two_level.load(); return QRB_OK; }
+  if (std::strcmp(key, "panel_rpt") == 0) { *value = g_panel_rpt.load(); return QRB_OK; }
   if (std::strcmp(key, "direct_blocks") == 0) { *value = qrb::host_direct_blocks(); return QRB_OK; }
   if (std::strcmp(key, "host_path") == 0) { *value = qrb::host_last_path(); return QRB_OK; }
   return QRB_ERR_INVALID_ARG;

@@ -114,6 +114,9 @@ int launch_larfb(const float* V, int64_t sVb, int64_t ldv, const float* T,
                  cudaStream_t stream);
 
 int panel_cluster_size(int r);
+// qrb_set_config("panel_rpt"): rows per thread of the panel kernel, 1, 2 or 4
+// (0 = automatic: 1 up to 128 rows, else 4).
+int panel_rpt();
 
 // Tensor-core (tcgen05, 3xTF32) trailing update for k = 32 reflectors and
 // 16-byte aligned row-major operands; same contract as launch_larfb.
@@ -125,16 +128,41 @@ int launch_larfb_tc(const float* V, int64_t sVb, int64_t ldv, const float* T,
                     int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
                     int64_t batch, int r, int c, cudaStream_t stream);
 
+// Two-level blocking (64 reflectors = two panels). larfb64: C_dst <- C_src -
+// V T^T V^T C_src for r x c blocks (r >= 64) with 64 reflectors read from V's
+// strictly lower part and T 64 x 64 per matrix (row stride 64); operands must
+// pass larfb64_supported (16-byte aligned rows and matrices, c % 4 == 0).
+// t64: fill the cross block of such a T in place from V (r > 64 rows), the
+// diagonal blocks T1 and T2 having been written by the two panels.
+bool larfb64_supported(const float* V, int64_t sVb, int64_t ldv, const float* Csrc,
+                       int64_t sCsb, int64_t ldcs, const float* Cdst, int64_t sCdb,
+                       int64_t ldcd, int c);
+int launch_larfb64(const float* V, int64_t sVb, int64_t ldv, const float* T, int64_t sTb,
+                   const float* Csrc, int64_t sCsb, int64_t ldcs, float* Cdst, int64_t sCdb,
+                   int64_t ldcd, int64_t batch, int r, int c, cudaStream_t stream);
+int launch_t64(const float* V, int64_t sVb, int64_t ldv, float* T64, int64_t sT64b,
+               int64_t batch, int r, cudaStream_t stream);
+
 // Device-side error flag set by kernels whose bounded waits timed out
 // (synchronous read; optionally reset to 0), and its device address.
 int device_error_flag(int* value, bool reset);
 int device_error_ptr(int** p);
 
+// The blocked route's factor scratch, carved from the caller's workspace of
+// `bytes` for `batch` matrices: T one 32 x 32 factor per matrix (required),
+// T2 a second one for the panel look-ahead, T64 one 64 x 64 factor per matrix
+// for two-level blocking (each nullptr when the workspace is too small).
+struct FactorScratch {
+  float* T = nullptr;
+  float* T2 = nullptr;
+  float* T64 = nullptr;
+};
+FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch);
+
 // Whole factorization of already validated arguments, enqueued on `stream`
-// (no fault injection, no sync check); T is one T factor per matrix of the
-// qrb_workspace_bytes scratch, T2 (or nullptr) a second one for the look-ahead.
-int geqrf_enqueue(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau, float* T,
-                  float* T2, int64_t batch, int n, cudaStream_t stream);
+// (no fault injection, no sync check), the blocked route's factors in ws.
+int geqrf_enqueue(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau,
+                  const FactorScratch& ws, int64_t batch, int n, cudaStream_t stream);
 
 // The public entry points' shared epilogue pieces: consume one injected
 // failure (fail_next), and apply the sync_check mode to a call's status.

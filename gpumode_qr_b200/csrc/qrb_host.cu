@@ -196,6 +196,8 @@ int qrb_geqrf_f32_host(const float* A_host, float* H_host, float* tau_host, int6
   float* T = reinterpret_cast<float*>(reinterpret_cast<char*>(tau_d) +
                                       align_up((size_t)batch * n * sizeof(float)));
 
+  // one chunk's factors at a time (the chunks run in order on one stream)
+  const qrb::FactorScratch fs = qrb::factor_scratch(T, qrb_workspace_bytes(batch, n), batch);
   HostPipe* p = host_pipe();
   if (p == nullptr) return QRB_ERR_DEVICE;
   int rc = QRB_OK;
@@ -224,8 +226,7 @@ int qrb_geqrf_f32_host(const float* A_host, float* H_host, float* tau_host, int6
       }
       rc = where == qrb::HostMem::kTau
                ? qrb::launch_fused_small(Mc, nn, n, Mc, dt + b0 * n, cnt, n, p->comp, where)
-               : qrb::geqrf_enqueue(Mc, nn, n, Mc, tc, T, T + batch * qrb::kPanelW * qrb::kPanelW,
-                                    cnt, n, p->comp);
+               : qrb::geqrf_enqueue(Mc, nn, n, Mc, tc, fs, cnt, n, p->comp);
       if (rc != QRB_OK) break;
       if (cudaEventRecord(p->factored[c], p->comp) != cudaSuccess ||
           cudaStreamWaitEvent(p->out, p->factored[c], 0) != cudaSuccess ||

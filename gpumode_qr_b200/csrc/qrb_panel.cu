@@ -71,7 +71,7 @@ __device__ __forceinline__ float pick32(const float (&v)[W], int j) {
 }
 
 template <int RPT>
-__global__ void __launch_bounds__(RPT >= 4 ? kPanelCtaThreads : kMaxThreads, 1)
+__global__ void __launch_bounds__(RPT >= 2 ? kPanelCtaThreads : kMaxThreads, 1)
 k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
         float* __restrict__ dst, int64_t sb_dst, int64_t ld_dst,
         float* __restrict__ tau_out, int64_t tau_sb, float* __restrict__ T_out,
@@ -294,12 +294,21 @@ int launch_panel_rpt(const float* src, int64_t sb_src, int64_t ld_src,
 // Rows per thread: 1 up to 128 rows (one CTA of up to 128 threads), else 4:
 // one CTA of up to 256 threads up to 1024 rows, beyond that a cluster of cs
 // CTAs of 256 threads (cs a power of two, <= 8 for the launch to be accepted).
+// qrb_set_config("panel_rpt") = 1 (CTAs of up to 512 threads) or 2 (up to 256)
+// selects that many rows per thread instead (4 where that would need more than
+// 8 CTAs).
 static void panel_shape(int r, int* rpt, int* cs, int* nt) {
-  const int R = r > 128 ? 4 : 1;
-  const int per_cta_max = kPanelCtaThreads * R;
-  const int need = (r + per_cta_max - 1) / per_cta_max;
+  const int pref = panel_rpt();
+  int R = pref > 0 ? pref : (r > 128 ? 4 : 1);
   int c = 1;
-  while (c < need) c <<= 1;  // cluster sizes 1, 2, 4, 8
+  for (;;) {
+    const int per_cta_max = (R >= 2 ? kPanelCtaThreads : kMaxThreads) * R;
+    const int need = (r + per_cta_max - 1) / per_cta_max;
+    c = 1;
+    while (c < need) c <<= 1;  // cluster sizes 1, 2, 4, 8
+    if (c <= kMaxCluster || R >= 4) break;
+    R = 4;
+  }
   int threads = (r + R * c - 1) / (R * c);
   threads = ((threads + 31) / 32) * 32;
   if (threads < 32) threads = 32;
@@ -325,6 +334,10 @@ int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
   if (batch * cs > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
   if (rpt == 1)
     return launch_panel_rpt<1>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
+                               tau_sb, T_out, T_sb, t_ld, V_out, batch, r, w, cs,
+                               nt, stream);
+  if (rpt == 2)
+    return launch_panel_rpt<2>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
                                tau_sb, T_out, T_sb, t_ld, V_out, batch, r, w, cs,
                                nt, stream);
   return launch_panel_rpt<4>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,

@@ -60,10 +60,10 @@ QRB_API const char* qrb_status_string(int status);
 /* Largest n that qrb_geqrf_f32 accepts. */
 QRB_API int32_t qrb_max_n(void);
 
-/* Bytes of device workspace to give qrb_geqrf_f32 for (batch, n): two 32 x 32
- * T factors per matrix when n > 32, 0 otherwise. Half of it (one factor per
- * matrix) is the minimum accepted; the second half enables the panel
- * look-ahead ("lookahead" below). */
+/* Bytes of device workspace to give qrb_geqrf_f32 for (batch, n): four
+ * 32 x 32 units (16 KiB) per matrix when n > 32, 0 otherwise. A quarter of it
+ * (one T factor per matrix) is the minimum accepted; half enables the panel
+ * look-ahead ("lookahead" below), all of it two-level blocking ("two_level"). */
 QRB_API size_t qrb_workspace_bytes(int64_t batch, int32_t n);
 
 /*
@@ -176,7 +176,9 @@ QRB_API int qrb_panel_qr_f32(const float* P, int64_t strideP_b, int64_t strideP_
  * factored panel to the trailing columns. Replaces the three batched GEMMs of
  * _hh_panel_blocked_qr (src/qrbench/variants.py:800-804).
  *
- *   V      reflectors, batch x r x k (k <= 32), strides (strideV_b,
+ *   V      reflectors, batch x r x k (k <= 32, or k = 64: the two-level
+ *          block, which needs 16-byte aligned V and C rows and matrices and
+ *          c % 4 == 0, else QRB_ERR_UNSUPPORTED), strides (strideV_b,
  *          strideV_row). Only the strictly lower part is read: the diagonal is
  *          taken as 1 and the upper part as 0, so V may point into a packed H.
  *   T      batch x k x k contiguous (stride k*k), upper triangular.
@@ -240,6 +242,15 @@ QRB_API int qrb_ormqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row
  *                 needs the full qrb_workspace_bytes. Panel j + 1 and the
  *                 update of its columns run on a second stream while the rest
  *                 of step j's update runs; results are unchanged.
+ *   "two_level"   blocked route: 0 (default) = off, 1 = on; needs the full
+ *                 qrb_workspace_bytes. Two 32-column panels are combined into
+ *                 one 64-reflector block (T 64 x 64) for the trailing update;
+ *                 takes precedence over "lookahead". Same results to FP32
+ *                 rounding; slower than the default on B200 at every measured
+ *                 size, kept as an option.
+ *   "panel_rpt"   rows per thread of the panel kernel: 0 (default) = 1 up to
+ *                 128 rows, else 4; 1 or 2 force that many (CTAs of up to 512
+ *                 or 256 threads; 4 where more than 8 CTAs would be needed).
  *   "mid_fused"   1 (default): 32 < n <= 64, and 64 < n <= 128 up to 592
  *                 matrices, are factored by one CTA per matrix in one launch;
  *                 0: always the blocked panel route above n = 32.

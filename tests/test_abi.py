@@ -58,7 +58,7 @@ def test_status_strings_and_constants():
 def test_workspace_bytes():
     L = _lib.lib()
     assert L.qrb_workspace_bytes(4096, 32) == 0
-    assert L.qrb_workspace_bytes(8, 64) == 2 * 8 * 32 * 32 * 4
+    assert L.qrb_workspace_bytes(8, 64) == 4 * 8 * 32 * 32 * 4
     assert L.qrb_workspace_bytes(0, 512) == 0
 
 
@@ -66,7 +66,7 @@ def test_host_entry_workspace_and_validation_without_gpu():
     L = _lib.lib()
     mats, taus = 8 * 64 * 64 * 4, 8 * 64 * 4
     up = lambda x: (x + 255) // 256 * 256
-    assert L.qrb_host_workspace_bytes(8, 64) == up(mats) + up(taus) + 2 * 8 * 32 * 32 * 4
+    assert L.qrb_host_workspace_bytes(8, 64) == up(mats) + up(taus) + 4 * 8 * 32 * 32 * 4
     assert L.qrb_host_workspace_bytes(4096, 32) == up(4096 * 32 * 32 * 4) + up(4096 * 32 * 4)
     assert L.qrb_host_workspace_bytes(0, 64) == 0
     assert L.qrb_host_workspace_bytes(4, 8193) == 0
@@ -189,6 +189,18 @@ def test_config_keys():
     _lib.set_config("lookahead", 2)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("lookahead", 3)
+    assert _lib.get_config("two_level") == 0
+    _lib.set_config("two_level", 1)
+    assert _lib.get_config("two_level") == 1
+    _lib.set_config("two_level", 0)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("two_level", 2)
+    assert _lib.get_config("panel_rpt") == 0
+    for v in (1, 2, 4, 0):
+        _lib.set_config("panel_rpt", v)
+        assert _lib.get_config("panel_rpt") == v
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("panel_rpt", 3)
     assert _lib.get_config("mid_fused") == 1
     _lib.set_config("mid_fused", 0)
     assert _lib.get_config("mid_fused") == 0

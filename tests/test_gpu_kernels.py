@@ -127,6 +127,30 @@ def test_larfb_kernel_matches_fp64(r, k, c, larfb_kind):
     assert _rel(Cd, want) < tol
 
 
+@pytest.mark.parametrize("r,c", [(64, 4), (65, 64), (100, 36), (512, 448), (1000, 132),
+                                 (4096, 64), (2049, 200)])
+def test_larfb_two_level_block_matches_fp64(r, c):
+    # k = 64: the two-level block (two panels' reflectors in one update)
+    g = torch.Generator().manual_seed(r + 3 * c)
+    b, k = 3, 64
+    Vfull = torch.randn(b, r, k, generator=g)
+    Vexp = torch.tril(Vfull, -1) + torch.eye(r, k)
+    T = torch.triu(torch.randn(b, k, k, generator=g)) * 0.25
+    C = torch.randn(b, r, c, generator=g)
+    want = oracle.larfb(Vexp.numpy(), T.numpy(), C.numpy(), f64=True)
+    Cd = C.to(DEV)
+    api.larfb(Vfull.to(DEV), T.to(DEV), Cd)
+    assert _rel(Cd, want) < 1e-5
+
+
+def test_larfb_two_level_block_needs_aligned_operands():
+    V = torch.randn(2, 100, 64, device=DEV)
+    T = torch.randn(2, 64, 64, device=DEV)
+    C = torch.randn(2, 100, 6, device=DEV)  # c % 4 != 0
+    with pytest.raises(_lib.QRBError):
+        api.larfb(V, T, C)
+
+
 def test_larfb_strided_views_inside_a_matrix(larfb_kind):
     # V and C as views into one packed matrix, as the blocked driver uses them
     g = torch.Generator().manual_seed(9)
@@ -253,7 +277,7 @@ def test_panel_lookahead_gives_identical_results(n, groups):
             outs[la] = api.geqrf(A)
         torch.cuda.synchronize()
         # minimal workspace: one factor per matrix, look-ahead requested but unavailable
-        ws_one = api.workspace_bytes(b, n) // 2
+        ws_one = api.workspace_bytes(b, n) // 4
         ws = torch.empty(ws_one, dtype=torch.uint8, device=DEV)
         H = torch.empty_like(A)
         tau = torch.empty(b, n, device=DEV)
@@ -267,3 +291,76 @@ def test_panel_lookahead_gives_identical_results(n, groups):
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
     assert torch.equal(H, outs[0][0]) and torch.equal(tau, outs[0][1])
     assert checker.check(A.cpu(), outs[1][0].cpu(), outs[1][1].cpu()).passed
+
+
+@pytest.mark.parametrize("n", [129, 130, 200, 256, 512, 1000, 1100])
+@pytest.mark.parametrize("groups", [1, 2])
+def test_two_level_blocking_matches_one_level(n, groups):
+    # Two panels combined into one 64-reflector update: the same factorization
+    # up to FP32 rounding (different summation order), FP64 gates passing.
+    # n % 4 != 0 takes the aligned-operand fallback (two 32-wide updates).
+    b = 4
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(2 * n + groups)).to(DEV)
+    old = {k: _lib.get_config(k) for k in ("two_level", "groups", "mid_fused")}
+    outs = {}
+    try:
+        _lib.set_config("groups", groups)
+        _lib.set_config("mid_fused", 0)
+        for tl in (0, 1):
+            _lib.set_config("two_level", tl)
+            outs[tl] = api.geqrf(A)
+            torch.cuda.synchronize()
+        # a two-factor workspace cannot hold the 64 x 64 factor: one-level route
+        ws_two = api.workspace_bytes(b, n) // 2
+        ws = torch.empty(ws_two, dtype=torch.uint8, device=DEV)
+        H = torch.empty_like(A)
+        tau = torch.empty(b, n, device=DEV)
+        rc = _lib.lib().qrb_geqrf_f32(A.data_ptr(), n * n, n, H.data_ptr(), tau.data_ptr(), b, n,
+                                      ws.data_ptr(), ws_two, torch.cuda.current_stream().cuda_stream)
+        _lib.check(rc)
+        torch.cuda.synchronize()
+    finally:
+        for k, v in old.items():
+            _lib.set_config(k, v)
+    assert checker.check(A.cpu(), outs[1][0].cpu(), outs[1][1].cpu()).passed
+    par = checker.parity(outs[1][0].cpu(), outs[1][1].cpu(), outs[0][0].cpu(), outs[0][1].cpu())
+    assert par.ok(RTOL), par
+    assert torch.equal(H, outs[0][0]) and torch.equal(tau, outs[0][1])
+
+
+def test_two_level_blocking_against_lapack():
+    # elementwise against CPU LAPACK geqrf on a well-conditioned problem
+    # (column scales 1 .. 1e-2, the benchmark's cond 1e2 family)
+    from gpumode_qr_b200 import inputs
+    prob = inputs.make_benchmark_problem({"batch": 3, "n": 640, "cond": 2})
+    A = prob.tensor
+    old = _lib.get_config("two_level")
+    try:
+        _lib.set_config("two_level", 1)
+        H, tau = api.geqrf(A.to(DEV))
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_config("two_level", old)
+    Hr, tr = torch.geqrf(A)
+    par = checker.parity(H.cpu(), tau.cpu(), Hr, tr)
+    assert par.ok(1e-3), par
+
+
+@pytest.mark.parametrize("rpt", [1, 2, 4])
+@pytest.mark.parametrize("n", [160, 512, 1100, 2100])
+def test_panel_rows_per_thread_variants(rpt, n):
+    # rows per thread of the panel kernel changes the reduction grouping only
+    b = 2
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(n + rpt)).to(DEV)
+    H0, t0 = api.geqrf(A)
+    old = _lib.get_config("panel_rpt")
+    try:
+        _lib.set_config("panel_rpt", rpt)
+        H, tau = api.geqrf(A)
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_config("panel_rpt", old)
+    assert checker.check(A.cpu(), H.cpu(), tau.cpu()).passed
+    # a Gaussian matrix of n = 2100 has cond ~ 1e4: the trailing tau move by a
+    # few 1e-4 under a different summation order; the north-star bar is 1e-3
+    assert checker.parity(H.cpu(), tau.cpu(), H0.cpu(), t0.cpu()).ok(1e-3)
