@@ -17,6 +17,8 @@ __all__ = [
     "householder_product",
     "ormqr",
     "geqrf_host",
+    "gram",
+    "gram_geqrf",
     "VARIANTS",
     "VARIANT_INFO",
     "CHAMPION",
@@ -30,7 +32,7 @@ from .variants import CHAMPION, VARIANT_INFO, VARIANTS  # noqa: E402
 
 def __getattr__(name):  # lazy: keep `import gpumode_qr_b200` torch-free
     if name in ("geqrf", "impl", "hh_fused_qr", "hh_panel_qr", "larfb", "householder_product",
-                "ormqr", "geqrf_host"):
+                "ormqr", "geqrf_host", "gram", "gram_geqrf"):
         from . import api
 
         return getattr(api, name)

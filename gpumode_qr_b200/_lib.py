@@ -29,6 +29,8 @@ SIGNATURES: dict[str, tuple] = {
     "qrb_orgqr_f32": (ctypes.c_int, [_P, _I64, _I64, _P, _I32, _P, _I64, _I32, _P, _SZ, _P]),
     "qrb_ormqr_f32": (ctypes.c_int, [_P, _I64, _I64, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32,
                                      _I32, _P, _SZ, _P]),
+    "qrb_gram_f32": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I32, _I32, _P]),
+    "qrb_gram_geqrf_f32": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _I64, _I32, _I32, _P, _SZ, _P]),
     "qrb_geqrf_f32_host": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _P, _SZ, _I32, _P]),
     "qrb_fused_qr_f32": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _I64, _I32, _P]),
     "qrb_fused_max_n": (_I32, []),

@@ -10,6 +10,8 @@
   (``src/qrbench/triton_kernels.py:912-967``).
 * :func:`larfb` — the trailing block-reflector update
   (``src/qrbench/variants.py:800-804``).
+* :func:`gram`, :func:`gram_geqrf` — the statistics ``G @ G.mT`` that the
+  reference's workload factors, alone or followed by the factorization.
 
 Every function runs the CUDA library on the caller's current stream. Inputs
 that the library cannot take (CPU tensors, other dtypes, non-square shapes)
@@ -17,6 +19,8 @@ raise; nothing falls back to another implementation. ``A`` is never modified.
 """
 
 from __future__ import annotations
+
+import math
 
 import torch
 
@@ -189,6 +193,55 @@ def geqrf_host(A_host: torch.Tensor, H_host: torch.Tensor, tau_host: torch.Tenso
             torch.cuda.current_stream(dev).cuda_stream,
         )
         _lib.check(rc)
+
+
+def _gram_input(G: torch.Tensor) -> torch.Tensor:
+    _require_cuda_f32("G", G)
+    if G.dim() < 2:
+        raise ValueError(f"G must be [..., n, k], got {tuple(G.shape)}")
+    n, k = G.shape[-2], G.shape[-1]
+    if n > max_n():
+        raise ValueError(f"n={n} exceeds the supported maximum {max_n()}")
+    if k == 0:  # nothing to read: S = 0
+        return G.new_empty((math.prod(G.shape[:-2]), n, 0))
+    return _as_rowmajor_batch(G, n, k)
+
+
+def gram(G: torch.Tensor) -> torch.Tensor:
+    """``S = G @ G.mT`` in FP32 (no TF32) for ``G [..., n, k]``: the statistics
+    the reference's workload factors (its task statement, ``AGENTS.md:27``).
+    ``S`` is ``[..., n, n]``, exactly symmetric, a new tensor."""
+    G3 = _gram_input(G)
+    n, k = G.shape[-2], G.shape[-1]
+    S = torch.empty((*G.shape[:-2], n, n), dtype=G.dtype, device=G.device)
+    if S.numel() == 0:
+        return S
+    with torch.cuda.device(G.device):
+        rc = _lib.lib().qrb_gram_f32(G3.data_ptr(), G3.stride(0), G3.stride(1), S.data_ptr(),
+                                     G3.shape[0], n, k, _stream(G.device))
+    _lib.check(rc)
+    return S
+
+
+def gram_geqrf(G: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """``geqrf(G @ G.mT)`` in one library call: ``(H, tau)`` of the Gram matrix
+    of ``G [..., n, k]``, with ``torch.geqrf`` semantics as :func:`geqrf`."""
+    G3 = _gram_input(G)
+    n, k = G.shape[-2], G.shape[-1]
+    lead = G.shape[:-2]
+    H = torch.empty((*lead, n, n), dtype=G.dtype, device=G.device)
+    tau = torch.empty((*lead, n), dtype=G.dtype, device=G.device)
+    if H.numel() == 0:
+        return H, tau
+    b = G3.shape[0]
+    with torch.cuda.device(G.device):
+        ws_n = workspace_bytes(b, n)
+        ws = torch.empty(max(ws_n, 16), dtype=torch.uint8, device=G.device)
+        rc = _lib.lib().qrb_gram_geqrf_f32(G3.data_ptr(), G3.stride(0), G3.stride(1),
+                                           H.data_ptr(), tau.data_ptr(), b, n, k, ws.data_ptr(),
+                                           ws_n, _stream(G.device))
+    _lib.check(rc)
+    return H, tau
 
 
 def hh_fused_qr(A: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -215,6 +215,27 @@ QRB_API int qrb_ormqr_f32(const float* H, int64_t strideH_b, int64_t strideH_row
                           void* stream);
 
 /*
+ * The step in front of the factorization in the reference's workload: the
+ * statistics S = G G^T of gradients viewed as [basis_dim n, contracted_dim k]
+ * (reference AGENTS.md:27, "statistics are formed as G @ G.T, and QR is run on
+ * square basis_dim x basis_dim matrices"). No reference function computes it;
+ * it replaces the caller's torch G @ G.mT (FP32, no TF32) in front of impl().
+ *
+ * qrb_gram_f32: G batch x n x k, strides (strideG_b, strideG_row >= k), unit
+ * column stride; S batch x n x n contiguous, both triangles written (exactly
+ * symmetric). k = 0 gives S = 0. S must not overlap G.
+ *
+ * qrb_gram_geqrf_f32: (H, tau) = geqrf(G G^T) in one call: the Gram matrix is
+ * formed into H and factored in place; the same workspace as qrb_geqrf_f32
+ * (qrb_workspace_bytes(batch, n)). H must not overlap G.
+ */
+QRB_API int qrb_gram_f32(const float* G, int64_t strideG_b, int64_t strideG_row, float* S,
+                         int64_t batch, int32_t n, int32_t k, void* stream);
+QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t strideG_row,
+                               float* H, float* tau, int64_t batch, int32_t n, int32_t k,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Tuning and test hooks (never needed for correct use). Keys:
  *   "fail_next"   value v > 0: the next v calls of any compute entry point
  *                 return QRB_ERR_INJECTED without enqueuing work (host-side

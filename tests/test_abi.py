@@ -27,7 +27,7 @@ def test_header_declares_the_expected_entry_points():
         "qrb_version", "qrb_status_string", "qrb_max_n", "qrb_workspace_bytes", "qrb_geqrf_f32",
         "qrb_geqrf_f32_noalloc", "qrb_host_workspace_bytes", "qrb_geqrf_f32_host", "qrb_fused_qr_f32",
         "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32", "qrb_orgqr_workspace_bytes",
-        "qrb_orgqr_f32", "qrb_ormqr_f32",
+        "qrb_orgqr_f32", "qrb_ormqr_f32", "qrb_gram_f32", "qrb_gram_geqrf_f32",
         "qrb_set_config", "qrb_get_config",
     }
 
@@ -85,6 +85,32 @@ def test_host_entry_workspace_and_validation_without_gpu():
     assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, ws, need - 1, 0, None) == 3
     assert L.qrb_geqrf_f32_host(FAKE, FAKE, FAKE, 8, 64, ctypes.c_void_p(0x100010), need, 0,
                                 None) == 1
+
+
+def test_gram_validation_without_gpu():
+    # every call here returns before anything is enqueued
+    L = _lib.lib()
+    ws = ctypes.c_void_p(0x100000)
+    need = L.qrb_workspace_bytes(2, 64)
+    # empty problems
+    assert L.qrb_gram_f32(None, 0, 0, None, 0, 64, 64, None) == 0
+    assert L.qrb_gram_f32(None, 0, 0, None, 2, 0, 64, None) == 0
+    assert L.qrb_gram_geqrf_f32(None, 0, 0, None, None, 0, 64, 64, None, 0, None) == 0
+    # negative sizes, null pointers, row stride < k, overlapping matrices, too large
+    assert L.qrb_gram_f32(FAKE, 64 * 80, 80, FAKE, -1, 64, 80, None) == 1
+    assert L.qrb_gram_f32(None, 64 * 80, 80, FAKE, 2, 64, 80, None) == 1
+    assert L.qrb_gram_f32(FAKE, 64 * 80, 80, None, 2, 64, 80, None) == 1
+    assert L.qrb_gram_f32(FAKE, 64 * 80, 79, FAKE, 2, 64, 80, None) == 1
+    assert L.qrb_gram_f32(FAKE, 64 * 80 - 1, 80, FAKE, 2, 64, 80, None) == 1
+    assert L.qrb_gram_f32(FAKE, 0, 80, FAKE, 1, 8193, 80, None) == 2
+    # gram + geqrf: null tau, short / missing / misaligned workspace
+    assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, None, 2, 64, 80, ws, need, None) == 1
+    assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, FAKE, 2, 64, 80, ws, need // 4 - 1,
+                                None) == 3
+    assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, FAKE, 2, 64, 80, None, need, None) == 3
+    assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, FAKE, 2, 64, 80,
+                                ctypes.c_void_p(0x100004), need, None) == 1
+    assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 79, FAKE, FAKE, 2, 64, 80, ws, need, None) == 1
 
 
 def test_orgqr_ormqr_validation_without_gpu():
