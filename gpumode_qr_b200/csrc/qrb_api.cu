@@ -23,6 +23,7 @@ std::atomic<int64_t> g_mid_fused{1};
 std::atomic<int64_t> g_lookahead{2};  // 0 off, 1 on, 2 from kLookaheadMinN
 std::atomic<int64_t> g_two_level{0};  // 0 off, 1 on
 std::atomic<int64_t> g_panel_rpt{0};
+std::atomic<int64_t> g_gram_tile{0};
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -252,6 +253,7 @@ bool host_ramp() { return g_host_ramp.load() != 0; }
 int fused_cpl() { return (int)g_fused_cpl.load(); }
 bool mid_fused_enabled() { return g_mid_fused.load() != 0; }
 int panel_rpt() { return (int)g_panel_rpt.load(); }
+int gram_tile() { return (int)g_gram_tile.load(); }
 int64_t host_direct_blocks() {
   const int64_t b = g_direct_blocks.load();
   return b > 0 ? b : kHostDirectBlocks;
@@ -491,6 +493,11 @@ int qrb_set_config(const char* key, int64_t value) {
     g_panel_rpt.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "gram_tile") == 0) {
+    if (value != 0 && value != 64 && value != 128) return QRB_ERR_INVALID_ARG;
+    g_gram_tile.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "mid_fused") == 0) {
     if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
     g_mid_fused.store(value);
@@ -539,6 +546,7 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "lookahead") == 0) { *value = g_lookahead.load(); return QRB_OK; }
   if (std::strcmp(key, "two_level") == 0) { *value = g_two_level.load(); return QRB_OK; }
   if (std::strcmp(key, "panel_rpt") == 0) { *value = g_panel_rpt.load(); return QRB_OK; }
+  if (std::strcmp(key, "gram_tile") == 0) { *value = g_gram_tile.load(); return QRB_OK; }
   if (std::strcmp(key, "direct_blocks") == 0) { *value = qrb::host_direct_blocks(); return QRB_OK; }
   if (std::strcmp(key, "host_path") == 0) { *value = qrb::host_last_path(); return QRB_OK; }
   return QRB_ERR_INVALID_ARG;

@@ -117,6 +117,9 @@ int panel_cluster_size(int r);
 // qrb_set_config("panel_rpt"): rows per thread of the panel kernel, 1, 2 or 4
 // (0 = automatic: 1 up to 128 rows, else 4).
 int panel_rpt();
+// qrb_set_config("gram_tile"): S tile of the Gram kernel, 64 or 128 (0 =
+// automatic: 128 above n = 64).
+int gram_tile();
 
 // Tensor-core (tcgen05, 3xTF32) trailing update for k = 32 reflectors and
 // 16-byte aligned row-major operands; same contract as launch_larfb.

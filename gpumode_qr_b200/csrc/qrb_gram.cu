@@ -32,6 +32,7 @@ constexpr int GT_LD = TS + 4;  // transposed staging row stride
 constexpr int TL_LD = TS + 1;  // summed tile row stride (conflict-free mirror reads)
 
 constexpr int RAW_LD = KC + 4;  // row-major landing buffer row stride
+constexpr int kGramBigTileMinN = 64;  // 128 x 128 tiles above this n
 
 struct __align__(16) SmemGram {
   union {
@@ -224,25 +225,202 @@ k_gram(const float* __restrict__ G, int64_t sGb, int64_t ldg, float* __restrict_
   }
 }
 
+// 128 x 128 tiles without the split over chunk columns: thread (ty, tx) of
+// 16 x 16 owns tile rows {4 ty .. 4 ty + 3, 64 + 4 ty ..} and columns
+// {4 tx .., 64 + 4 tx ..} (8 x 8 outputs, 32 packed FMAs per four 16-byte
+// shared loads, no partial sums to reduce); chunks of 32 columns of G land
+// row-major by cp.async while the previous chunk is multiplied and are then
+// transposed into the second of two [column][row] buffers.
+constexpr int TB = 128;
+constexpr int TB_LD = TB + 4;
+struct __align__(16) SmemGram128 {
+  float rawP[TB * RAW_LD];
+  float rawQ[TB * RAW_LD];
+  float P[2][KC * TB_LD];
+  float Q[2][KC * TB_LD];
+};
+
 template <bool VEC>
+__global__ void __launch_bounds__(NT, 2)
+k_gram128(const float* __restrict__ G, int64_t sGb, int64_t ldg, float* __restrict__ S,
+          int n, int k, int nt) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  SmemGram128& sm = *reinterpret_cast<SmemGram128*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int64_t m = blockIdx.y;
+  int ti, tj;
+  tile_of((int)blockIdx.x, nt, &ti, &tj);
+  const int p0 = ti * TB, q0 = tj * TB;
+  const bool diag = ti == tj;
+  const float* __restrict__ Gm = G + m * sGb;
+
+  auto issue_chunk = [&](int t0) {
+    if (VEC) {
+#pragma unroll
+      for (int e = 0; e < (TB * KC) / (4 * NT); ++e) {
+        const int idx = tid + e * NT;
+        const int row = idx >> 3, c4 = (idx & 7) << 2;
+        const int t = t0 + c4;
+        const int ip = p0 + row, iq = q0 + row;
+        const bool okp = ip < n && t < k, okq = !diag && iq < n && t < k;
+        cp_async16(&sm.rawP[row * RAW_LD + c4], okp ? Gm + (int64_t)ip * ldg + t : Gm, okp);
+        if (!diag)
+          cp_async16(&sm.rawQ[row * RAW_LD + c4], okq ? Gm + (int64_t)iq * ldg + t : Gm, okq);
+      }
+    } else {
+#pragma unroll 4
+      for (int e = 0; e < (TB * KC) / NT; ++e) {
+        const int idx = tid + e * NT;
+        const int row = idx >> 5, c = idx & 31;
+        const int t = t0 + c;
+        const int ip = p0 + row, iq = q0 + row;
+        const bool okp = ip < n && t < k, okq = !diag && iq < n && t < k;
+        cp_async4(&sm.rawP[row * RAW_LD + c], okp ? Gm + (int64_t)ip * ldg + t : Gm, okp);
+        if (!diag)
+          cp_async4(&sm.rawQ[row * RAW_LD + c], okq ? Gm + (int64_t)iq * ldg + t : Gm, okq);
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+  // consecutive threads take consecutive rows of one 4-column group, so the
+  // 16-byte reads and the transposed scalar stores are both conflict-free
+  auto transpose_chunk = [&](int buf) {
+#pragma unroll
+    for (int e = 0; e < (TB * KC) / (4 * NT); ++e) {
+      const int idx = tid + e * NT;
+      const int row = idx & (TB - 1), c4 = (idx >> 7) << 2;
+      const float4 a = *reinterpret_cast<const float4*>(&sm.rawP[row * RAW_LD + c4]);
+      float* P = sm.P[buf];
+      P[(c4 + 0) * TB_LD + row] = a.x;
+      P[(c4 + 1) * TB_LD + row] = a.y;
+      P[(c4 + 2) * TB_LD + row] = a.z;
+      P[(c4 + 3) * TB_LD + row] = a.w;
+      if (!diag) {
+        const float4 b = *reinterpret_cast<const float4*>(&sm.rawQ[row * RAW_LD + c4]);
+        float* Q = sm.Q[buf];
+        Q[(c4 + 0) * TB_LD + row] = b.x;
+        Q[(c4 + 1) * TB_LD + row] = b.y;
+        Q[(c4 + 2) * TB_LD + row] = b.z;
+        Q[(c4 + 3) * TB_LD + row] = b.w;
+      }
+    }
+  };
+
+  const int ty = tid >> 4, tx = tid & 15;
+  const int ra = 4 * ty, ca = 4 * tx;  // row groups ra, 64 + ra; column groups ca, 64 + ca
+  float2 acc[8][4];  // rows ra..ra+3, 64+ra..; column pairs (ca, ca+1), (ca+2, ca+3), (64+ca, ..)
+#pragma unroll
+  for (int x = 0; x < 8; ++x)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[x][j] = make_float2(0.f, 0.f);
+
+  const int nch = (k + KC - 1) / KC;
+  issue_chunk(0);
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  __syncthreads();
+  transpose_chunk(0);
+  __syncthreads();
+  for (int ch = 0; ch < nch; ++ch) {
+    const int buf = ch & 1;
+    const bool more = ch + 1 < nch;
+    if (more) issue_chunk((ch + 1) * KC);
+    const float* pb = sm.P[buf];
+    const float* qb = diag ? pb : sm.Q[buf];
+#pragma unroll 4
+    for (int t = 0; t < KC; ++t) {
+      const float4 a0 = *reinterpret_cast<const float4*>(pb + t * TB_LD + ra);
+      const float4 a1 = *reinterpret_cast<const float4*>(pb + t * TB_LD + 64 + ra);
+      const float4 b0 = *reinterpret_cast<const float4*>(qb + t * TB_LD + ca);
+      const float4 b1 = *reinterpret_cast<const float4*>(qb + t * TB_LD + 64 + ca);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                            make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        const float2 ax = make_float2(av[x], av[x]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[x][j] = __ffma2_rn(ax, bp[j], acc[x][j]);
+      }
+    }
+    if (more) {
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      __syncthreads();
+      transpose_chunk(buf ^ 1);
+    }
+    __syncthreads();
+  }
+
+  float* __restrict__ Sm = S + m * (int64_t)n * n;
+  const bool vst = (n & 3) == 0;  // 16-byte row stores stay aligned
+#pragma unroll
+  for (int x = 0; x < 8; ++x) {  // the tile: rows p0 + (x < 4 ? ra + x : 64 + ra + x - 4)
+    const int i = p0 + (x < 4 ? ra + x : 60 + ra + x);
+    if (i >= n) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = q0 + h * 64 + ca;
+      const float v[4] = {acc[x][2 * h].x, acc[x][2 * h].y, acc[x][2 * h + 1].x,
+                          acc[x][2 * h + 1].y};
+      float* g = Sm + (int64_t)i * n + j;
+      if (vst && j + 3 < n) {
+        *reinterpret_cast<float4*>(g) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int y = 0; y < 4; ++y)
+          if (j + y < n) g[y] = v[y];
+      }
+    }
+  }
+  if (!diag) {  // the mirror: S[q0 + col][p0 + row]
+#pragma unroll
+    for (int y = 0; y < 8; ++y) {  // tile column y of this thread
+      const int jc = q0 + (y < 4 ? ca + y : 60 + ca + y);
+      if (jc >= n) continue;
+      const int pair = (y < 4 ? 0 : 2) + ((y & 3) >> 1);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i0 = p0 + h * 64 + ra;
+        float v[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const float2 a = acc[4 * h + x][pair];
+          v[x] = (y & 1) ? a.y : a.x;
+        }
+        float* g = Sm + (int64_t)jc * n + i0;
+        if (vst && i0 + 3 < n) {
+          *reinterpret_cast<float4*>(g) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+          for (int x = 0; x < 4; ++x)
+            if (i0 + x < n) g[x] = v[x];
+        }
+      }
+    }
+  }
+}
+
+template <bool VEC, bool BIG>
 int launch_gram_t(const float* G, int64_t sGb, int64_t ldg, float* S, int64_t batch, int n, int k,
                   cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;
+  auto kern = BIG ? k_gram128<VEC> : k_gram<VEC>;
+  const size_t smem = BIG ? sizeof(SmemGram128) : sizeof(SmemGram);
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(k_gram<VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(SmemGram)) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
       return QRB_ERR_LAUNCH;
     attr_set[dev] = true;
   }
-  const int nt = (n + TS - 1) / TS;
+  const int tile = BIG ? TB : TS;
+  const int nt = (n + tile - 1) / tile;
   const unsigned tiles = (unsigned)(nt * (nt + 1) / 2);
   constexpr int64_t kMaxGridY = 65535;
   for (int64_t b0 = 0; b0 < batch; b0 += kMaxGridY) {
     const int64_t nb = batch - b0 < kMaxGridY ? batch - b0 : kMaxGridY;
-    k_gram<VEC><<<dim3(tiles, (unsigned)nb, 1), NT, sizeof(SmemGram), stream>>>(
-        G + b0 * sGb, sGb, ldg, S + b0 * (int64_t)n * n, n, k, nt);
+    kern<<<dim3(tiles, (unsigned)nb, 1), NT, smem, stream>>>(G + b0 * sGb, sGb, ldg,
+                                                             S + b0 * (int64_t)n * n, n, k, nt);
     note_launches(1);
     if (cudaGetLastError() != cudaSuccess) return QRB_ERR_LAUNCH;
   }
@@ -253,8 +431,13 @@ int launch_gram(const float* G, int64_t sGb, int64_t ldg, float* S, int64_t batc
                 cudaStream_t stream) {
   const bool vec = (reinterpret_cast<uintptr_t>(G) & 15) == 0 && ldg % 4 == 0 &&
                    (batch == 1 || sGb % 4 == 0) && k % 4 == 0;
-  return vec ? launch_gram_t<true>(G, sGb, ldg, S, batch, n, k, stream)
-             : launch_gram_t<false>(G, sGb, ldg, S, batch, n, k, stream);
+  const int pref = gram_tile();
+  const bool big = pref == 128 || (pref == 0 && n > kGramBigTileMinN);
+  if (big)
+    return vec ? launch_gram_t<true, true>(G, sGb, ldg, S, batch, n, k, stream)
+               : launch_gram_t<false, true>(G, sGb, ldg, S, batch, n, k, stream);
+  return vec ? launch_gram_t<true, false>(G, sGb, ldg, S, batch, n, k, stream)
+             : launch_gram_t<false, false>(G, sGb, ldg, S, batch, n, k, stream);
 }
 
 bool bad_gram_args(const float* G, int64_t sGb, int64_t ldg, const void* out, int64_t batch,

@@ -227,6 +227,12 @@ def test_config_keys():
         assert _lib.get_config("panel_rpt") == v
     with pytest.raises(_lib.QRBError):
         _lib.set_config("panel_rpt", 3)
+    assert _lib.get_config("gram_tile") == 0
+    for v in (64, 128, 0):
+        _lib.set_config("gram_tile", v)
+        assert _lib.get_config("gram_tile") == v
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("gram_tile", 32)
     assert _lib.get_config("mid_fused") == 1
     _lib.set_config("mid_fused", 0)
     assert _lib.get_config("mid_fused") == 0

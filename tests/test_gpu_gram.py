@@ -13,7 +13,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from gpumode_qr_b200 import api, checker
+from gpumode_qr_b200 import _lib, api, checker
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
@@ -25,10 +25,18 @@ def _gram64(G: torch.Tensor) -> torch.Tensor:
     return g @ g.transpose(-1, -2)
 
 
+@pytest.fixture(params=[0, 64, 128], ids=["auto", "tile64", "tile128"])
+def gram_tile(request):
+    old = _lib.get_config("gram_tile")
+    _lib.set_config("gram_tile", request.param)
+    yield request.param
+    _lib.set_config("gram_tile", old)
+
+
 @pytest.mark.parametrize("b,n,k", [(3, 64, 64), (2, 100, 37), (4, 512, 512), (2, 130, 1000),
                                    (1, 32, 4096), (5, 1, 7), (3, 200, 4), (2, 65, 33),
-                                   (64, 32, 128), (1, 1000, 96)])
-def test_gram_matches_fp64(b, n, k):
+                                   (64, 32, 128), (1, 1000, 96), (2, 129, 64), (1, 257, 40)])
+def test_gram_matches_fp64(b, n, k, gram_tile):
     G = torch.randn(b, n, k, generator=torch.Generator().manual_seed(b * 1000 + n + k))
     S = api.gram(G.to(DEV))
     torch.cuda.synchronize()
