@@ -352,6 +352,47 @@ def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
     return res
 
 
+def gram_sweep(dev, flush_buf) -> dict:
+    """The statistics step in front of the factorization (S = G G^T, then QR of
+    S) at the shape the reference's task statement singles out (batched
+    512 x 512, contracted dimension 512): kernel time, FP32 roofline fraction
+    of the Gram kernel (n (n + 1) k FLOPs per matrix, the symmetric count),
+    Gram + factorization time, cuBLAS FP32 G @ G.mT (TF32 off) on the same GPU,
+    and FP64 parity of S on four matrices."""
+    import torch
+
+    from gpumode_qr_b200 import api
+
+    b, n, k = 640, 512, 512
+    g = torch.Generator().manual_seed(7)
+    G_cpu = torch.randn(b, n, k, generator=g)
+    G = G_cpu.to(dev)
+    stream = torch.cuda.current_stream(dev)
+    S = api.gram(G)
+    ms = statistics.median(time_device_steps(lambda: api.gram(G), 10, 3, flush_buf, stream))
+    ms_qr = statistics.median(time_device_steps(lambda: api.gram_geqrf(G), 5, 2, flush_buf, stream))
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ms_torch = statistics.median(
+            time_device_steps(lambda: torch.matmul(G, G.mT), 10, 3, flush_buf, stream))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old_tf32
+    g64 = G_cpu[:4].double()
+    want = g64 @ g64.transpose(-1, -2)
+    err = float((S[:4].double().cpu() - want).abs().max() / want.abs().max())
+    flops = b * n * (n + 1) * k
+    tf = flops / (ms / 1e3) / 1e12
+    del G, S
+    torch.cuda.empty_cache()
+    return {"workload": f"gram_b{b}_n{n}_k{k}", "gram_ms": ms, "gram_geqrf_ms": ms_qr,
+            "torch_fp32_matmul_ms": ms_torch,
+            "roofline": {"bound": "fp32_ffma", "achieved": tf, "peak": FP32_FFMA_NOMINAL_TFLOPS,
+                         "unit": "TFLOP/s", "frac": tf / FP32_FFMA_NOMINAL_TFLOPS,
+                         "flops_per_matrix": n * (n + 1) * k},
+            "s_rel_err_vs_fp64": err}
+
+
 def pcie_probe(A_host, H_host, A_dev, H_dev, dev, reps: int = 10) -> dict:
     """Copy-engine bandwidth of this box for the e2e step's buffers: one
     host-to-device copy, one device-to-host copy, and both at once on two
@@ -504,6 +545,7 @@ def run_ours(args, info) -> int:
     extra = {}
     if info.rank == 0 and world == 1 and not args.no_configs:
         extra["per_config"] = per_config_sweep(dev, flush_buf, not args.no_cpu, peaks)
+        extra["gram"] = gram_sweep(dev, flush_buf)
     cpu = None
     if info.rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_geqrf_rate(A_cpu, args.cpu_seconds)
