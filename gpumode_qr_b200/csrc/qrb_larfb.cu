@@ -4,7 +4,7 @@
 // three products of the reference's trailing update (src/qrbench/variants.py
 // :800-804, W1 = V^T C, W2 = T^T W1, C -= V W2) without writing the k x 64
 // intermediate to global memory:
-//   pass 1  W = V^T C over all r rows: 64-row chunks of V and C double-buffered
+//   pass 1  W = V^T C over all r rows: 96-row chunks of V and C double-buffered
 //           into shared memory with cp.async; each warp takes every 8th row
 //           and each lane accumulates an 8 x 8 register block of W (32 packed
 //           FP32x2 FMAs per four 16-byte shared loads); the eight warp
@@ -30,7 +30,7 @@ constexpr int K = 32;        // reflectors per block (padded)
 constexpr int TC = 64;       // columns of C per CTA
 constexpr int NT = 256;      // threads per CTA (8 warps)
 constexpr int NW = NT / 32;
-constexpr int RC1 = 64;      // rows per pass-1 chunk
+constexpr int RC1 = 96;      // rows per pass-1 chunk
 constexpr int RC2 = 256;     // rows per pass-2 chunk
 constexpr int VS_LD = K + 4;     // pass-1 V chunk row stride (floats)
 constexpr int CS_LD = TC + 4;    // pass-1 C chunk row stride
