@@ -9,11 +9,14 @@
 //           and each lane accumulates an 8 x 8 register block of W (32 packed
 //           FP32x2 FMAs per four 16-byte shared loads); the eight warp
 //           partials are summed, then W <- T^T W is formed;
-//   pass 2  C -= V W over 256-row chunks: V is staged transposed in shared
-//           memory (negated) and each thread updates an 8-row x 8-column block
-//           of C in registers with packed FMAs (columns c, c+1, c+2, c+3 and
-//           c+32..c+35, so that a warp's global loads and stores cover whole
-//           128-byte rows).
+//   pass 2  C -= V W over 256-row chunks: each thread updates an 8-row x
+//           8-column block of C in registers with packed FMAs (columns c, c+1,
+//           c+2, c+3 and c+32..c+35, so that a warp's global loads and stores
+//           cover whole 128-byte rows). With 16-byte aligned operands V is
+//           staged row-major by cp.async (double-buffered, the first chunk
+//           requested before W <- T^T W; 16-byte units swizzled by row group)
+//           and W is stored negated; otherwise V is staged transposed and
+//           negated through registers.
 // V is read through its strictly lower part only: the diagonal is taken as 1
 // and everything above it as 0 (so V can point into a packed H), columns at or
 // beyond k as 0.
@@ -46,7 +49,8 @@ struct __align__(16) Smem {
   union {
     Stage st;                 // pass 1 staging
     float Wp[NW][K * TC];     // per-warp partial W (after pass 1)
-    float Vt[K * VT_LD];      // pass 2 transposed V chunk
+    float Vt[K * VT_LD];      // pass 2 transposed V chunk (unaligned operands)
+    float Vr[2][RC2 * K];     // pass 2 V chunks as loaded, 16-byte units swizzled
   } u;
   float Ws[K * WS_LD];
   float Ts[K * T_LD];
@@ -66,6 +70,7 @@ struct __align__(1024) SmemTc {
     Stage st;
     float Wp[NW][K * TC];
     unsigned char A[2][2][A2T_BYTES];       // [buffer][hi, lo]
+    float Vr[2][RC2 * K];                   // (FFMA pass 2 only; keeps one code path)
   } u;
   unsigned char B[2][B2T_BYTES];            // [hi, lo]
   float Ws[K * WS_LD];
@@ -396,6 +401,24 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
     *reinterpret_cast<float4*>(ws + 4) = s1;
   }
   __syncthreads();
+  // Pass 2 (FFMA, aligned operands) stages V row-major with cp.async: row i of
+  // a chunk keeps its eight 16-byte units at positions u ^ ((i / 8) % 8), so
+  // that the eight-row groups a warp reads at once fall on distinct banks.
+  // The first chunk is requested here, before T^T W (the partials are summed).
+  auto issue_v2 = [&](int i0, int buf) {
+#pragma unroll
+    for (int e = 0; e < (RC2 * K) / (4 * NT); ++e) {
+      const int idx = tid + e * NT;
+      const int row = idx >> 3, u = idx & 7;
+      const int i = i0 + row;
+      const bool ok = i < r;
+      const float* g = ok ? Vm + (int64_t)i * ldv + 4 * u : Vm;
+      cp_async16(&sm.u.Vr[buf][row * K + ((u ^ ((row >> 3) & 7)) << 2)], g, ok);
+    }
+    cp_async_commit();
+  };
+  constexpr bool kRowMajorP2 = VEC && !TCP2;
+  if constexpr (kRowMajorP2) issue_v2(0, 0);
   {
     const int cc = tid & 63;
     const int ab = (tid >> 6) << 3;
@@ -409,12 +432,87 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
       for (int x = 0; x < 8; ++x) o[x] = fmaf(sm.Ts[q * T_LD + ab + x], wq, o[x]);
     }
     __syncthreads();  // every thread has read the sums in Ws
+    // stored negated for the row-major pass 2 (C += V (-W') is a plain FMA)
+    const float sg = kRowMajorP2 ? -1.f : 1.f;
 #pragma unroll
-    for (int x = 0; x < 8; ++x) sm.Ws[(ab + x) * WS_LD + cc] = o[x];
+    for (int x = 0; x < 8; ++x) sm.Ws[(ab + x) * WS_LD + cc] = sg * o[x];
   }
 
   if constexpr (TCP2) {
     pass2_tc(sm, Vm, ldv, Cm, ldcs, Dm, ldcd, r, c, c0, tid, warp, lane, err);
+  } else if constexpr (kRowMajorP2) {
+  // ---------------- pass 2: C += V (-W'), V row-major ----------------
+  const int rg = (tid >> 3) << 3;   // chunk rows rg..rg+7
+  const int cq = (tid & 7) << 2;    // tile cols cq..cq+3 and cq+32..cq+35
+  const int sw = (tid >> 3) & 7;    // swizzle of rows rg..rg+7
+  const int colA = c0 + cq, colB = c0 + cq + 32;
+  int it = 0;
+  for (int i0 = 0; i0 < r; i0 += RC2, ++it) {
+    const int buf = it & 1;
+    __syncthreads();  // W' ready (first) / the other V buffer consumed (later)
+    if (i0 + RC2 < r) {
+      issue_v2(i0 + RC2, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    float2 cv[8][4];
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+      const int i = i0 + rg + x;
+      const float* g = Cm + (int64_t)i * ldcs;
+      float4 ta = make_float4(0.f, 0.f, 0.f, 0.f), tb = ta;
+      if (i < r && colA < c) ta = *reinterpret_cast<const float4*>(g + colA);
+      if (i < r && colB < c) tb = *reinterpret_cast<const float4*>(g + colB);
+      cv[x][0] = make_float2(ta.x, ta.y); cv[x][1] = make_float2(ta.z, ta.w);
+      cv[x][2] = make_float2(tb.x, tb.y); cv[x][3] = make_float2(tb.z, tb.w);
+    }
+    __syncthreads();  // this chunk of V has landed for every thread
+    if (i0 == 0) {  // unit-lower mask on the top rows (k == 32 here)
+      for (int e = tid; e < K * K; e += NT) {
+        const int row = e >> 5, a = e & 31;
+        if (row <= a)
+          sm.u.Vr[buf][row * K + (((a >> 2) ^ ((row >> 3) & 7)) << 2) + (a & 3)] =
+              row == a ? 1.f : 0.f;
+      }
+      __syncthreads();
+    }
+    const float* vb = sm.u.Vr[buf];
+#pragma unroll 2
+    for (int a4 = 0; a4 < K / 4; ++a4) {
+      float4 vq[8];
+#pragma unroll
+      for (int x = 0; x < 8; ++x)
+        vq[x] = *reinterpret_cast<const float4*>(vb + (rg + x) * K + ((a4 ^ sw) << 2));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int a = 4 * a4 + u;
+        const float4 wA = *reinterpret_cast<const float4*>(&sm.Ws[a * WS_LD + cq]);
+        const float4 wB = *reinterpret_cast<const float4*>(&sm.Ws[a * WS_LD + cq + 32]);
+        const float2 wp[4] = {make_float2(wA.x, wA.y), make_float2(wA.z, wA.w),
+                              make_float2(wB.x, wB.y), make_float2(wB.z, wB.w)};
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+          const float v = u == 0 ? vq[x].x : u == 1 ? vq[x].y : u == 2 ? vq[x].z : vq[x].w;
+          const float2 vx = make_float2(v, v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) cv[x][j] = __ffma2_rn(vx, wp[j], cv[x][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+      const int i = i0 + rg + x;
+      if (i >= r) continue;
+      float* g = Dm + (int64_t)i * ldcd;
+      if (colA < c)
+        *reinterpret_cast<float4*>(g + colA) =
+            make_float4(cv[x][0].x, cv[x][0].y, cv[x][1].x, cv[x][1].y);
+      if (colB < c)
+        *reinterpret_cast<float4*>(g + colB) =
+            make_float4(cv[x][2].x, cv[x][2].y, cv[x][3].x, cv[x][3].y);
+    }
+  }
   } else {
   // ---------------- pass 2: C -= V W ----------------
   const int rg = (tid >> 3) << 3;   // chunk rows rg..rg+7
