@@ -7,7 +7,10 @@
 //
 // Thread t keeps column t in registers as NP / 2 row pairs, plus copies of its
 // diagonal element a_tt and sub-diagonal element a_(t+1)t in scalars (updated
-// alongside, bit for bit). Column step J (a runtime loop, one block barrier):
+// alongside, bit for bit). The column steps run as runtime loops in phases of
+// 16 (J in [16 P, 16 P + 16)), each phase compiled with its own static row
+// range (rows from 16 P: above them u is zero), so the work per step shrinks
+// as the factorization proceeds. Column step J (one block barrier):
 //   owner t = J  forms the reflector from alpha = a_JJ and sigma (its
 //                look-ahead sum), and publishes u with u_i = 0 above J,
 //                u_J = alpha - beta and u_i = x_i below J (so v = scale * u)
@@ -21,6 +24,8 @@
 // alpha - beta), so the buffer holds zeros above J without a runtime index
 // into the register array. A finished column keeps x unscaled; it is scaled
 // once when H is stored (deferred scaling), with beta on the diagonal.
+#include <type_traits>
+
 #include "qrb_common.cuh"
 
 namespace qrb {
@@ -58,11 +63,13 @@ k_fused_cta(const float* __restrict__ A, int64_t sAb, int64_t sAr, float* __rest
 
   // sigma of this thread's column below its diagonal: pairs past the one
   // holding row t, plus row t + 1 when it shares that pair with row t.
-  auto below_diag_sumsq = [&]() {
+  // (pairs before QS are known to lie at or above the diagonal: t >= 2 QS)
+  auto below_diag_sumsq = [&](auto qs) {
+    constexpr int QS = decltype(qs)::value;
     const int q0 = t >> 1;
     float2 s2 = make_float2(0.f, 0.f), s3 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int q = 0; q < NQ; ++q) {
+    for (int q = QS; q < NQ; ++q) {
       if (q > q0) {
         if (q & 1)
           s3 = __ffma2_rn(a[q], a[q], s3);
@@ -74,70 +81,89 @@ k_fused_cta(const float* __restrict__ A, int64_t sAb, int64_t sAr, float* __rest
     if ((t & 1) == 0) s = fmaf(sub, sub, s);
     return s;
   };
-  float sig = (t == 0) ? below_diag_sumsq() : 0.f;
+  float sig = (t == 0) ? below_diag_sumsq(std::integral_constant<int, 0>{}) : 0.f;
   __syncthreads();  // buffers zeroed before the first owner writes
 
+  // Column steps in phases of 16: in phase P every step has J >= 16 P, so rows
+  // above 16 P hold u = 0 and are skipped at compile time (row pairs from 8 P,
+  // 16-byte groups from 4 P); the skipped terms were exact zeros.
+  auto phase = [&](auto pc) {
+    constexpr int P = decltype(pc)::value;
+    if constexpr (P < NP / 16) {
+      constexpr int QS = 8 * P;  // first row pair
+      constexpr int GS = 4 * P;  // first 4-row group
+      const int j_end = min(16 * (P + 1), n - 1);
 #pragma unroll 1
-  for (int J = 0; J < n - 1; ++J) {
-    const int par = J & 1;
-    float* ub = ubuf[par];
-    if (t == J) {
-      const Reflector h = make_reflector(diag, sig);
-      const float ujj = diag - h.beta;
-      const unsigned us = (unsigned)__cvta_generic_to_shared(ub);
-      // rows from the 4-group holding row J + 1 on (the group may include rows
-      // <= J; they are fixed below)
+      for (int J = 16 * P; J < j_end; ++J) {
+        const int par = J & 1;
+        float* ub = ubuf[par];
+        if (t == J) {
+          const Reflector h = make_reflector(diag, sig);
+          const float ujj = diag - h.beta;
+          const unsigned us = (unsigned)__cvta_generic_to_shared(ub);
+          // rows from the 4-group holding row J + 1 on (the group may include
+          // rows <= J; they are fixed below)
 #pragma unroll
-      for (int g = 0; g < NP / 4; ++g) {
-        const unsigned on = (4 * g + 3 > J) ? 1u : 0u;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %0, 0;\n\t"
-            "@p st.shared.v4.f32 [%1], {%2, %3, %4, %5};\n\t}\n" ::"r"(on),
-            "r"(us + 16u * g), "f"(a[2 * g].x), "f"(a[2 * g].y), "f"(a[2 * g + 1].x),
-            "f"(a[2 * g + 1].y)
-            : "memory");
+          for (int g = GS; g < NP / 4; ++g) {
+            const unsigned on = (4 * g + 3 > J) ? 1u : 0u;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %0, 0;\n\t"
+                "@p st.shared.v4.f32 [%1], {%2, %3, %4, %5};\n\t}\n" ::"r"(on),
+                "r"(us + 16u * g), "f"(a[2 * g].x), "f"(a[2 * g].y), "f"(a[2 * g + 1].x),
+                "f"(a[2 * g + 1].y)
+                : "memory");
+          }
+          // rows J-3 .. J-1 to zero (stale from two steps ago or written
+          // above), row J to alpha - beta
+#pragma unroll
+          for (int d = 3; d >= 1; --d)
+            if (J - d >= 0) ub[J - d] = 0.f;
+          ub[J] = ujj;
+          coef[par][0] = h.tau;
+          coef[par][1] = h.scale;
+          mt[J] = h.tau;
+          mb[J] = h.beta;
+          ms[J] = h.scale;
+        }
+        __syncthreads();
+        const float tau = coef[par][0];
+        const float scale = coef[par][1];
+        float2 d0 = make_float2(0.f, 0.f), d1 = d0, d2 = d0, d3 = d0;
+#pragma unroll
+        for (int g = GS; g < NQ / 2; ++g) {
+          const float4 u = reinterpret_cast<const float4*>(ub)[g];
+          if (g & 1) {
+            d2 = __ffma2_rn(make_float2(u.x, u.y), a[2 * g], d2);
+            d3 = __ffma2_rn(make_float2(u.z, u.w), a[2 * g + 1], d3);
+          } else {
+            d0 = __ffma2_rn(make_float2(u.x, u.y), a[2 * g], d0);
+            d1 = __ffma2_rn(make_float2(u.z, u.w), a[2 * g + 1], d1);
+          }
+        }
+        const float dsum = ((d0.x + d0.y) + (d1.x + d1.y)) + ((d2.x + d2.y) + (d3.x + d3.y));
+        const float f = (t > J && col) ? tau * (scale * dsum) : 0.f;
+        const float ng = -(f * scale);
+        const float2 ng2 = make_float2(ng, ng);
+#pragma unroll
+        for (int g = GS; g < NQ / 2; ++g) {
+          const float4 u = reinterpret_cast<const float4*>(ub)[g];
+          a[2 * g] = __ffma2_rn(ng2, make_float2(u.x, u.y), a[2 * g]);
+          a[2 * g + 1] = __ffma2_rn(ng2, make_float2(u.z, u.w), a[2 * g + 1]);
+        }
+        diag = fmaf(ng, ub[t], diag);
+        if (t + 1 < NP) sub = fmaf(ng, ub[t + 1], sub);
+        if (t == J + 1) sig = below_diag_sumsq(std::integral_constant<int, QS>{});
       }
-      // rows J-3 .. J-1 to zero (stale from two steps ago or written above),
-      // row J to alpha - beta
-#pragma unroll
-      for (int d = 3; d >= 1; --d)
-        if (J - d >= 0) ub[J - d] = 0.f;
-      ub[J] = ujj;
-      coef[par][0] = h.tau;
-      coef[par][1] = h.scale;
-      mt[J] = h.tau;
-      mb[J] = h.beta;
-      ms[J] = h.scale;
     }
-    __syncthreads();
-    const float tau = coef[par][0];
-    const float scale = coef[par][1];
-    float2 d0 = make_float2(0.f, 0.f), d1 = d0, d2 = d0, d3 = d0;
-#pragma unroll
-    for (int g = 0; g < NQ / 2; ++g) {
-      const float4 u = reinterpret_cast<const float4*>(ub)[g];
-      if (g & 1) {
-        d2 = __ffma2_rn(make_float2(u.x, u.y), a[2 * g], d2);
-        d3 = __ffma2_rn(make_float2(u.z, u.w), a[2 * g + 1], d3);
-      } else {
-        d0 = __ffma2_rn(make_float2(u.x, u.y), a[2 * g], d0);
-        d1 = __ffma2_rn(make_float2(u.z, u.w), a[2 * g + 1], d1);
-      }
-    }
-    const float dsum = ((d0.x + d0.y) + (d1.x + d1.y)) + ((d2.x + d2.y) + (d3.x + d3.y));
-    const float f = (t > J && col) ? tau * (scale * dsum) : 0.f;
-    const float ng = -(f * scale);
-    const float2 ng2 = make_float2(ng, ng);
-#pragma unroll
-    for (int g = 0; g < NQ / 2; ++g) {
-      const float4 u = reinterpret_cast<const float4*>(ub)[g];
-      a[2 * g] = __ffma2_rn(ng2, make_float2(u.x, u.y), a[2 * g]);
-      a[2 * g + 1] = __ffma2_rn(ng2, make_float2(u.z, u.w), a[2 * g + 1]);
-    }
-    diag = fmaf(ng, ub[t], diag);
-    if (t + 1 < NP) sub = fmaf(ng, ub[t + 1], sub);
-    if (t == J + 1) sig = below_diag_sumsq();
-  }
+  };
+  phase(std::integral_constant<int, 0>{});
+  phase(std::integral_constant<int, 1>{});
+  phase(std::integral_constant<int, 2>{});
+  phase(std::integral_constant<int, 3>{});
+  phase(std::integral_constant<int, 4>{});
+  phase(std::integral_constant<int, 5>{});
+  phase(std::integral_constant<int, 6>{});
+  phase(std::integral_constant<int, 7>{});
   __syncthreads();
 
   // H: R above the diagonal, beta on it, v = scale * x below; tau.
