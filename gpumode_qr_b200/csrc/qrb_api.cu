@@ -252,6 +252,7 @@ int host_direct_mode() { return (int)g_host_direct.load(); }
 bool host_ramp() { return g_host_ramp.load() != 0; }
 int fused_cpl() { return (int)g_fused_cpl.load(); }
 bool mid_fused_enabled() { return g_mid_fused.load() != 0; }
+bool mid_fused_always() { return g_mid_fused.load() == 2; }
 int panel_rpt() { return (int)g_panel_rpt.load(); }
 int gram_tile() { return (int)g_gram_tile.load(); }
 int64_t host_direct_blocks() {
@@ -279,11 +280,15 @@ FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch) {
 int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
                   const FactorScratch& ws, int64_t batch, int n, cudaStream_t s) {
   if (n <= kFusedMaxN) return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
-  // The CTA-per-matrix kernel is latency-friendly (one launch) but does about
-  // twice the blocked route's arithmetic: measured on B200 it wins at n <= 64
-  // for every batch (2x) and above n = 64 while the batch fits about two waves
-  // (1.2-1.4x at 8-200 matrices), and loses at 1024 x 96 (436 vs 271 us).
-  if (n <= kFusedMidMaxN && mid_fused_enabled() && (n <= 64 || batch <= kFusedMidMaxBatch))
+  // The CTA-per-matrix kernel is latency-friendly (one launch) but does more
+  // arithmetic than the blocked route and runs in waves of 296 CTAs (2 per SM
+  // at 128 threads). Measured on B200 it wins at n <= 64 for every batch, at
+  // 96 < n <= 128 for every batch (the blocked route needs four panels there:
+  // 1.08 vs 1.75 ms at 4096 x 97, 1.24 vs 1.59 ms at 4096 x 128), and at
+  // 64 < n <= 96 up to two waves (145 vs 160 us at 592 x 80; 233 vs 199 us at
+  // 740 x 96).
+  if (n <= kFusedMidMaxN && mid_fused_enabled() &&
+      (n <= 64 || n > 96 || batch <= kFusedMidMaxBatch || mid_fused_always()))
     return launch_fused_mid(A, strideA_b, strideA_row, H, tau, batch, n, s);
   if (ws.T == nullptr) return QRB_ERR_WORKSPACE;
   // Automatic: 4 groups from n = 1024 on (measured on B200: 30.6 vs 32.8 ms for
@@ -499,7 +504,7 @@ int qrb_set_config(const char* key, int64_t value) {
     return QRB_OK;
   }
   if (std::strcmp(key, "mid_fused") == 0) {
-    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
     g_mid_fused.store(value);
     return QRB_OK;
   }

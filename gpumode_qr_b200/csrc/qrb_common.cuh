@@ -12,7 +12,7 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kPanelW = 32;        // panel / block-reflector width
 constexpr int kFusedMaxN = 32;     // largest n of the warp-per-matrix kernel
 constexpr int kFusedMidMaxN = 128; // largest n of the CTA-per-matrix fused kernel
-constexpr int64_t kFusedMidMaxBatch = 592;  // above n = 64: about two waves of 2 CTAs per SM
+constexpr int64_t kFusedMidMaxBatch = 592;  // 64 < n <= 96: two waves of 2 CTAs per SM
 constexpr int kLookaheadMinN = 4096;  // automatic panel look-ahead from this n (measured on B200:
                                       // 29.7 vs 30.5 ms at 8 x 4096, slower at n = 512 and 1024)
 constexpr int kMaxN = 8192;        // 4096 rows per CTA-cluster of 8 x 512 x 2
@@ -87,10 +87,11 @@ int launch_fused_small(const float* A, int64_t sAb, int64_t sAr, float* H,
 // CTA-per-matrix fused QR for kFusedMaxN < n <= kFusedMidMaxN (one launch).
 int launch_fused_mid(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau,
                      int64_t batch, int n, cudaStream_t stream);
-// qrb_set_config("mid_fused"): 1 (default) = 32 < n <= 64, and 64 < n <= 128
-// up to kFusedMidMaxBatch matrices, run the CTA-per-matrix fused kernel;
-// 0 = always the blocked panel route.
+// qrb_set_config("mid_fused"): 1 (default) = 32 < n <= 64 and 96 < n <= 128,
+// and 64 < n <= 96 up to kFusedMidMaxBatch matrices, run the CTA-per-matrix
+// fused kernel; 2 = every 32 < n <= 128; 0 = always the blocked panel route.
 bool mid_fused_enabled();
+bool mid_fused_always();
 
 // Factor the r x w panel starting at (row 0, col 0) of src (row stride ld_src,
 // matrix stride sb_src) into dst; tau to tau_out[m*tau_sb + c]; T to

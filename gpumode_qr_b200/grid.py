@@ -48,7 +48,8 @@ def regime(batch: int, n: int, ms: float, peaks: dict) -> dict:
     floor_ms = max(t_hbm, t_flop) * 1e3
     return {
         "path": ("fused" if n <= 32 else
-                 "fused_cta" if n <= 128 and (n <= 64 or batch <= 592) else "blocked"),
+                 "fused_cta" if n <= 128 and (n <= 64 or n > 96 or batch <= 592) else
+                 "blocked"),
         "bound": bound,
         "floor_ms": floor_ms,
         "roofline_frac": floor_ms / ms if ms > 0 else None,

@@ -272,9 +272,11 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *   "panel_rpt"   rows per thread of the panel kernel: 0 (default) = 1 up to
  *                 128 rows, else 4; 1 or 2 force that many (CTAs of up to 512
  *                 or 256 threads; 4 where more than 8 CTAs would be needed).
- *   "mid_fused"   1 (default): 32 < n <= 64, and 64 < n <= 128 up to 592
- *                 matrices, are factored by one CTA per matrix in one launch;
- *                 0: always the blocked panel route above n = 32.
+ *   "mid_fused"   1 (default): 32 < n <= 64 and 96 < n <= 128, and
+ *                 64 < n <= 96 up to 592 matrices, are factored by one CTA per
+ *                 matrix in one launch;
+ *                 2: every 32 < n <= 128 that way; 0: always the blocked panel
+ *                 route above n = 32.
  *   "fused_cpl"   n <= 32 kernel: 2 or 4 matrices per warp, 0 (default) = 4 up
  *                 to 4736 matrices, else 2. Results are identical either way.
  *   "host_ramp"   1: qrb_geqrf_f32_host cuts the batch into pieces of relative

@@ -236,9 +236,11 @@ def test_config_keys():
     assert _lib.get_config("mid_fused") == 1
     _lib.set_config("mid_fused", 0)
     assert _lib.get_config("mid_fused") == 0
+    _lib.set_config("mid_fused", 2)
+    assert _lib.get_config("mid_fused") == 2
     _lib.set_config("mid_fused", 1)
     with pytest.raises(_lib.QRBError):
-        _lib.set_config("mid_fused", 2)
+        _lib.set_config("mid_fused", 3)
     assert _lib.get_config("fused_cpl") == 0
     _lib.set_config("fused_cpl", 4)
     assert _lib.get_config("fused_cpl") == 4
