@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """Generate the golden fixtures in this directory from the reference itself.
 
-Run once, in a checkout that has the reference ``gpumode_qr`` source tree
-(path from ``--reference``, default ``/root/reference``); the fixtures are
+Run once, on a machine that has the reference ``gpumode_qr`` source tree
+(``--reference PATH``, the checkout's root directory); the fixtures are
 committed and the tests never need the reference at run time.
 
 Sources of truth:
@@ -33,7 +33,8 @@ REPO = HERE.parents[1]
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root directory of the reference gpumode_qr checkout")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
     sys.path.insert(0, str(REPO))
