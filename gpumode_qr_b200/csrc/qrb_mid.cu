@@ -18,7 +18,9 @@
 //   all t > J    d = scale * sum_i u_i a_i,  a_i -= (tau d scale) u_i over the
 //                whole padded row range (rows above J see u_i = 0, row J
 //                loses tau d), with the packed FP32x2 FMA;
-//   thread J+1   forms sigma_(J+1) = sum_{i > J+1} a_i^2 for the next step.
+//   thread J+1   keeps sigma_(J+1) = sum_{i > J+1} a_i^2 for the next step,
+//                accumulated (by every thread, for its own column) inside
+//                the update loop.
 // The owner writes u with 16-byte stores of its row pairs from the group that
 // holds row J + 1 on, then fixes rows J-3 .. J with scalar stores (zeros and
 // alpha - beta), so the buffer holds zeros above J without a runtime index
@@ -144,15 +146,27 @@ k_fused_cta(const float* __restrict__ A, int64_t sAb, int64_t sAr, float* __rest
         const float f = (t > J && col) ? tau * (scale * dsum) : 0.f;
         const float ng = -(f * scale);
         const float2 ng2 = make_float2(ng, ng);
+        // the next owner's norm below its diagonal (pairs past t / 2, plus
+        // row t + 1 for even t), accumulated as the pairs are updated, in the
+        // order of below_diag_sumsq; every thread computes it, thread J + 1
+        // keeps it
+        const int q0 = t >> 1;
+        float2 s2 = make_float2(0.f, 0.f), s3 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int g = GS; g < NQ / 2; ++g) {
           const float4 u = reinterpret_cast<const float4*>(ub)[g];
           a[2 * g] = __ffma2_rn(ng2, make_float2(u.x, u.y), a[2 * g]);
           a[2 * g + 1] = __ffma2_rn(ng2, make_float2(u.z, u.w), a[2 * g + 1]);
+          if (2 * g > q0) s2 = __ffma2_rn(a[2 * g], a[2 * g], s2);
+          if (2 * g + 1 > q0) s3 = __ffma2_rn(a[2 * g + 1], a[2 * g + 1], s3);
         }
         diag = fmaf(ng, ub[t], diag);
         if (t + 1 < NP) sub = fmaf(ng, ub[t + 1], sub);
-        if (t == J + 1) sig = below_diag_sumsq(std::integral_constant<int, QS>{});
+        if (t == J + 1) {
+          float sq = (s2.x + s2.y) + (s3.x + s3.y);
+          if ((t & 1) == 0) sq = fmaf(sub, sub, sq);
+          sig = sq;
+        }
       }
     }
   };
