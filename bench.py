@@ -3,15 +3,19 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step is one factorization of one batch of the workload config (default:
-config 2, b=4096 n=32 iid N(0,1) seed 1) per rank. Scaling is weak: every rank
-factors its own shard of ``N x batch`` matrices (rank r takes matrices
-[r*b, (r+1)*b) of the seeded global batch); there is no collective on the hot
-path. Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA
-events on the launching stream, with a 256 MiB write between steps to flush L2
-(the workload fits in L2). The timed region is bracketed by a barrier and
+A step is one factorization of one batch of the workload config. The default
+workload is config 5 (b=8, n=4096, iid N(0,1), seed 4): the largest
+single-GPU config of the metric. Scaling is strong by default: the config's
+fixed global batch is sharded across the N ranks (``sharding.shard_range``;
+config 5 gives one matrix per GPU at N=8), with no collective on the hot path;
+``--scaling weak`` instead gives every rank a full batch of its own. Timing: W
+untimed warm-up steps, then K steps, each bracketed by CUDA events on the
+launching stream, with a 256 MiB write between steps to flush L2 (outside the
+events). The timed region is bracketed by a barrier and
 ``torch.cuda.synchronize()``; the reported time is the MAX over ranks of the
-summed step times. Rank 0 prints one JSON line.
+summed step times. Rank 0 prints one JSON line. At N > 1 the line also carries
+a strong-scaling sweep of configs 1-4 (``strong``); at N = 1 a per-config
+sweep with gates, parity and CPU times (``per_config``).
 
 ``--impl reference`` times the reference's own CPU implementation of the path,
 ``torch.geqrf`` on the host cores (``src/qrbench/reference.py:18-20``), on the
@@ -42,22 +46,37 @@ FP32_FFMA_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # at clocks.max.sm
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--config", type=int, default=2, help="workload config index (1-5)")
-    ap.add_argument("--no-configs", action="store_true", help="skip the per-config sweep")
+    ap.add_argument("--config", type=int, default=5, help="workload config index (1-5)")
+    ap.add_argument("--scaling", choices=("strong", "weak"), default="strong",
+                    help="strong: shard the config's batch over the ranks; weak: a batch per rank")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-config sweeps")
     ap.add_argument("--no-cpu", action="store_true", help="skip CPU geqrf timings")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget")
-    ap.add_argument("--larfb-kind", type=int, default=None, choices=(0, 1, 2),
-                    help="trailing update: 0 FFMA (default), 1 tcgen05 3xTF32, 2 FFMA + tcgen05")
+    ap.add_argument("--set", action="append", default=[], metavar="KEY=VALUE",
+                    help="library test hook (qrb_set_config) applied before timing; repeatable")
     ap.add_argument("--chunks", type=int, default=0,
-                    help="e2e pipeline depth for qrb_geqrf_f32_host (0 = 6 for n <= 64, else 4)")
+                    help="e2e pipeline depth for qrb_geqrf_f32_host (0 = automatic)")
     ap.add_argument("--batch", type=int, default=None,
-                    help="matrices per GPU (default: the config's batch); for small profiling cases")
+                    help="global batch (default: the config's batch); for small profiling cases")
+    ap.add_argument("--workload", choices=("geqrf", "gram"), default="geqrf",
+                    help="gram: time the statistics step S = G G^T (b=--batch or 640, n=k=512)")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed steps only: no gate, e2e, CPU baseline or sweep (profiling)")
     return ap.parse_args(argv)
+
+
+def apply_hooks(items) -> dict:
+    from gpumode_qr_b200 import _lib
+
+    out = {}
+    for it in items:
+        key, _, val = it.partition("=")
+        _lib.set_config(key.strip(), int(val))
+        out[key.strip()] = int(val)
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -141,15 +160,49 @@ def measured_peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d.get("hbm_gbs"), "bf16_tflops": d.get("bf16_tflops"), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": d.get("hbm_gbs"), "bf16_tflops": d.get("bf16_tflops"),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
 
 
-def profile_traffic(workload: str):
+def flop_peak(route: str, peaks: dict) -> tuple[float, str, str]:
+    """(peak TFLOP/s, bound, derivation) of the pipe a large-n route computes on.
+
+    The tensor-core routes run 3xTF32: three TF32 MMAs per FP32 product, and
+    B200's dense TF32 rate is half its BF16 rate, so the effective peak is the
+    BF16 figure / 6. The FFMA routes have no measured FP32 figure, so the
+    nominal CUDA-core rate is used."""
+    if "tcgen05" in route:
+        bf16 = peaks["bf16_tflops"]
+        return (bf16 / 6.0, "tensor",
+                f"{peaks['source']} bf16 burst {bf16} TFLOP/s / 2 (tf32 rate) / 3 (3xTF32 products)")
+    return (FP32_FFMA_NOMINAL_TFLOPS, "fp32_ffma",
+            "nominal 148 SMs x 128 FFMA x 2 x 1965 MHz (no measured FP32 figure)")
+
+
+def profile_record(workload: str):
+    """Per-workload figures taken from committed ncu summaries under profiles/
+    (DRAM traffic per launch of the dominant kernel, its share of the launch
+    list), or None."""
     p = REPO / "profiles" / "roofline_traffic.json"
     if not p.exists():
         return None
-    return json.loads(p.read_text()).get(workload)
+    rec = json.loads(p.read_text()).get(workload)
+    return rec if isinstance(rec, dict) else None
+
+
+def config_dict(cfg, global_batch: int, scaling: str) -> dict:
+    """The workload description, identical in both arms."""
+    inp = ("iid N(0,1)" if cfg.kind == "iid" else
+           f"U diag(logspace(0, {cfg.log10_cond:g}, n)) V^T, U and V Haar")
+    return {"workload": f"cfg{cfg.index}_b{global_batch}_n{cfg.n}", "global_batch": global_batch,
+            "n": cfg.n, "seed": cfg.seed, "inputs": inp, "scaling": scaling}
+
+
+def global_batch_of(args, cfg, world: int) -> int:
+    b = cfg.batch if args.batch is None else args.batch
+    return b * world if args.scaling == "weak" else b
 
 
 # ---------------------------------------------------------------------------
@@ -161,7 +214,7 @@ def cpu_geqrf_rate(A_cpu, budget_s: float, min_reps: int = 2, max_reps: int = 20
     import torch
 
     torch.set_num_threads(os.cpu_count() or 1)
-    torch.geqrf(A_cpu[: min(A_cpu.shape[0], 64)])  # warm-up (threads, MKL init)
+    torch.geqrf(A_cpu[:1])  # warm-up (threads, MKL init)
     times = []
     t_end = time.perf_counter() + budget_s
     while len(times) < max_reps and (len(times) < min_reps or time.perf_counter() < t_end):
@@ -202,7 +255,8 @@ def run_reference(args, info) -> int:
     import torch
 
     cfg = inputs.config(args.config)
-    A = inputs.make_config_input(cfg)
+    gb = global_batch_of(args, cfg, info.world)
+    A = inputs.make_config_input(cfg, gb)
     torch.set_num_threads(os.cpu_count() or 1)
     for _ in range(max(1, min(args.warmup, 3))):
         torch.geqrf(A)
@@ -218,7 +272,7 @@ def run_reference(args, info) -> int:
         torch.geqrf(A)
         times.append(time.perf_counter() - t0)
     total = sum(times)
-    value = cfg.batch * steps / total
+    value = gb * steps / total
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -230,18 +284,19 @@ def run_reference(args, info) -> int:
         "ms_per_step": total / steps * 1e3,
         "median_ms": statistics.median(times) * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded torch.Generator, CPU)",
-        "config": {"workload": cfg.name, "batch": cfg.batch, "n": cfg.n, "seed": cfg.seed},
+        "data": "synthetic (seeded torch.Generator on CPU)",
+        "config": config_dict(cfg, gb, args.scaling),
         "cpu_baseline": {
             "value": value,
             "unit": UNIT,
             "cores": torch.get_num_threads(),
             "kind": "reference",
-            "sample": (f"torch.geqrf on CPU (the reference's geqrf_reference), {steps} steps of "
-                       f"the full {cfg.batch}-matrix batch"),
+            "sample": (f"torch.geqrf on CPU (the reference's geqrf_reference, "
+                       f"src/qrbench/reference.py:18-20), {steps} steps of the full "
+                       f"{gb}-matrix batch, all host threads"),
         },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -272,6 +327,33 @@ def time_device_steps(step, steps: int, warmup: int, flush_buf, stream):
     return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
+def global_input(cfg, batch: int, info, dev):
+    """(CPU tensor on rank 0 else None, device tensor of the whole seeded batch
+    on every rank). Rank 0 draws the batch on its CPU; other ranks receive it
+    by an NCCL broadcast (set-up only, outside every timed region)."""
+    import torch
+    import torch.distributed as dist
+
+    from gpumode_qr_b200 import inputs
+
+    if info.rank == 0:
+        A_cpu = inputs.make_config_input(cfg, batch)
+        A = A_cpu.to(dev)
+    else:
+        A_cpu = None
+        A = torch.empty(batch, cfg.n, cfg.n, dtype=torch.float32, device=dev)
+    if info.initialized:
+        dist.broadcast(A, src=0)
+    return A_cpu, A
+
+
+def large_n_roofline(cfg, ms: float, rows: int, route: str, peaks: dict) -> dict:
+    pk, bound, src = flop_peak(route, peaks)
+    tf = 4.0 / 3.0 * cfg.n**3 * rows / (ms / 1e3) / 1e12
+    return {"bound": bound, "achieved": tf, "peak": pk, "unit": "TFLOP/s", "frac": tf / pk,
+            "peak_source": src, "frac_of_fp32_nominal": tf / FP32_FFMA_NOMINAL_TFLOPS}
+
+
 def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
     import torch
 
@@ -286,14 +368,15 @@ def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
         H = torch.empty_like(A)
         tau = torch.empty(cfg.batch, cfg.n, device=dev)
         fn = api.geqrf_into_fn(A, H, tau)
-        iters = 10
-        times = time_device_steps(fn, iters, 3, flush_buf, stream)
+        route = api.route(cfg.batch, cfg.n)
+        times = time_device_steps(fn, 10, 3, flush_buf, stream)
         med = statistics.median(times)
         gpu_ms.append(med)
         gate = checker.check(A, H, tau)
         rec = {
             "batch": cfg.batch,
             "n": cfg.n,
+            "route": route,
             "median_ms": med,
             "min_ms": min(times),
             "matrices_per_s": cfg.batch / (med / 1e3),
@@ -306,10 +389,7 @@ def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
             rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
                                "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"]}
         else:
-            tf = cfg.flops / (med / 1e3) / 1e12
-            rec["roofline"] = {"bound": "fp32_ffma", "achieved": tf, "peak": FP32_FFMA_NOMINAL_TFLOPS,
-                               "unit": "TFLOP/s", "frac": tf / FP32_FFMA_NOMINAL_TFLOPS,
-                               "peak_source": "nominal 148 SMs x 128 FFMA x 2 x 1965 MHz"}
+            rec["roofline"] = large_n_roofline(cfg, med, cfg.batch, route, peaks)
         if cpu:
             torch.set_num_threads(os.cpu_count() or 1)
             torch.geqrf(A_cpu[:1])
@@ -327,12 +407,11 @@ def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
                 rec["parity_vs_geqrf"] = {"h_rel": par.h_rel, "tau_rel": par.tau_rel,
                                           "col_rel": par.col_rel, "ok": par.ok()}
         if cfg.n >= 512:
-            # the trailing-update pipe per n: FFMA (default), tcgen05 3xTF32 for
-            # both products, FFMA + tcgen05 for the second (median of 3 each)
+            # the trailing-update pipe per n, whole factorization (median of 3 each)
             kinds = {}
             old_kind = _lib.get_config("larfb_kind")
             try:
-                for kind, name in ((0, "ffma"), (1, "tcgen05_3xtf32"), (2, "ffma_then_tcgen05")):
+                for kind, name in api.LARFB_KINDS.items():
                     _lib.set_config("larfb_kind", kind)
                     kinds[name] = statistics.median(time_device_steps(fn, 3, 1, flush_buf, stream))
             finally:
@@ -352,7 +431,44 @@ def per_config_sweep(dev, flush_buf, cpu: bool, peaks: dict) -> dict:
     return res
 
 
-def gram_sweep(dev, flush_buf) -> dict:
+def strong_sweep(info, dev, flush_buf, peaks: dict, skip: int) -> dict:
+    """Strong scaling of the other configs at this N: each config's fixed batch
+    sharded over the ranks, 10 timed steps, MAX over ranks of the per-rank
+    median. Every rank runs the same steps and collectives."""
+    import torch
+
+    from gpumode_qr_b200 import api, inputs, sharding
+
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    for cfg in inputs.CONFIGS:
+        if cfg.index == skip:
+            continue
+        _, A_glob = global_input(cfg, cfg.batch, info, dev)
+        s, e = sharding.shard_range(cfg.batch, info.rank, info.world)
+        A = A_glob[s:e].contiguous()
+        del A_glob
+        H = torch.empty_like(A)
+        tau = torch.empty(A.shape[0], cfg.n, device=dev)
+        sharding.barrier(info)
+        if e > s:
+            med = statistics.median(
+                time_device_steps(api.geqrf_into_fn(A, H, tau), 10, 3, flush_buf, stream))
+        else:
+            med = 0.0
+        med = sharding.max_over_ranks(med, info)
+        rec = {"global_batch": cfg.batch, "max_batch_per_gpu": -(-cfg.batch // info.world),
+               "median_ms": med, "matrices_per_s": cfg.batch / (med / 1e3)}
+        if cfg.n > 64:
+            rec["roofline_per_gpu"] = large_n_roofline(
+                cfg, med, -(-cfg.batch // info.world), api.route(max(e - s, 1), cfg.n), peaks)
+        out[cfg.name] = rec
+        del A, H, tau
+        torch.cuda.empty_cache()
+    return out
+
+
+def gram_sweep(dev, flush_buf, b: int = 640) -> dict:
     """The statistics step in front of the factorization (S = G G^T, then QR of
     S) at the shape the reference's task statement singles out (batched
     512 x 512, contracted dimension 512): kernel time, FP32 roofline fraction
@@ -363,7 +479,7 @@ def gram_sweep(dev, flush_buf) -> dict:
 
     from gpumode_qr_b200 import api
 
-    b, n, k = 640, 512, 512
+    n, k = 512, 512
     g = torch.Generator().manual_seed(7)
     G_cpu = torch.randn(b, n, k, generator=g)
     G = G_cpu.to(dev)
@@ -445,6 +561,24 @@ def pcie_probe(A_host, H_host, A_dev, H_dev, dev, reps: int = 10) -> dict:
             "method": "pinned cudaMemcpyAsync of the step's A / H buffers, median of %d" % reps}
 
 
+def run_gram_quick(args, info) -> int:
+    """Profiling workload: the Gram kernel alone, device-timed."""
+    import torch
+
+    from gpumode_qr_b200 import api
+
+    dev = torch.device("cuda", info.local_rank if info.initialized else 0)
+    b = args.batch or 640
+    G = torch.randn(b, 512, 512, generator=torch.Generator().manual_seed(7)).to(dev)
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    times = time_device_steps(lambda: api.gram(G), args.steps, args.warmup, flush_buf,
+                              torch.cuda.current_stream(dev))
+    if info.rank == 0:
+        print(json.dumps({"quick": True, "workload": f"gram_b{b}_n512_k512",
+                          "median_ms": statistics.median(times)}), flush=True)
+    return 0
+
+
 def run_ours(args, info) -> int:
     import torch
 
@@ -452,29 +586,28 @@ def run_ours(args, info) -> int:
 
     dev = torch.device("cuda", info.local_rank if info.initialized else 0)
     torch.cuda.set_device(dev)
-    if args.larfb_kind is not None:
-        _lib.set_config("larfb_kind", args.larfb_kind)
+    hooks = apply_hooks(args.set)
+    if args.workload == "gram":
+        return run_gram_quick(args, info)
     cfg = inputs.config(args.config)
-    if args.batch is not None:
-        cfg = inputs.Config(cfg.index, args.batch, cfg.n, cfg.kind, cfg.seed, cfg.log10_cond, cfg.parity)
-    b = cfg.batch
     world = info.world
-    g_cfg = inputs.Config(cfg.index, b * world, cfg.n, cfg.kind, cfg.seed, cfg.log10_cond, cfg.parity)
-    A_all = inputs.make_config_input(g_cfg) if world > 1 else inputs.make_config_input(cfg)
-    s, e = sharding.shard_range(b * world, info.rank, world)
-    A_cpu = A_all[s:e].contiguous()
-    del A_all
-    A = A_cpu.to(dev)
+    gb = global_batch_of(args, cfg, world)
+    A_glob_cpu, A_glob = global_input(cfg, gb, info, dev)
+    s, e = sharding.shard_range(gb, info.rank, world)
+    rows = e - s
+    A = A_glob[s:e].contiguous()
+    del A_glob
     H = torch.empty_like(A)
-    tau = torch.empty(A.shape[0], cfg.n, device=dev)
+    tau = torch.empty(rows, cfg.n, device=dev)
     flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    step = api.geqrf_into_fn(A, H, tau)
+    step = api.geqrf_into_fn(A, H, tau) if rows > 0 else (lambda: None)
+    route = api.route(max(rows, 1), cfg.n)
 
     # correctness gate on this rank's shard before timing
     step()
     torch.cuda.synchronize()
-    gate = checker.check(A, H, tau) if not args.quick else None
+    gate = checker.check(A, H, tau) if (not args.quick and rows > 0) else None
     if gate is not None and not gate.passed:
         print(f"[bench] rank {info.rank}: gate FAILED {gate.as_dict()}", file=sys.stderr)
 
@@ -498,28 +631,31 @@ def run_ours(args, info) -> int:
     sharding.barrier(info)
     torch.cuda.synchronize()
     times = [a.elapsed_time(z) for a, z in zip(starts, ends)]
+    my_med = statistics.median(times)
     total_ms = sharding.max_over_ranks(sum(times), info)
-    med_ms = sharding.max_over_ranks(statistics.median(times), info)
-    total_mats = b * world * args.steps
-    value = total_mats / (total_ms / 1e3)
+    med_ms = sharding.max_over_ranks(my_med, info)
+    value = gb * args.steps / (total_ms / 1e3)
     launches_total = int(sharding.sum_over_ranks(launches, info))
 
     if args.quick:
         if info.rank == 0:
-            print(json.dumps({"quick": True, "workload": cfg.name, "batch_per_gpu": b,
-                              "median_ms": med_ms, "value": value, "unit": UNIT}), flush=True)
+            print(json.dumps({"quick": True, "workload": f"cfg{cfg.index}_b{gb}_n{cfg.n}",
+                              "route": route, "batch_per_gpu": rows, "median_ms": med_ms,
+                              "value": value, "unit": UNIT, "hooks": hooks}), flush=True)
         return 0
 
     # e2e through the public API with pinned host buffers (copies in the timed region)
-    A_host = A_cpu.pin_memory()
+    A_host = A.cpu().pin_memory()
     H_host = torch.empty_like(A_host).pin_memory()
     tau_host = torch.empty(A_host.shape[0], cfg.n).pin_memory()
     e2e_steps = max(3, min(args.steps, 50))
-
-    e2e_ws = torch.empty(api.host_workspace_bytes(b, cfg.n), dtype=torch.uint8, device=dev)
+    e2e_ws = torch.empty(max(api.host_workspace_bytes(max(rows, 1), cfg.n), 16), dtype=torch.uint8,
+                         device=dev)
 
     def e2e_step():
-        api.geqrf_host(A_host, H_host, tau_host, device=dev, chunks=args.chunks, workspace=e2e_ws)
+        if rows > 0:
+            api.geqrf_host(A_host, H_host, tau_host, device=dev, chunks=args.chunks,
+                           workspace=e2e_ws)
 
     for _ in range(2):
         e2e_step()
@@ -534,26 +670,44 @@ def run_ours(args, info) -> int:
     torch.cuda.synchronize()
     e2e_ms = sharding.max_over_ranks(e_s.elapsed_time(e_e), info)
     sharding.barrier(info)
-    e2e_value = b * world * e2e_steps / (e2e_ms / 1e3)
+    e2e_value = gb * e2e_steps / (e2e_ms / 1e3)
     h2d = A_host.numel() * 4
     d2h = H_host.numel() * 4 + tau_host.numel() * 4
-    pcie = pcie_probe(A_host, H_host, A, H, dev)
-    pcie["bound_ms"] = max(h2d / (pcie["h2d_gbs"] * 1e6), d2h / (pcie["d2h_gbs"] * 1e6))
-    pcie["e2e_frac"] = pcie["bound_ms"] / (e2e_ms / e2e_steps)
+    pcie = pcie_probe(A_host, H_host, A, H, dev) if rows > 0 else {}
+    if pcie:
+        pcie["bound_ms"] = max(h2d / (pcie["h2d_gbs"] * 1e6), d2h / (pcie["d2h_gbs"] * 1e6))
+        pcie["e2e_frac"] = pcie["bound_ms"] / (e2e_ms / e2e_steps)
 
     peaks = measured_peaks()
     extra = {}
-    if info.rank == 0 and world == 1 and not args.no_configs:
-        extra["per_config"] = per_config_sweep(dev, flush_buf, not args.no_cpu, peaks)
-        extra["gram"] = gram_sweep(dev, flush_buf)
+    if not args.no_configs:
+        if world == 1:
+            if info.rank == 0:
+                extra["per_config"] = per_config_sweep(dev, flush_buf, not args.no_cpu, peaks)
+                extra["gram"] = gram_sweep(dev, flush_buf)
+        else:
+            extra["strong"] = strong_sweep(info, dev, flush_buf, peaks, cfg.index)
     cpu = None
     if info.rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_geqrf_rate(A_cpu, args.cpu_seconds)
+        cpu = cpu_geqrf_rate(A_glob_cpu, args.cpu_seconds)
 
     if info.rank == 0:
-        alg_bytes = 2 * b * cfg.n * cfg.n * 4
-        ach = alg_bytes / (statistics.mean(times) / 1e3) / 1e9
-        traffic = profile_traffic(cfg.name)
+        rec = profile_record(f"cfg{cfg.index}_b{gb}_n{cfg.n}") or {}
+        if cfg.n <= 64:
+            alg_bytes = 2 * rows * cfg.n * cfg.n * 4
+            ach = alg_bytes / (statistics.mean(times) / 1e3) / 1e9
+            roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": ach / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                    "algorithmic_bytes_per_launch": alg_bytes}
+        else:
+            roof = large_n_roofline(cfg, statistics.mean(times), rows, route, peaks)
+            roof["algorithmic_flops_per_step"] = 4.0 / 3.0 * cfg.n**3 * rows
+            roof["scope"] = ("the whole factorization step on this GPU (panels and trailing "
+                             "updates), CUDA events on the launching stream")
+        roof["traffic"] = rec.get("traffic_bytes_per_launch")
+        roof["kernel"] = rec.get("kernel") or route
+        if rec:
+            roof["profile"] = {k: v for k, v in rec.items() if k != "traffic_bytes_per_launch"}
         line = {
             "metric": METRIC,
             "value": value,
@@ -564,31 +718,16 @@ def run_ours(args, info) -> int:
             "ms_per_step": total_ms / args.steps,
             "median_ms": med_ms,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": args.scaling,
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic (seeded torch.Generator on CPU, copied to HBM)",
-            "config": {
-                "workload": cfg.name,
-                "batch_per_gpu": b,
-                "global_batch": b * world,
-                "n": cfg.n,
-                "seed": cfg.seed,
-                "l2": "flushed between steps (256 MiB write, outside the step events)",
-                "parallelism": f"batch-sharded dp{world}, no collective on the hot path",
-            },
-            "roofline": {
-                "bound": "hbm",
-                "achieved": ach,
-                "peak": peaks["hbm_gbs"],
-                "unit": "GB/s",
-                "frac": ach / peaks["hbm_gbs"],
-                "traffic": traffic,
-                "peak_source": peaks["source"],
-                "kernel": ("k_fused (one launch per step)" if cfg.n <= 32 else
-                           "k_fused_cta (one launch per step)" if cfg.n <= 64 else "whole step"),
-                "algorithmic_bytes_per_launch": alg_bytes,
-            },
+            "config": config_dict(cfg, gb, args.scaling),
+            "sharding": {"batch_per_gpu_rank0": rows, "max_batch_per_gpu": -(-gb // world),
+                         "parallelism": f"batch-sharded dp{world}, no collective on the hot path",
+                         "l2": "flushed between steps (256 MiB write, outside the step events)"},
+            "route": route,
+            "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
@@ -597,8 +736,9 @@ def run_ours(args, info) -> int:
                     "pcie": pcie},
             "gpu_launches": launches_total,
             "clocks": clk.summary(),
-            "gates": {"factor": gate.factor_residual, "orth": gate.orth_residual,
-                      "passed": gate.passed},
+            "gates": ({"factor": gate.factor_residual, "orth": gate.orth_residual,
+                       "passed": gate.passed} if gate is not None else None),
+            "hooks": hooks,
             **extra,
         }
         print(json.dumps(line), flush=True)

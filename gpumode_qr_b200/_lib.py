@@ -22,6 +22,7 @@ SIGNATURES: dict[str, tuple] = {
     "qrb_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "qrb_max_n": (_I32, []),
     "qrb_workspace_bytes": (_SZ, [_I64, _I32]),
+    "qrb_route": (ctypes.c_int, [_I64, _I32, _SZ]),
     "qrb_geqrf_f32": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _I64, _I32, _P, _SZ, _P]),
     "qrb_geqrf_f32_noalloc": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _I64, _I32, _P]),
     "qrb_host_workspace_bytes": (_SZ, [_I64, _I32]),

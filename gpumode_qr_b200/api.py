@@ -52,6 +52,31 @@ def workspace_bytes(batch: int, n: int) -> int:
     return int(_lib.lib().qrb_workspace_bytes(int(batch), int(n)))
 
 
+# Trailing-update kinds of the blocked route (qrb_set_config("larfb_kind")).
+LARFB_KINDS = {0: "ffma", 1: "tcgen05_staged_3xtf32", 2: "ffma_then_tcgen05"}
+_ROUTES = {1: "fused_warp", 2: "fused_cta", 3: "blocked"}
+
+
+def route(batch: int, n: int, workspace: int | None = None) -> str:
+    """The route ``qrb_geqrf_f32`` takes for ``(batch, n)`` with ``workspace``
+    bytes (default: :func:`workspace_bytes`), as text, e.g.
+    ``"blocked:ffma,groups=4,lookahead"`` (``qrb_route``)."""
+    ws = workspace_bytes(batch, n) if workspace is None else int(workspace)
+    code = int(_lib.lib().qrb_route(int(batch), int(n), ws))
+    base = _ROUTES.get(code & 0xF)
+    if base is None:
+        return "none"
+    if base != "blocked":
+        return base
+    parts = [LARFB_KINDS.get((code >> 4) & 0xF, f"kind{(code >> 4) & 0xF}"),
+             f"groups={(code >> 12) & 0xF}"]
+    if code & (1 << 8):
+        parts.append("lookahead")
+    if code & (1 << 9):
+        parts.append("two_level")
+    return base + ":" + ",".join(parts)
+
+
 def max_n() -> int:
     return int(_lib.lib().qrb_max_n())
 

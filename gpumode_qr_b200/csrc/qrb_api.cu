@@ -272,14 +272,15 @@ FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch) {
   return f;
 }
 
-// The whole factorization of validated arguments, enqueued on s: the fused
-// warp kernel for n <= 32, the fused CTA kernel for 32 < n <= 128 where it
-// wins, the blocked loop otherwise (optionally split into batch groups on
-// internal streams, with the panel look-ahead or two-level blocking where
-// selected and the workspace holds their factors).
-int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
-                  const FactorScratch& ws, int64_t batch, int n, cudaStream_t s) {
-  if (n <= kFusedMaxN) return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
+// The route of one factorization: which kernels run and how the blocked loop
+// is organised. With every test hook at its default this is a pure function
+// of (batch, n, the workspace the caller gave), reported by qrb_route().
+Plan make_plan(int64_t batch, int n, const FactorScratch& ws) {
+  Plan p;
+  if (n <= kFusedMaxN) {
+    p.route = kRouteFusedWarp;
+    return p;
+  }
   // The CTA-per-matrix kernel is latency-friendly (one launch) but does more
   // arithmetic than the blocked route and runs in waves of 296 CTAs (2 per SM
   // at 128 threads). Measured on B200 it wins at n <= 64 for every batch, at
@@ -288,23 +289,53 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
   // 64 < n <= 96 up to two waves (145 vs 160 us at 592 x 80; 233 vs 199 us at
   // 740 x 96).
   if (n <= kFusedMidMaxN && mid_fused_enabled() &&
-      (n <= 64 || n > 96 || batch <= kFusedMidMaxBatch || mid_fused_always()))
-    return launch_fused_mid(A, strideA_b, strideA_row, H, tau, batch, n, s);
-  if (ws.T == nullptr) return QRB_ERR_WORKSPACE;
+      (n <= 64 || n > 96 || batch <= kFusedMidMaxBatch || mid_fused_always())) {
+    p.route = kRouteFusedCta;
+    return p;
+  }
+  if (ws.T == nullptr) return p;  // kRouteNone: the blocked route needs a T factor
+  p.route = kRouteBlocked;
+  p.larfb = (int)g_larfb_kind.load();
   // Automatic: 4 groups from n = 1024 on (measured on B200: 30.6 vs 32.8 ms for
   // 8 x 4096^2), else 2; at most half the batch.
   int groups = (int)g_groups.load();
   if (groups == 0) groups = n >= 1024 ? 4 : 2;
   if (groups > batch / 2) groups = (int)(batch / 2);
   if (batch < 4) groups = 1;
+  p.groups = groups < 1 ? 1 : groups;
   // Two-level blocking (opt-in: measured on B200 it is slower at every size,
   // 5.58 vs 5.22 ms at 640 x 512^2, 35.0 vs 29.6 ms at 8 x 4096^2) needs a
   // 64 x 64 factor per matrix, the look-ahead a second 32 x 32 one; two-level
   // takes precedence.
-  const bool tl = ws.T64 != nullptr && g_two_level.load() == 1;
+  p.two_level = ws.T64 != nullptr && g_two_level.load() == 1;
   const int64_t la_mode = g_lookahead.load();
-  const bool la = !tl && ws.T2 != nullptr &&
-                  (la_mode == 1 || (la_mode == 2 && n >= kLookaheadMinN));
+  p.lookahead = !p.two_level && ws.T2 != nullptr &&
+                (la_mode == 1 || (la_mode == 2 && n >= kLookaheadMinN));
+  return p;
+}
+
+int route_code(const Plan& p) {
+  if (p.route != kRouteBlocked) return p.route;
+  return p.route | (p.larfb << 4) | (p.lookahead ? 1 << 8 : 0) | (p.two_level ? 1 << 9 : 0) |
+         (p.groups << 12);
+}
+
+// The whole factorization of validated arguments, enqueued on s, as
+// make_plan routes it: the fused warp kernel for n <= 32, the fused CTA kernel
+// for 32 < n <= 128 where it wins, the blocked loop otherwise (optionally
+// split into batch groups on internal streams, with the panel look-ahead or
+// two-level blocking where selected and the workspace holds their factors).
+int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
+                  const FactorScratch& ws, int64_t batch, int n, cudaStream_t s) {
+  const Plan plan = make_plan(batch, n, ws);
+  if (plan.route == kRouteFusedWarp)
+    return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
+  if (plan.route == kRouteFusedCta)
+    return launch_fused_mid(A, strideA_b, strideA_row, H, tau, batch, n, s);
+  if (plan.route != kRouteBlocked) return QRB_ERR_WORKSPACE;
+  const int groups = plan.groups;
+  const bool tl = plan.two_level;
+  const bool la = plan.lookahead;
   if (groups <= 1 && !la) {
     if (tl) return blocked_qr2(A, strideA_b, strideA_row, H, tau, ws.T64, batch, n, s);
     return blocked_qr(A, strideA_b, strideA_row, H, tau, ws.T, batch, n, s);
@@ -366,7 +397,7 @@ const char* qrb_status_string(int status) {
 }
 
 int32_t qrb_max_n(void) { return qrb::kMaxN; }
-int32_t qrb_fused_max_n(void) { return qrb::kFusedMaxN; }
+int32_t qrb_fused_max_n(void) { return qrb::kFusedMidMaxN; }
 
 size_t qrb_workspace_bytes(int64_t batch, int32_t n) {
   if (batch <= 0 || n <= qrb::kFusedMaxN) return 0;
@@ -376,17 +407,34 @@ size_t qrb_workspace_bytes(int64_t batch, int32_t n) {
   return 4 * (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float);
 }
 
+int qrb_route(int64_t batch, int32_t n, size_t workspace_bytes) {
+  if (batch <= 0 || n <= 0 || n > qrb::kMaxN) return 0;
+  qrb::FactorScratch fs;
+  if (n > qrb::kFusedMaxN) {
+    // the same carving as qrb_geqrf_f32 (a stand-in base address: only which
+    // factors fit matters here)
+    static float dummy[4];
+    fs = qrb::factor_scratch(dummy, workspace_bytes, batch);
+  }
+  return qrb::route_code(qrb::make_plan(batch, n, fs));
+}
+
 int qrb_fused_qr_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
                      float* H, float* tau, int64_t batch, int32_t n,
                      void* stream) {
   if (batch < 0 || n < 0) return QRB_ERR_INVALID_ARG;
   if (batch == 0 || n == 0) return QRB_OK;
   if (!A || !H || !tau) return QRB_ERR_INVALID_ARG;
-  if (n > qrb::kFusedMaxN) return QRB_ERR_UNSUPPORTED;
+  if (n > qrb::kFusedMidMaxN) return QRB_ERR_UNSUPPORTED;
   if (bad_matrix_strides(strideA_b, strideA_row, n, n, batch)) return QRB_ERR_INVALID_ARG;
   if (take_injected_failure()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return finish(qrb::launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s), s);
+  // The reference's fused operator covers n <= 128 (src/qrbench/variants.py:698,
+  // :741): lanes of a warp per matrix up to n = 32, one CTA per matrix above.
+  const int rc = n <= qrb::kFusedMaxN
+                     ? qrb::launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s)
+                     : qrb::launch_fused_mid(A, strideA_b, strideA_row, H, tau, batch, n, s);
+  return finish(rc, s);
 }
 
 int qrb_panel_qr_f32(const float* P, int64_t strideP_b, int64_t strideP_row,

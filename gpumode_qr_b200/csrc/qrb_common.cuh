@@ -163,6 +163,18 @@ struct FactorScratch {
 };
 FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch);
 
+// The route of one qrb_geqrf_f32 call (see qrb_route in the public header).
+constexpr int kRouteNone = 0, kRouteFusedWarp = 1, kRouteFusedCta = 2, kRouteBlocked = 3;
+struct Plan {
+  int route = kRouteNone;
+  int larfb = 0;       // trailing update: 0 FFMA, 1 / 2 tcgen05 staged by the CUDA cores
+  int groups = 1;      // batch groups on internal streams
+  bool lookahead = false;
+  bool two_level = false;
+};
+Plan make_plan(int64_t batch, int n, const FactorScratch& ws);
+int route_code(const Plan& p);
+
 // Whole factorization of already validated arguments, enqueued on `stream`
 // (no fault injection, no sync check), the blocked route's factors in ws.
 int geqrf_enqueue(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau,

@@ -67,6 +67,25 @@ QRB_API int32_t qrb_max_n(void);
 QRB_API size_t qrb_workspace_bytes(int64_t batch, int32_t n);
 
 /*
+ * The route qrb_geqrf_f32 takes for (batch, n) given a workspace of
+ * workspace_bytes, as a bit field (0 = no route: bad size, or too little
+ * workspace for the blocked route):
+ *   bits 0-3   1 = fused, lanes of a warp per matrix (n <= 32);
+ *              2 = fused, one CTA per matrix (32 < n <= 128);
+ *              3 = blocked panel route;
+ *   bits 4-7   blocked trailing update: 0 = FP32 FFMA; 1 = tcgen05 3xTF32 with
+ *              operands staged by the CUDA cores; 2 = FFMA then tcgen05;
+ *   bit 8      panel look-ahead on a second stream;
+ *   bit 9      two-level (64-reflector) blocking;
+ *   bits 12-15 batch groups on internal streams.
+ * With every test hook of qrb_set_config at its default, the route is a pure
+ * function of (batch, n, workspace_bytes): nothing else that a caller does
+ * changes the kernels a call runs. It mirrors the reference's champion
+ * dispatch (src/qrbench/variants.py:876-917), which routes by n alone.
+ */
+QRB_API int qrb_route(int64_t batch, int32_t n, size_t workspace_bytes);
+
+/*
  * Batched square QR: the full hot path, one call per factorization.
  * Replaces the reference's registered impl callable
  *   impl(A: [b, n, n] fp32) -> (H, tau)
@@ -142,9 +161,12 @@ QRB_API int qrb_geqrf_f32_host(const float* A_host, float* H_host, float* tau_ho
                                size_t workspace_bytes, int32_t chunks, void* stream);
 
 /*
- * Fused whole-matrix QR for small n (n <= 32): 16 (or 8) lanes factor one
- * matrix in registers, two (or four) matrices per warp, in a single launch. Replaces hh_fused_qr / _hh_fused_qr_kernel
- * (src/qrbench/triton_kernels.py:722-755, :641-720).
+ * Fused whole-matrix QR for small n (n <= 128), one launch. n <= 32: 16 (or
+ * 8) lanes factor one matrix in registers, two (or four) matrices per warp;
+ * 32 < n <= 128: one CTA per matrix, one thread per column. Replaces
+ * hh_fused_qr / _hh_fused_qr_kernel (src/qrbench/triton_kernels.py:722-755,
+ * :641-720) as make_hh_fused_smalln routes it (cap 128,
+ * src/qrbench/variants.py:698, :741).
  */
 QRB_API int qrb_fused_qr_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
                      float* H, float* tau, int64_t batch, int32_t n,
@@ -236,7 +258,11 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
                                void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Tuning and test hooks (never needed for correct use). Keys:
+ * Test hooks (never needed for correct use). They are process-wide: a value
+ * set here changes the route of every later call in the process, on every
+ * thread and device, until it is set back, so only tests and benchmarks set
+ * them; at their defaults the route depends on (batch, n, workspace) alone
+ * (qrb_route). Keys:
  *   "fail_next"   value v > 0: the next v calls of any compute entry point
  *                 return QRB_ERR_INJECTED without enqueuing work (host-side
  *                 fault injection for tests).

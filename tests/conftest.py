@@ -6,6 +6,7 @@ paths); they are skipped when none is visible. Everything else runs on CPU.
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -16,6 +17,21 @@ REPO = Path(__file__).resolve().parents[1]
 GOLDEN = Path(__file__).resolve().parent / "golden"
 if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
+
+
+def reference_checkout() -> Path | None:
+    """The reference's source tree (``src/qrbench`` + ``scripts/``), if present:
+    ``$QRBENCH_REFERENCE``, else the git-ignored ``baseline/_ref/gpumode_qr``
+    copy that travels with the repository to GPU boxes. None when neither has
+    ``scripts/run_baseline.py``."""
+    cands = []
+    if os.environ.get("QRBENCH_REFERENCE"):
+        cands.append(Path(os.environ["QRBENCH_REFERENCE"]))
+    cands.append(REPO / "baseline" / "_ref" / "gpumode_qr")
+    for c in cands:
+        if (c / "scripts" / "run_baseline.py").exists() and (c / "src" / "qrbench").exists():
+            return c.resolve()
+    return None
 
 
 def pytest_configure(config):

@@ -10,7 +10,7 @@ import subprocess
 import pytest
 from conftest import REPO
 
-from gpumode_qr_b200 import _lib
+from gpumode_qr_b200 import _lib, api
 from gpumode_qr_b200.build import LIB_PATH
 
 HEADER = REPO / "include" / "qrb200.h"
@@ -28,7 +28,7 @@ def test_header_declares_the_expected_entry_points():
         "qrb_geqrf_f32_noalloc", "qrb_host_workspace_bytes", "qrb_geqrf_f32_host", "qrb_fused_qr_f32",
         "qrb_fused_max_n", "qrb_panel_qr_f32", "qrb_larfb_f32", "qrb_orgqr_workspace_bytes",
         "qrb_orgqr_f32", "qrb_ormqr_f32", "qrb_gram_f32", "qrb_gram_geqrf_f32",
-        "qrb_set_config", "qrb_get_config",
+        "qrb_set_config", "qrb_get_config", "qrb_route",
     }
 
 
@@ -52,7 +52,7 @@ def test_status_strings_and_constants():
         assert s.startswith("qrb:")
     assert "unknown" in _lib.status_string(99)
     assert L.qrb_max_n() == 8192
-    assert L.qrb_fused_max_n() == 32
+    assert L.qrb_fused_max_n() == 128
 
 
 def test_workspace_bytes():
@@ -155,7 +155,7 @@ def test_argument_validation_without_gpu():
     # in-place requires a contiguous A
     assert L.qrb_geqrf_f32(FAKE, 8192, 128, FAKE, FAKE, 2, 64, ws, 1 << 20, None) == 1
     # kernel-level entry points
-    assert L.qrb_fused_qr_f32(FAKE, 64 * 64, 64, FAKE, FAKE, 1, 64, None) == 2
+    assert L.qrb_fused_qr_f32(FAKE, 129 * 129, 129, FAKE, FAKE, 1, 129, None) == 2
     assert L.qrb_panel_qr_f32(FAKE, 100 * 33, 33, FAKE, None, FAKE, FAKE, 1, 100, 33, None) == 2
     assert L.qrb_panel_qr_f32(FAKE, 100, 10, FAKE, None, FAKE, FAKE, 1, 5, 10, None) == 2
     assert L.qrb_larfb_f32(FAKE, 64 * 8, 8, None, FAKE, 64 * 8, 8, 1, 64, 8, 8, None) == 1
@@ -263,3 +263,20 @@ def test_config_keys():
     with pytest.raises(_lib.QRBError):
         _lib.get_config("no_such_key")
 
+
+
+def test_route_is_a_function_of_batch_n_and_workspace():
+    # with every hook at its default the route depends on (batch, n, workspace)
+    # only; the reference's champion dispatch routes by n alone
+    L = _lib.lib()
+    assert L.qrb_route(4096, 32, 0) & 0xF == 1
+    assert L.qrb_route(8, 64, 0) & 0xF == 2
+    assert L.qrb_route(8, 128, 0) & 0xF == 2
+    assert L.qrb_route(0, 64, 0) == 0 and L.qrb_route(4, 9000, 0) == 0
+    ws = L.qrb_workspace_bytes(8, 4096)
+    assert L.qrb_route(8, 4096, 0) == 0  # the blocked route needs workspace
+    code = L.qrb_route(8, 4096, ws)
+    assert code & 0xF == 3 and (code >> 12) & 0xF == 4
+    assert L.qrb_route(8, 4096, ws) == code  # no hidden state between queries
+    assert api.route(640, 512).startswith("blocked:")
+    assert api.route(4096, 32) == "fused_warp"

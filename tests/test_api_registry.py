@@ -6,16 +6,15 @@ import importlib
 import subprocess
 import sys
 import types
-from pathlib import Path
 
 import pytest
 import torch
-from conftest import REPO
+from conftest import REPO, reference_checkout
 
 import gpumode_qr_b200 as pkg
 from gpumode_qr_b200 import api, variants
 
-REFERENCE = Path("/root/reference")
+REFERENCE = reference_checkout()
 
 
 def test_import_is_torch_free():
@@ -73,7 +72,7 @@ def test_register_into_fake_qrbench():
     assert fake.CHAMPION == "x"
 
 
-@pytest.mark.skipif(not (REFERENCE / "src" / "qrbench").exists(), reason="reference checkout absent")
+@pytest.mark.skipif(REFERENCE is None, reason="reference checkout absent")
 def test_register_into_reference_qrbench_and_list():
     code = f"""
 import sys
@@ -92,7 +91,7 @@ print('ok')
     assert out.stdout.strip().endswith("ok")
 
 
-@pytest.mark.skipif(not (REFERENCE / "scripts" / "run_baseline.py").exists(), reason="reference absent")
+@pytest.mark.skipif(REFERENCE is None, reason="reference checkout absent")
 def test_harness_shim_lists_our_variant():
     out = subprocess.run(
         [sys.executable, "-m", "gpumode_qr_b200.harness", "--reference", str(REFERENCE), "--list"],

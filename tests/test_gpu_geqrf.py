@@ -215,7 +215,7 @@ def test_error_paths_raise():
     with pytest.raises(ValueError):
         api.geqrf(torch.randn(2, 4, 5, device=DEV))
     with pytest.raises(ValueError):
-        api.hh_fused_qr(torch.randn(2, 33, 33, device=DEV))
+        api.hh_fused_qr(torch.randn(2, 129, 129, device=DEV))
 
 
 @pytest.mark.parametrize("b,n,chunks", [(10, 48, 3), (4096, 32, 0), (7, 100, 64), (5, 33, 1),

@@ -52,6 +52,25 @@ def test_fused_kernel_every_small_n(n):
     assert (tau[:, -1] == 0).all()
 
 
+@pytest.mark.parametrize("n", [33, 40, 64, 65, 96, 97, 127, 128])
+def test_fused_operator_covers_the_reference_cap(n):
+    # hh_fused_qr serves every n <= 128, as the reference's make_hh_fused_smalln
+    # (src/qrbench/variants.py:698, :741); above 32 one CTA factors one matrix.
+    A = torch.randn(5, n, n, generator=torch.Generator().manual_seed(1000 + n))
+    H, tau = api.hh_fused_qr(A.to(DEV))
+    Ho, to = oracle.geqr2(A.numpy(), f64=True)
+    par = checker.parity(H.cpu(), tau.cpu(), Ho, to)
+    assert par.ok(RTOL), (n, par)
+    assert checker.check(A, H.cpu(), tau.cpu()).passed
+    Hg, tg = api.geqrf(A.to(DEV))  # the champion route runs the same kernel here
+    assert torch.equal(Hg, H) and torch.equal(tg, tau)
+
+
+def test_fused_operator_refuses_n_above_128():
+    with pytest.raises(ValueError, match="n <= 128"):
+        api.hh_fused_qr(torch.zeros(1, 129, 129, device=DEV))
+
+
 @pytest.mark.parametrize("n", [1, 5, 8, 9, 16, 17, 31, 32])
 @pytest.mark.parametrize("b", [1, 3, 5, 6, 7, 37, 4736, 4737])
 def test_fused_kernel_two_and_four_matrices_per_warp_agree(n, b):
