@@ -53,7 +53,8 @@ def workspace_bytes(batch: int, n: int) -> int:
 
 
 # Trailing-update kinds of the blocked route (qrb_set_config("larfb_kind")).
-LARFB_KINDS = {0: "ffma", 1: "tcgen05_staged_3xtf32", 2: "ffma_then_tcgen05"}
+LARFB_KINDS = {0: "ffma", 1: "tcgen05_staged_3xtf32", 2: "ffma_then_tcgen05",
+               3: "tcgen05_tma_3xtf32"}
 _ROUTES = {1: "fused_warp", 2: "fused_cta", 3: "blocked"}
 
 

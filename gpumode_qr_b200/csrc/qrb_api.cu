@@ -7,12 +7,13 @@
 #include <mutex>
 
 #include "qrb_common.cuh"
+#include "qrb_tma.cuh"
 
 namespace {
 
 std::atomic<int64_t> g_fail_next{0};
 std::atomic<int64_t> g_sync_check{0};
-std::atomic<int64_t> g_larfb_kind{0};  // 0 = FFMA, 1 = tcgen05 3xTF32
+std::atomic<int64_t> g_larfb_kind{-1};  // -1 automatic, else a kLarfb* kind
 std::atomic<int64_t> g_launches{0};
 std::atomic<int64_t> g_groups{0};  // 0 = automatic
 std::atomic<int64_t> g_host_direct{3};
@@ -24,6 +25,8 @@ std::atomic<int64_t> g_lookahead{2};  // 0 off, 1 on, 2 from kLookaheadMinN
 std::atomic<int64_t> g_two_level{0};  // 0 off, 1 on
 std::atomic<int64_t> g_panel_rpt{0};
 std::atomic<int64_t> g_gram_tile{0};
+std::atomic<int64_t> g_wait_limit{2000000000LL};  // clock cycles, about 1 s
+std::atomic<int64_t> g_skip_mma{0};
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -71,24 +74,52 @@ bool bad_matrix_strides(int64_t sb, int64_t srow, int64_t rows, int64_t cols,
 // per 32-column panel one panel kernel (reflectors, tau, T) and one trailing
 // update of the columns to its right. The first step reads A and writes H,
 // so no separate copy pass is needed; later steps work in place on H.
+// The tensor-core trailing update's operands for one batch group: tensor
+// maps over the whole call's batch, the split-reflector planes, and the
+// group's first matrix in them.
+struct TmaRoute {
+  const qrb::LarfbMaps* maps;
+  float* Vs;            // plane 0, matrix 0 of the call
+  int64_t batch_total;  // matrices the maps and planes cover
+  int64_t m0;           // this group's first matrix
+  // hi plane of V-buffer `buf` at this group's first matrix
+  float* vsplit(int buf, int n) const {
+    return Vs + ((int64_t)(2 * buf) * batch_total + m0) * n * qrb::kPanelW;
+  }
+  int64_t plane(int n) const { return batch_total * n * qrb::kPanelW; }
+};
+
+// The blocked factorization of one contiguous group of matrices on `s`:
+// per 32-column panel one panel kernel (reflectors, tau, T) and one trailing
+// update of the columns to its right. On the FFMA route the first step reads
+// A and writes H, so no separate copy pass is needed; later steps work in
+// place on H. On the tensor-core route (tr non-null) H already holds A, the
+// panel also writes its split reflectors and the update is the TMA-fed kernel.
 int blocked_qr(const float* A, int64_t strideA_b, int64_t strideA_row, float* H,
-               float* tau, float* T, int64_t batch, int n, cudaStream_t s) {
+               float* tau, float* T, int64_t batch, int n, cudaStream_t s,
+               const TmaRoute* tr = nullptr) {
   const int64_t nn = (int64_t)n * n;
   const int W = qrb::kPanelW;
   for (int j0 = 0; j0 < n; j0 += W) {
     const int w = n - j0 < W ? n - j0 : W;
     const int r = n - j0;
-    const float* src = (j0 == 0) ? A : H;
-    const int64_t sb = (j0 == 0) ? strideA_b : nn;
-    const int64_t ld = (j0 == 0) ? strideA_row : n;
+    const bool first = j0 == 0 && tr == nullptr;
+    const float* src = first ? A : H;
+    const int64_t sb = first ? strideA_b : nn;
+    const int64_t ld = first ? strideA_row : n;
     float* Hp = H + (int64_t)j0 * n + j0;
-    int rc = qrb::launch_panel(src + (int64_t)j0 * ld + j0, sb, ld, Hp, nn, n, tau + j0, n, T,
-                               (int64_t)W * W, W, nullptr, batch, r, w, s);
-    if (rc != QRB_OK) return rc;
     const int c = n - j0 - w;
+    float* vs = (tr != nullptr && c > 0) ? tr->vsplit(0, n) : nullptr;
+    int rc = qrb::launch_panel(src + (int64_t)j0 * ld + j0, sb, ld, Hp, nn, n, tau + j0, n, T,
+                               (int64_t)W * W, W, nullptr, batch, r, w, s, vs,
+                               (int64_t)n * W, tr ? tr->plane(n) : 0, j0);
+    if (rc != QRB_OK) return rc;
     if (c > 0) {
-      rc = larfb_any(Hp, nn, n, T, (int64_t)W * W, W, src + (int64_t)j0 * ld + j0 + w, sb, ld,
-                     Hp + w, nn, n, batch, r, w, c, s);
+      rc = tr != nullptr
+               ? qrb::launch_larfb_tma(*tr->maps, T, (int64_t)W * W, tr->m0, batch, j0, j0 + w,
+                                       n, n, 0, s)
+               : larfb_any(Hp, nn, n, T, (int64_t)W * W, W, src + (int64_t)j0 * ld + j0 + w, sb,
+                           ld, Hp + w, nn, n, batch, r, w, c, s);
       if (rc != QRB_OK) return rc;
     }
   }
@@ -106,38 +137,48 @@ int blocked_qr(const float* A, int64_t strideA_b, int64_t strideA_row, float* H,
 int blocked_qr_lookahead(const float* A, int64_t strideA_b, int64_t strideA_row, float* H,
                          float* tau, float* T0, float* T1, int64_t batch, int n,
                          cudaStream_t sb, cudaStream_t sp, cudaEvent_t evP, cudaEvent_t evB,
-                         cudaEvent_t joinP) {
+                         cudaEvent_t joinP, const TmaRoute* tr = nullptr) {
   const int64_t nn = (int64_t)n * n;
   const int W = qrb::kPanelW;
   if (cudaEventRecord(evB, sb) != cudaSuccess || cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess)
     return QRB_ERR_LAUNCH;
   int rc = QRB_OK;
   for (int j0 = 0, step = 0; j0 < n && rc == QRB_OK; j0 += W, ++step) {
-    float* T = (step & 1) ? T1 : T0;
+    const int buf = step & 1;
+    float* T = buf ? T1 : T0;
     const int w = n - j0 < W ? n - j0 : W;
     const int r = n - j0;
-    const float* src = (j0 == 0) ? A : H;
-    const int64_t sbt = (j0 == 0) ? strideA_b : nn;
-    const int64_t ld = (j0 == 0) ? strideA_row : n;
+    const bool first = j0 == 0 && tr == nullptr;
+    const float* src = first ? A : H;
+    const int64_t sbt = first ? strideA_b : nn;
+    const int64_t ld = first ? strideA_row : n;
     float* Hp = H + (int64_t)j0 * n + j0;
+    const int c = n - j0 - w;
+    float* vs = (tr != nullptr && c > 0) ? tr->vsplit(buf, n) : nullptr;
     rc = qrb::launch_panel(src + (int64_t)j0 * ld + j0, sbt, ld, Hp, nn, n, tau + j0, n, T,
-                           (int64_t)W * W, W, nullptr, batch, r, w, sp);
+                           (int64_t)W * W, W, nullptr, batch, r, w, sp, vs, (int64_t)n * W,
+                           tr ? tr->plane(n) : 0, j0);
     if (rc != QRB_OK) break;
     if (cudaEventRecord(evP, sp) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
-    const int c = n - j0 - w;
     if (c <= 0) break;
     const int ca = c < W ? c : W, cbw = c - ca;
     const float* ca_src = src + (int64_t)j0 * ld + j0 + w;
     // part a on sp, after part b of the previous step
     if (cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
-    rc = larfb_any(Hp, nn, n, T, (int64_t)W * W, W, ca_src, sbt, ld, Hp + w, nn, n, batch, r, w,
-                   ca, sp);
+    rc = tr != nullptr
+             ? qrb::launch_larfb_tma(*tr->maps, T, (int64_t)W * W, tr->m0, batch, j0, j0 + w,
+                                     j0 + w + ca, n, buf, sp)
+             : larfb_any(Hp, nn, n, T, (int64_t)W * W, W, ca_src, sbt, ld, Hp + w, nn, n, batch,
+                         r, w, ca, sp);
     if (rc != QRB_OK) break;
     // part b on sb, after panel j
     if (cudaStreamWaitEvent(sb, evP, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
     if (cbw > 0) {
-      rc = larfb_any(Hp, nn, n, T, (int64_t)W * W, W, ca_src + ca, sbt, ld, Hp + w + ca, nn, n,
-                     batch, r, w, cbw, sb);
+      rc = tr != nullptr
+               ? qrb::launch_larfb_tma(*tr->maps, T, (int64_t)W * W, tr->m0, batch, j0,
+                                       j0 + w + ca, n, n, buf, sb)
+               : larfb_any(Hp, nn, n, T, (int64_t)W * W, W, ca_src + ca, sbt, ld, Hp + w + ca,
+                           nn, n, batch, r, w, cbw, sb);
       if (rc != QRB_OK) break;
     }
     if (cudaEventRecord(evB, sb) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
@@ -260,8 +301,19 @@ int64_t host_direct_blocks() {
   return b > 0 ? b : kHostDirectBlocks;
 }
 int finish_call(int rc, cudaStream_t stream) { return finish(rc, stream); }
+long long device_wait_limit() { return (long long)g_wait_limit.load(); }
+bool test_skip_mma() { return g_skip_mma.load() != 0; }
 
-FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch) {
+size_t vsplit_bytes(int64_t batch, int n) {
+  if (batch <= 0 || n < kTmaMinN || n % 4 != 0) return 0;
+  return 4 * (size_t)batch * n * kPanelW * sizeof(float);
+}
+
+size_t min_workspace_bytes(int64_t batch) {
+  return (size_t)batch * kPanelW * kPanelW * sizeof(float);
+}
+
+FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch, int n) {
   FactorScratch f;
   const size_t unit = (size_t)batch * kPanelW * kPanelW * sizeof(float);
   float* base = static_cast<float*>(workspace);
@@ -269,6 +321,8 @@ FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch) {
   f.T = base;
   if (bytes >= 2 * unit) f.T2 = base + unit / sizeof(float);
   if (bytes >= 4 * unit) f.T64 = base;
+  const size_t vb = vsplit_bytes(batch, n);
+  if (vb != 0 && bytes >= 4 * unit + vb) f.Vs = base + 4 * unit / sizeof(float);
   return f;
 }
 
@@ -295,7 +349,15 @@ Plan make_plan(int64_t batch, int n, const FactorScratch& ws) {
   }
   if (ws.T == nullptr) return p;  // kRouteNone: the blocked route needs a T factor
   p.route = kRouteBlocked;
-  p.larfb = (int)g_larfb_kind.load();
+  // Trailing update: the TMA-fed tensor-core kernel where the workspace holds
+  // the split reflectors and the rows are 16-byte aligned (n % 4 == 0), FFMA
+  // elsewhere; the test hook picks a kind explicitly.
+  const int64_t kind = g_larfb_kind.load();
+  const bool tma_ok = ws.Vs != nullptr && n >= kTmaMinN && larfb_tma_supported(n);
+  if (kind < 0)
+    p.larfb = tma_ok ? kLarfbTma : kLarfbFfma;
+  else
+    p.larfb = (kind == kLarfbTma && !tma_ok) ? kLarfbFfma : (int)kind;
   // Automatic: 4 groups from n = 1024 on (measured on B200: 30.6 vs 32.8 ms for
   // 8 x 4096^2), else 2; at most half the batch.
   int groups = (int)g_groups.load();
@@ -308,6 +370,7 @@ Plan make_plan(int64_t batch, int n, const FactorScratch& ws) {
   // 64 x 64 factor per matrix, the look-ahead a second 32 x 32 one; two-level
   // takes precedence.
   p.two_level = ws.T64 != nullptr && g_two_level.load() == 1;
+  if (p.two_level && p.larfb == kLarfbTma) p.larfb = kLarfbFfma;  // two-level runs on FFMA
   const int64_t la_mode = g_lookahead.load();
   p.lookahead = !p.two_level && ws.T2 != nullptr &&
                 (la_mode == 1 || (la_mode == 2 && n >= kLookaheadMinN));
@@ -336,16 +399,54 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
   const int groups = plan.groups;
   const bool tl = plan.two_level;
   const bool la = plan.lookahead;
+  // Tensor-core route: H must hold A before the first update adds into it in
+  // place, and one set of tensor maps covers the whole call.
+  LarfbMaps maps;
+  const bool tma = plan.larfb == kLarfbTma;
+  if (tma) {
+    const int64_t nn = (int64_t)n * n;
+    if (A != H) {
+      cudaError_t e = cudaSuccess;
+      if (strideA_b == (int64_t)n * strideA_row) {
+        e = cudaMemcpy2DAsync(H, (size_t)n * sizeof(float), A, (size_t)strideA_row * sizeof(float),
+                              (size_t)n * sizeof(float), (size_t)(batch * n),
+                              cudaMemcpyDeviceToDevice, s);
+      } else {
+        for (int64_t m = 0; m < batch && e == cudaSuccess; ++m)
+          e = cudaMemcpy2DAsync(H + m * nn, (size_t)n * sizeof(float), A + m * strideA_b,
+                                (size_t)strideA_row * sizeof(float), (size_t)n * sizeof(float),
+                                (size_t)n, cudaMemcpyDeviceToDevice, s);
+      }
+      if (e != cudaSuccess) return QRB_ERR_LAUNCH;
+      A = H;
+      strideA_b = nn;
+      strideA_row = n;
+    }
+    const int rc = make_larfb_maps(&maps, H, ws.Vs, batch, n);
+    if (rc != QRB_OK) return rc;
+  }
+  auto route_of = [&](int64_t m0) {
+    TmaRoute r;
+    r.maps = &maps;
+    r.Vs = ws.Vs;
+    r.batch_total = batch;
+    r.m0 = m0;
+    return r;
+  };
   if (groups <= 1 && !la) {
     if (tl) return blocked_qr2(A, strideA_b, strideA_row, H, tau, ws.T64, batch, n, s);
-    return blocked_qr(A, strideA_b, strideA_row, H, tau, ws.T, batch, n, s);
+    const TmaRoute r0 = route_of(0);
+    return blocked_qr(A, strideA_b, strideA_row, H, tau, ws.T, batch, n, s, tma ? &r0 : nullptr);
   }
   SideStreams* ss = side_streams();
   if (ss == nullptr) return QRB_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(ss->mu);
-  if (groups <= 1)
+  if (groups <= 1) {
+    const TmaRoute r0 = route_of(0);
     return blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, ws.T, ws.T2, batch, n, s,
-                                ss->sp[0], ss->evP[0], ss->evB[0], ss->joinP[0]);
+                                ss->sp[0], ss->evP[0], ss->evB[0], ss->joinP[0],
+                                tma ? &r0 : nullptr);
+  }
   // Split the batch into groups that run the same kernel sequence on separate
   // internal streams, forked from and joined back into the caller's stream, so
   // that one group's (latency-bound) panel kernels overlap another group's
@@ -359,16 +460,18 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     if (b1 <= b0) continue;
     cudaStream_t gs = ss->s[g];
     if (cudaStreamWaitEvent(gs, ss->fork, 0) != cudaSuccess) return QRB_ERR_LAUNCH;
+    const TmaRoute rg = route_of(b0);
     if (tl)
       rc = blocked_qr2(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
                        ws.T64 + b0 * 4 * tper, b1 - b0, n, gs);
     else if (la)
       rc = blocked_qr_lookahead(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn,
                                 tau + b0 * n, ws.T + b0 * tper, ws.T2 + b0 * tper, b1 - b0, n,
-                                gs, ss->sp[g], ss->evP[g], ss->evB[g], ss->joinP[g]);
+                                gs, ss->sp[g], ss->evP[g], ss->evB[g], ss->joinP[g],
+                                tma ? &rg : nullptr);
     else
       rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
-                      ws.T + b0 * tper, b1 - b0, n, gs);
+                      ws.T + b0 * tper, b1 - b0, n, gs, tma ? &rg : nullptr);
     if (cudaEventRecord(ss->join[g], gs) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
     if (cudaStreamWaitEvent(s, ss->join[g], 0) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
   }
@@ -403,8 +506,10 @@ size_t qrb_workspace_bytes(int64_t batch, int32_t n) {
   if (batch <= 0 || n <= qrb::kFusedMaxN) return 0;
   // Four 32 x 32 units per matrix: one compact-WY factor T is the minimum, a
   // second enables the panel look-ahead, all four (one 64 x 64 factor) the
-  // two-level blocking.
-  return 4 * (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float);
+  // two-level blocking; then the split reflectors of the tensor-core update
+  // (two V buffers x hi / lo, n x 32 each) where that update applies.
+  return 4 * (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float) +
+         qrb::vsplit_bytes(batch, n);
 }
 
 int qrb_route(int64_t batch, int32_t n, size_t workspace_bytes) {
@@ -414,7 +519,7 @@ int qrb_route(int64_t batch, int32_t n, size_t workspace_bytes) {
     // the same carving as qrb_geqrf_f32 (a stand-in base address: only which
     // factors fit matters here)
     static float dummy[4];
-    fs = qrb::factor_scratch(dummy, workspace_bytes, batch);
+    fs = qrb::factor_scratch(dummy, workspace_bytes, batch, n);
   }
   return qrb::route_code(qrb::make_plan(batch, n, fs));
 }
@@ -489,10 +594,10 @@ int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
   if (A == H && (strideA_row != n || strideA_b != (int64_t)n * n)) return QRB_ERR_INVALID_ARG;
   qrb::FactorScratch fs;
   if (n > qrb::kFusedMaxN) {
-    const size_t one = qrb_workspace_bytes(batch, n) / 4;  // the minimum: one factor each
+    const size_t one = qrb::min_workspace_bytes(batch);  // the minimum: one T factor each
     if (workspace == nullptr || workspace_bytes < one) return QRB_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
-    fs = qrb::factor_scratch(workspace, workspace_bytes, batch);
+    fs = qrb::factor_scratch(workspace, workspace_bytes, batch, n);
   }
   if (take_injected_failure()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -511,8 +616,24 @@ int qrb_set_config(const char* key, int64_t value) {
     g_sync_check.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "wait_limit") == 0) {
+    if (value < 1000 || value > 100000000000LL) return QRB_ERR_INVALID_ARG;
+    g_wait_limit.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "test_skip_mma") == 0) {
+    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    g_skip_mma.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "wait_probe") == 0) {  // run the probe on the legacy stream, synchronously
+    if (value < 1000 || value > 100000000000LL) return QRB_ERR_INVALID_ARG;
+    const int rc = qrb::launch_wait_probe(value, nullptr);
+    if (rc != QRB_OK) return rc;
+    return cudaDeviceSynchronize() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
+  }
   if (std::strcmp(key, "larfb_kind") == 0) {
-    if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
+    if (value < -1 || value > 3) return QRB_ERR_INVALID_ARG;
     g_larfb_kind.store(value);
     return QRB_OK;
   }
@@ -584,6 +705,8 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "fail_next") == 0) { *value = g_fail_next.load(); return QRB_OK; }
   if (std::strcmp(key, "sync_check") == 0) { *value = g_sync_check.load(); return QRB_OK; }
   if (std::strcmp(key, "larfb_kind") == 0) { *value = g_larfb_kind.load(); return QRB_OK; }
+  if (std::strcmp(key, "wait_limit") == 0) { *value = g_wait_limit.load(); return QRB_OK; }
+  if (std::strcmp(key, "test_skip_mma") == 0) { *value = g_skip_mma.load(); return QRB_OK; }
   if (std::strcmp(key, "device_error") == 0) {
     int v = 0;
     const int rc = qrb::device_error_flag(&v, false);

@@ -98,10 +98,15 @@ bool mid_fused_always();
 // T_out[m*T_sb + row*t_ld + col] (t_ld == 32: a zero-padded 32 x 32 block;
 // t_ld == w: a dense w x w block). V_out, when non-null, receives the explicit
 // unit-lower reflectors (r x w, contiguous per matrix).
+// Vsplit, when non-null (w == 32 only), receives the unit-lower reflectors
+// split into a TF32 high part (row vs_row0 + i of matrix m at
+// Vsplit + m * vs_mat + (vs_row0 + i) * 32) and the TF32-rounded remainder
+// (vs_plane floats further on): the operands of the tensor-core update.
 int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
                  int64_t sb_dst, int64_t ld_dst, float* tau_out, int64_t tau_sb,
                  float* T_out, int64_t T_sb, int t_ld, float* V_out,
-                 int64_t batch, int r, int w, cudaStream_t stream);
+                 int64_t batch, int r, int w, cudaStream_t stream, float* Vsplit = nullptr,
+                 int64_t vs_mat = 0, int64_t vs_plane = 0, int vs_row0 = 0);
 
 // C_dst <- C_src - V T^T V^T C_src for r x c blocks, k <= 32 reflectors whose
 // strictly-lower part is read from V (unit diagonal implied). T is 32 x 32 per
@@ -147,6 +152,16 @@ int launch_larfb64(const float* V, int64_t sVb, int64_t ldv, const float* T, int
 int launch_t64(const float* V, int64_t sVb, int64_t ldv, float* T64, int64_t sT64b,
                int64_t batch, int r, cudaStream_t stream);
 
+// Clock-cycle limit of the bounded device-side waits (qrb_set_config
+// "wait_limit"; default about one second).
+long long device_wait_limit();
+// qrb_set_config("test_skip_mma"): the TMA-fed update issues no pass-1 MMAs,
+// so its bounded waits run out (tests of the timeout path only).
+bool test_skip_mma();
+// One probe kernel that waits on an mbarrier nobody arrives at for `limit`
+// cycles and then sets the device error flag.
+int launch_wait_probe(long long limit, cudaStream_t stream);
+
 // Device-side error flag set by kernels whose bounded waits timed out
 // (synchronous read; optionally reset to 0), and its device address.
 int device_error_flag(int* value, bool reset);
@@ -156,18 +171,31 @@ int device_error_ptr(int** p);
 // `bytes` for `batch` matrices: T one 32 x 32 factor per matrix (required),
 // T2 a second one for the panel look-ahead, T64 one 64 x 64 factor per matrix
 // for two-level blocking (each nullptr when the workspace is too small).
+// Vs: the split reflectors of the tensor-core update, [4][batch][n][32]
+// (planes 2 * buf + 0 / 1 = hi / lo of V-buffer buf), when the workspace
+// holds them.
 struct FactorScratch {
   float* T = nullptr;
   float* T2 = nullptr;
   float* T64 = nullptr;
+  float* Vs = nullptr;
 };
-FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch);
+FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch, int n);
+// Bytes of the split-reflector buffers for (batch, n), 0 where the
+// tensor-core update cannot run.
+size_t vsplit_bytes(int64_t batch, int n);
+// The smallest workspace the blocked route accepts: one T factor per matrix.
+size_t min_workspace_bytes(int64_t batch);
 
 // The route of one qrb_geqrf_f32 call (see qrb_route in the public header).
 constexpr int kRouteNone = 0, kRouteFusedWarp = 1, kRouteFusedCta = 2, kRouteBlocked = 3;
+constexpr int kLarfbFfma = 0, kLarfbTcStaged = 1, kLarfbTcPass2 = 2, kLarfbTma = 3;
+// Smallest n the blocked route gives the TMA-fed tensor-core update.
+constexpr int kTmaMinN = 129;
 struct Plan {
   int route = kRouteNone;
-  int larfb = 0;       // trailing update: 0 FFMA, 1 / 2 tcgen05 staged by the CUDA cores
+  int larfb = 0;       // trailing update: kLarfb* (0 FFMA, 1 / 2 tcgen05 staged by the
+                       // CUDA cores, 3 tcgen05 fed by TMA)
   int groups = 1;      // batch groups on internal streams
   bool lookahead = false;
   bool two_level = false;

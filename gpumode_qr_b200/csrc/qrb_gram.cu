@@ -485,10 +485,10 @@ int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t strideG_row, f
   if (!H) return QRB_ERR_INVALID_ARG;
   qrb::FactorScratch fs;
   if (n > qrb::kFusedMaxN) {
-    const size_t one = qrb_workspace_bytes(batch, n) / 4;
+    const size_t one = qrb::min_workspace_bytes(batch);
     if (workspace == nullptr || workspace_bytes < one) return QRB_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return QRB_ERR_INVALID_ARG;
-    fs = qrb::factor_scratch(workspace, workspace_bytes, batch);
+    fs = qrb::factor_scratch(workspace, workspace_bytes, batch, n);
   }
   if (qrb::take_injected_failure_any()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -197,7 +197,7 @@ int qrb_geqrf_f32_host(const float* A_host, float* H_host, float* tau_host, int6
                                       align_up((size_t)batch * n * sizeof(float)));
 
   // one chunk's factors at a time (the chunks run in order on one stream)
-  const qrb::FactorScratch fs = qrb::factor_scratch(T, qrb_workspace_bytes(batch, n), batch);
+  const qrb::FactorScratch fs = qrb::factor_scratch(T, qrb_workspace_bytes(batch, n), batch, n);
   HostPipe* p = host_pipe();
   if (p == nullptr) return QRB_ERR_DEVICE;
   int rc = QRB_OK;

@@ -1,0 +1,588 @@
+// Block-reflector trailing update C <- C - V (T^T (V^T C)) on the tcgen05
+// tensor cores in 3xTF32, fed by TMA: the three batched GEMMs of the
+// reference's trailing update (src/qrbench/variants.py:800-804) as one
+// persistent kernel over (matrix, 128-column tile of C) work items.
+//
+// Operands (all row-major in HBM, read through swizzled TMA boxes):
+//   C   the trailing block of H itself (rows j0.., the tile's columns);
+//   V   the panel's unit-lower reflectors, already split by the panel kernel
+//       into a TF32 high part and a TF32 remainder (Vs[hi|lo][matrix][row][32]);
+//   T   the panel's 32 x 32 compact-WY factor.
+// Each FP32 product a*b is formed as a_hi b_hi + a_hi b_lo + a_lo b_hi with
+// FP32 accumulation in TMEM (the lo*lo term, ~2^-22 relative, is dropped);
+// plain TF32 would not meet the FP32 accuracy gates.
+//
+// Per tile:
+//   pass 1  W^T = C^T V over all rows: D1 in TMEM (128 lanes = tile columns x
+//           32 columns = reflectors), as 8 interleaved partial sums. Both
+//           operands are MN-major (row-major C and V, contraction over rows),
+//           which kind::tf32 takes straight from TMA boxes in the 32-byte-atom
+//           128-byte swizzle. A 4-stage ring of 32-row chunks; the worker
+//           warps split each C chunk into hi (in place) and lo (a second
+//           buffer) while earlier chunks' MMAs run.
+//   T^T     W' = T^T W on the CUDA cores (each worker thread one column, read
+//           from TMEM), split into hi / lo and stored as the K-major B operand
+//           of pass 2.
+//   pass 2  D2 = V W' per 128-row chunk (K-major V boxes from TMA, two TMEM
+//           accumulators so one chunk's epilogue overlaps the next chunk's
+//           MMAs); the epilogue writes -D2 into a swizzled staging tile and a
+//           TMA reduce-add adds it to C in place (the L2 does the
+//           read-modify-write).
+// Warp roles: warp 0 = TMA producer (one lane), warp 1 = MMA issuer (one
+// lane; the warp owns the TMEM allocation), warps 2-9 = workers. The roles
+// hand chunks to each other through mbarriers, so loads run up to four
+// chunks ahead of the MMAs and the MMAs overlap the workers' splitting and
+// epilogues. Every wait is bounded: a timeout sets a block-wide abort flag and
+// the device error flag; every role then skips its remaining work (its
+// waits return at once), the block waits (bounded) for what it already
+// issued, frees its TMEM and returns. The test hook "test_skip_mma" withholds
+// the pass-1 MMAs so that this path runs.
+#include <mutex>
+
+#include "qrb_tc.cuh"
+#include "qrb_tma.cuh"
+
+namespace qrb {
+
+namespace tma {
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && p != nullptr)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      (void)cudaGetLastError();
+  });
+  return fn;
+}
+
+bool encode_f32_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                      const uint64_t* strides, uint32_t box0, uint32_t box1, bool atom32) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encoder();
+  if (fn == nullptr || rank < 2 || rank > 5 || box0 * 4 > 128) return false;
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = i == 0 ? box0 : (i == 1 ? box1 : 1u);
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) gs[i] = strides[i];
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<void*>(base), gd,
+            gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace tma
+
+namespace {
+
+constexpr int KR = 32;        // reflectors per block
+constexpr int TCOLS = 128;    // columns of C per tile
+constexpr int NWORK = 8;      // worker warps
+constexpr int NTH = 32 * (2 + NWORK);
+constexpr int R1 = 32;        // rows per pass-1 chunk
+constexpr int S1 = 4;         // pass-1 ring stages
+constexpr int R2 = 128;       // rows per pass-2 chunk (MMA M)
+constexpr uint32_t BOX1 = R1 * 128;   // one {32 x R1} FP32 box, 4 KiB
+constexpr uint32_t CST = 4 * BOX1;    // C part of a pass-1 stage: 4 boxes = 128 columns
+constexpr uint32_t BOX2 = R2 * 128;   // one {32 x 128} box, 16 KiB
+
+// Shared-memory map (bytes from a 1024-aligned base). A pass-1 stage holds the
+// C chunk (hi after the split), the V hi and lo boxes and the C lo buffer.
+// Pass 2 reuses the pass-1 region once every pass-1 MMA of the tile is done.
+constexpr uint32_t ST1 = CST + 2 * BOX1 + CST;    // 40 KiB
+constexpr uint32_t OFF_S1_VH = CST;
+constexpr uint32_t OFF_S1_VL = CST + BOX1;
+constexpr uint32_t OFF_S1_CL = CST + 2 * BOX1;
+constexpr uint32_t REGION = S1 * ST1;             // 160 KiB
+constexpr uint32_t OFF_V2 = 0;                    // pass 2: 2 stages x (V hi, V lo) boxes
+constexpr uint32_t OFF_STG = 4 * BOX2;            // pass 2: 4 staging boxes (-V W')
+constexpr uint32_t OFF_BH = 8 * BOX2;             // W' hi, K-major, 128 rows x 128 B
+constexpr uint32_t OFF_BL = OFF_BH + TCOLS * 128; // W' lo
+static_assert(OFF_BL + TCOLS * 128 <= REGION, "pass-2 buffers must fit the pass-1 region");
+constexpr uint32_t OFF_T = REGION;                // T, 32 x 33 floats
+constexpr int T_LD = KR + 1;
+constexpr uint32_t OFF_BAR = OFF_T + ((KR * T_LD * 4 + 127) / 128) * 128;
+// mbarriers
+constexpr int B_FULL1 = 0, B_SPLIT1 = B_FULL1 + S1, B_EMPTY1 = B_SPLIT1 + S1,
+              B_D1FULL = B_EMPTY1 + S1, B_B2READY = B_D1FULL + 1, B_V2FULL = B_B2READY + 1,
+              B_V2EMPTY = B_V2FULL + 2, B_ACCFULL = B_V2EMPTY + 2, B_ACCEMPTY = B_ACCFULL + 2,
+              B_TILEDONE = B_ACCEMPTY + 2, B_FIN = B_TILEDONE + 1, NBAR = B_FIN + 1;
+constexpr uint32_t OFF_TMEMV = OFF_BAR + NBAR * 8;
+constexpr uint32_t OFF_ABORT = OFF_TMEMV + 4;
+constexpr uint32_t SMEM_USED = OFF_ABORT + 12;
+constexpr size_t SMEM_BYTES = SMEM_USED + 1024;   // slack for aligning the base
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+
+// TMEM columns: pass 1 accumulates into NP1 partial accumulators of 32
+// columns (chunk ch into partial ch % NP1), summed in FP32 afterwards: the
+// tensor core's accumulation inside an MMA is not rounded to nearest at every
+// add, so one accumulator over thousands of rows drifts ~5x further from FP64
+// than FFMA; eight shorter chains keep it at FFMA's level. D2 buffers at 256
+// and 384.
+constexpr int NP1 = 8;
+constexpr uint32_t TM_COLS = 512;
+constexpr uint32_t TM_D2 = 256;
+constexpr uint32_t IDESC1 = tc::idesc(TCOLS, KR, /*a_mn=*/true, /*b_mn=*/true);
+constexpr uint32_t IDESC2 = tc::idesc(R2, TCOLS, /*a_mn=*/false, /*b_mn=*/false);
+
+// Shared-memory matrix descriptors (sm_100 version field 1) for the two
+// swizzled layouts used here, both with 128-byte rows:
+//  - K-major, 128-byte swizzle (layout type 2: 16-byte units of a row XORed
+//    with the row index mod 8, 8-row atoms of 1024 bytes): sbo = distance
+//    between 8-row M/N groups, lbo unused;
+//  - MN-major 32-bit operands, 128-byte swizzle with 32-byte atoms (layout
+//    type 1: 32-byte units XORed with the row index mod 4, 4-row atoms of 512
+//    bytes; the only MN-major layout kind::tf32 accepts, written by TMA's
+//    128B_ATOM_32B swizzle): lbo = distance between 32-element MN blocks,
+//    sbo = between 4-row K groups.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                          uint32_t layout) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+constexpr uint32_t kLayoutSw128 = 2, kLayoutSw128Atom32 = 1;
+__device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t saddr) {
+  return sdesc(saddr, 16, 1024, kLayoutSw128);
+}
+__device__ __forceinline__ uint64_t sdesc_mn32(uint32_t saddr, uint32_t lbo) {
+  return sdesc(saddr, lbo, 512, kLayoutSw128Atom32);
+}
+
+// 32 consecutive TMEM columns of this warp's lane quarter (no wait).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of 16-byte unit u of row `row` in a 128-byte-swizzled region
+// (rows of 128 bytes, 8-row atoms of 1024 bytes at a 1024-aligned base).
+__device__ __forceinline__ uint32_t sw128(int row, int u) {
+  return (uint32_t)(row * 128 + ((u ^ (row & 7)) << 4));
+}
+
+// Barrier among the worker warps only (named barrier 1), with an OR of a
+// per-thread flag: every worker gets the same answer.
+__device__ __forceinline__ bool workers_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(32 * NWORK)
+      : "memory");
+  return r != 0;
+}
+
+__global__ void __launch_bounds__(NTH, 1)
+k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUtensorMap mC2,
+            const __grid_constant__ CUtensorMap mV1, const __grid_constant__ CUtensorMap mV2,
+            const float* __restrict__ T, int64_t sTb, int m0, int ntiles, int ntc, int j0,
+            int col0, int col_end, int n, int vbuf, int* __restrict__ err, long long wait_limit,
+            int skip_mma) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = tma::smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* sm = smem_raw + (base - raw);
+  float* Ts = reinterpret_cast<float*>(sm + OFF_T);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_TMEMV);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + OFF_ABORT);
+  const uint32_t bar0 = base + OFF_BAR;
+  auto BAR = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = n - j0;
+  const int nch1 = (r + R1 - 1) / R1;
+  const int nch2 = (r + R2 - 1) / R2;
+
+  if (tid == 0) {
+    const uint32_t counts[NBAR] = {1, 1, 1, 1,                          // full1
+                                   NWORK, NWORK, NWORK, NWORK,          // split1
+                                   1, 1, 1, 1,                          // empty1
+                                   1,                                   // d1full
+                                   NWORK,                               // b2ready
+                                   1, 1, 1, 1, 1, 1,                    // v2full, v2empty, accfull
+                                   NWORK, NWORK,                        // accempty
+                                   1, 1};                               // tiledone, fin
+    for (int i = 0; i < NBAR; ++i) tma::mbar_init(BAR(i), counts[i]);
+    tma::mbar_fence_init();
+    *s_abort = 0;
+    tma::prefetch_map(&mC1);
+    tma::prefetch_map(&mV1);
+    tma::prefetch_map(&mV2);
+    tma::prefetch_map(&mC2);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     base + OFF_TMEMV),
+                 "r"(TM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    // ================= TMA producer =================
+    if (lane == 0) {
+      int g1 = 0, g2 = 0, it = 0;
+      int last1[S1] = {-1, -1, -1, -1}, last2[2] = {-1, -1};  // use index of the last load issued
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int m = m0 + t / ntc;
+        const int tc0 = col0 + (t % ntc) * TCOLS;
+        const int nbox = min(4, (col_end - tc0 + 31) / 32);
+        const uint32_t tx1 = (uint32_t)nbox * BOX1 + 2 * BOX1;
+        // the previous tile's pass 2 has released the shared buffers
+        if (it > 0 && *s_abort == 0)
+          tma::mbar_wait_or_abort(BAR(B_TILEDONE), (uint32_t)((it - 1) & 1), wait_limit, s_abort);
+        for (int ch = 0; ch < nch1; ++ch, ++g1) {
+          const int s = g1 % S1, u = g1 / S1;
+          if (*s_abort != 0) continue;
+          if (u > 0 &&
+              !tma::mbar_wait_or_abort(BAR(B_EMPTY1 + s), (uint32_t)((u - 1) & 1), wait_limit,
+                                       s_abort))
+            continue;
+          const uint32_t st = base + (uint32_t)s * ST1, fb = BAR(B_FULL1 + s);
+          const int y = j0 + ch * R1;
+          tma::mbar_expect_tx(fb, tx1);
+          for (int bq = 0; bq < nbox; ++bq)
+            tma::load_3d(st + bq * BOX1, &mC1, fb, tc0 + 32 * bq, y, m);
+          tma::load_4d(st + OFF_S1_VH, &mV1, fb, 0, y, m, 2 * vbuf);
+          tma::load_4d(st + OFF_S1_VL, &mV1, fb, 0, y, m, 2 * vbuf + 1);
+          last1[s] = u;
+        }
+        // pass 2 reuses the pass-1 region: wait until every pass-1 MMA is done
+        if (*s_abort == 0)
+          tma::mbar_wait_or_abort(BAR(B_D1FULL), (uint32_t)(it & 1), wait_limit, s_abort);
+        for (int p = 0; p < nch2; ++p, ++g2) {
+          const int v = g2 & 1, u = g2 >> 1;
+          if (*s_abort != 0) continue;
+          if (u > 0 &&
+              !tma::mbar_wait_or_abort(BAR(B_V2EMPTY + v), (uint32_t)((u - 1) & 1), wait_limit,
+                                       s_abort))
+            continue;
+          const uint32_t st = base + OFF_V2 + (uint32_t)v * 2 * BOX2, fb = BAR(B_V2FULL + v);
+          const int y = j0 + p * R2;
+          tma::mbar_expect_tx(fb, 2 * BOX2);
+          tma::load_4d(st, &mV2, fb, 0, y, m, 2 * vbuf);
+          tma::load_4d(st + BOX2, &mV2, fb, 0, y, m, 2 * vbuf + 1);
+          last2[v] = u;
+        }
+      }
+      if (*s_abort != 0) {
+        // bounded wait for the last load issued into every stage
+        for (int s = 0; s < S1; ++s)
+          if (last1[s] >= 0)
+            tma::mbar_wait_bounded(BAR(B_FULL1 + s), (uint32_t)(last1[s] & 1), wait_limit);
+        for (int v = 0; v < 2; ++v)
+          if (last2[v] >= 0)
+            tma::mbar_wait_bounded(BAR(B_V2FULL + v), (uint32_t)(last2[v] & 1), wait_limit);
+      }
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      int g1 = 0, g2 = 0, it = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        for (int ch = 0; ch < nch1; ++ch, ++g1) {
+          const int s = g1 % S1, u = g1 / S1;
+          if (*s_abort != 0 || skip_mma) continue;
+          if (!tma::mbar_wait_or_abort(BAR(B_SPLIT1 + s), (uint32_t)(u & 1), wait_limit, s_abort))
+            continue;
+          tc::fence_after();
+          const uint32_t st = base + (uint32_t)s * ST1;
+          const uint32_t d1 = tmem + 32u * (uint32_t)(ch % NP1);
+#pragma unroll
+          for (int ks = 0; ks < R1 / 8; ++ks) {
+            const uint64_t ah = sdesc_mn32(st + ks * 1024, BOX1);
+            const uint64_t al = sdesc_mn32(st + OFF_S1_CL + ks * 1024, BOX1);
+            const uint64_t bh = sdesc_mn32(st + OFF_S1_VH + ks * 1024, BOX1);
+            const uint64_t bl = sdesc_mn32(st + OFF_S1_VL + ks * 1024, BOX1);
+            tc::mma_tf32(d1, ah, bh, IDESC1, (ch >= NP1 || ks != 0) ? 1u : 0u);
+            tc::mma_tf32(d1, ah, bl, IDESC1, 1u);
+            tc::mma_tf32(d1, al, bh, IDESC1, 1u);
+          }
+          tc::mma_commit(BAR(B_EMPTY1 + s));
+        }
+        if (*s_abort == 0 && !skip_mma) tc::mma_commit(BAR(B_D1FULL));
+        // pass 2 once the workers have formed W'
+        if (*s_abort == 0)
+          tma::mbar_wait_or_abort(BAR(B_B2READY), (uint32_t)(it & 1), wait_limit, s_abort);
+        for (int p = 0; p < nch2; ++p, ++g2) {
+          const int v = g2 & 1, u = g2 >> 1;
+          if (*s_abort != 0) continue;
+          if (!tma::mbar_wait_or_abort(BAR(B_V2FULL + v), (uint32_t)(u & 1), wait_limit, s_abort))
+            continue;
+          if (u > 0 && !tma::mbar_wait_or_abort(BAR(B_ACCEMPTY + v), (uint32_t)((u - 1) & 1),
+                                                wait_limit, s_abort))
+            continue;
+          tc::fence_after();
+          const uint32_t va = base + OFF_V2 + (uint32_t)v * 2 * BOX2, vl = va + BOX2;
+          const uint32_t d = tmem + TM_D2 + 128u * (uint32_t)v;
+#pragma unroll
+          for (int ks = 0; ks < KR / 8; ++ks) {
+            const uint64_t ah = sdesc_kmajor(va + 32 * ks);
+            const uint64_t al = sdesc_kmajor(vl + 32 * ks);
+            const uint64_t bh = sdesc_kmajor(base + OFF_BH + 32 * ks);
+            const uint64_t bl = sdesc_kmajor(base + OFF_BL + 32 * ks);
+            tc::mma_tf32(d, ah, bh, IDESC2, ks != 0 ? 1u : 0u);
+            tc::mma_tf32(d, ah, bl, IDESC2, 1u);
+            tc::mma_tf32(d, al, bh, IDESC2, 1u);
+          }
+          tc::mma_commit(BAR(B_V2EMPTY + v));
+          tc::mma_commit(BAR(B_ACCFULL + v));
+        }
+      }
+      if (*s_abort != 0) {  // every MMA issued so far has completed before TMEM is freed
+        tc::mma_commit(BAR(B_FIN));
+        tma::mbar_wait_bounded(BAR(B_FIN), 0u, wait_limit);
+      }
+    }
+  } else {
+    // ================= workers =================
+    const int wt = tid - 64;               // 0..255
+    const int q = warp & 3;                // TMEM lane quarter of this warp
+    const int h = (warp - 2) >> 2;         // half of the reflectors / columns
+    const int row = 32 * q + lane;         // TMEM lane = tile column (pass 1) / chunk row (pass 2)
+    const bool issuer = wt == 0;
+    int g1 = 0, g2 = 0, it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int ml = t / ntc, m = m0 + ml;
+      const int tc0 = col0 + (t % ntc) * TCOLS;
+      const int nbox = min(4, (col_end - tc0 + 31) / 32);
+      const float* Tm = T + (int64_t)ml * sTb;
+      for (int e = wt; e < KR * KR; e += 32 * NWORK) Ts[(e >> 5) * T_LD + (e & 31)] = __ldg(Tm + e);
+      workers_sync_or(false);  // T in shared memory for the W' step below
+
+      // ---- pass 1: split each chunk's C boxes into hi (in place) and lo ----
+      const int units = nbox * (int)(BOX1 / 16);
+      for (int ch = 0; ch < nch1; ++ch, ++g1) {
+        const int s = g1 % S1, u = g1 / S1;
+        if (*s_abort != 0) continue;
+        // the chunk has landed (and, transitively, the MMAs of chunk g1 - S1
+        // that last read this stage's lo buffer are done)
+        if (!tma::mbar_wait_or_abort(BAR(B_FULL1 + s), (uint32_t)(u & 1), wait_limit, s_abort))
+          continue;
+        float4* c4 = reinterpret_cast<float4*>(sm + (uint32_t)s * ST1);
+        float4* l4 = reinterpret_cast<float4*>(sm + (uint32_t)s * ST1 + OFF_S1_CL);
+        for (int e = wt; e < units; e += 32 * NWORK) {
+          float4 hi, lo;
+          tc::split4(c4[e], hi, lo);
+          c4[e] = hi;
+          l4[e] = lo;
+        }
+        tma::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) tma::mbar_arrive(BAR(B_SPLIT1 + s));
+      }
+
+      // ---- W' = T^T W ----
+      bool skip = *s_abort != 0 ||
+                  !tma::mbar_wait_or_abort(BAR(B_D1FULL), (uint32_t)(it & 1), wait_limit, s_abort);
+      skip = __any_sync(tc::kFullMask, skip);  // tcgen05.ld below is warp-collective
+      if (!skip) {
+        tc::fence_after();
+        float w[32], wp[32];
+        const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+        tmem_ld32_nowait(tl, w);
+        tmem_wait_ld();
+        const int np = nch1 < NP1 ? nch1 : NP1;
+        for (int pp = 1; pp < np; ++pp) {
+          tmem_ld32_nowait(tl + 32u * (uint32_t)pp, wp);
+          tmem_wait_ld();
+#pragma unroll
+          for (int b = 0; b < 32; ++b) w[b] += wp[b];
+        }
+        float o[16];
+        if (h == 0) {  // W'[a] for a < 16: T[b][a] = 0 for b > a
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float acc = 0.f;
+#pragma unroll
+            for (int b = 0; b < 16; ++b) acc = fmaf(Ts[b * T_LD + i], w[b], acc);
+            o[i] = acc;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float acc = 0.f;
+#pragma unroll
+            for (int b = 0; b < 32; ++b) acc = fmaf(Ts[b * T_LD + 16 + i], w[b], acc);
+            o[i] = acc;
+          }
+        }
+        // B operand of pass 2, K-major: row = tile column, 128 bytes = 32 reflectors
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float4 hi, lo;
+          tc::split4(make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]), hi, lo);
+          const uint32_t off = sw128(row, 4 * h + j);
+          *reinterpret_cast<float4*>(sm + OFF_BH + off) = hi;
+          *reinterpret_cast<float4*>(sm + OFF_BL + off) = lo;
+        }
+        tma::fence_proxy_async();
+        tc::fence_before();
+        __syncwarp();
+        if (lane == 0) tma::mbar_arrive(BAR(B_B2READY));
+      }
+
+      // ---- pass 2 epilogues: C += -(V W') by TMA reduce-add ----
+      for (int p = 0; p < nch2; ++p, ++g2) {
+        const int v = g2 & 1, u = g2 >> 1;
+        bool sk = *s_abort != 0 ||
+                  !tma::mbar_wait_or_abort(BAR(B_ACCFULL + v), (uint32_t)(u & 1), wait_limit,
+                                           s_abort);
+        sk = __any_sync(tc::kFullMask, sk);
+        float d0[32], d1[32];
+        if (!sk) {
+          tc::fence_after();
+          const uint32_t ta =
+              tmem + ((uint32_t)(32 * q) << 16) + TM_D2 + 128u * (uint32_t)v + 64u * (uint32_t)h;
+          tmem_ld32_nowait(ta, d0);
+          tmem_ld32_nowait(ta + 32, d1);
+          tmem_wait_ld();
+          tc::fence_before();
+          __syncwarp();
+          if (lane == 0) tma::mbar_arrive(BAR(B_ACCEMPTY + v));
+        }
+        if (issuer) tma::bulk_wait_read_all();  // the previous reduce has read the staging tile
+        if (workers_sync_or(sk || *s_abort != 0)) continue;
+#pragma unroll
+        for (int uu = 0; uu < 8; ++uu) {
+          *reinterpret_cast<float4*>(sm + OFF_STG + (2 * h) * BOX2 + sw128(row, uu)) =
+              make_float4(-d0[4 * uu], -d0[4 * uu + 1], -d0[4 * uu + 2], -d0[4 * uu + 3]);
+          *reinterpret_cast<float4*>(sm + OFF_STG + (2 * h + 1) * BOX2 + sw128(row, uu)) =
+              make_float4(-d1[4 * uu], -d1[4 * uu + 1], -d1[4 * uu + 2], -d1[4 * uu + 3]);
+        }
+        tma::fence_proxy_async();
+        workers_sync_or(false);
+        if (issuer) {
+          for (int bq = 0; bq < nbox; ++bq)
+            tma::reduce_add_3d(&mC2, base + OFF_STG + bq * BOX2, tc0 + 32 * bq, j0 + R2 * p, m);
+          tma::bulk_commit();
+        }
+      }
+      if (issuer) {  // the tile's buffers are free once the last reduce has read its staging
+        tma::bulk_wait_read_all();
+        tma::mbar_arrive(BAR(B_TILEDONE));
+      }
+    }
+    if (issuer) tma::bulk_wait_all();  // every reduce-add has completed
+  }
+
+  // ---------------- teardown ----------------
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  if (tid == 0 && *s_abort != 0) atomicExch(err, 1);
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_COLS)
+                 : "memory");
+}
+
+// Test probe of the bounded wait: one thread waits on an mbarrier phase that
+// nothing completes, for `limit` cycles, then records the timeout in the
+// device error flag and returns.
+__global__ void k_wait_probe(int* __restrict__ err, long long limit) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = tma::smem_addr(&bar);
+  tma::mbar_init(b, 1);
+  tma::mbar_fence_init();
+  if (!tma::mbar_wait_bounded(b, 0u, limit)) atomicExch(err, 1);
+}
+
+}  // namespace
+
+int launch_wait_probe(long long limit, cudaStream_t stream) {
+  int* err = nullptr;
+  if (device_error_ptr(&err) != QRB_OK) return QRB_ERR_DEVICE;
+  k_wait_probe<<<1, 1, 0, stream>>>(err, limit);
+  note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
+}
+
+bool larfb_tma_supported(int n) { return n % 4 == 0 && n > KR && tma::encoder() != nullptr; }
+
+int make_larfb_maps(LarfbMaps* maps, const float* H, const float* Vs, int64_t batch, int n) {
+  if (maps == nullptr || H == nullptr || Vs == nullptr || batch <= 0 || n % 4 != 0 ||
+      batch > 0x7fffffffLL)
+    return QRB_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(H) & 15) != 0 || (reinterpret_cast<uintptr_t>(Vs) & 15) != 0)
+    return QRB_ERR_UNSUPPORTED;
+  const uint64_t nn = (uint64_t)n;
+  const uint64_t cdims[3] = {nn, nn, (uint64_t)batch};
+  const uint64_t cstr[2] = {nn * 4, nn * nn * 4};
+  const uint64_t vdims[4] = {(uint64_t)KR, nn, (uint64_t)batch, 4};
+  const uint64_t vstr[3] = {KR * 4, nn * KR * 4, (uint64_t)batch * nn * KR * 4};
+  // pass-1 boxes are MN-major operands (32-byte-atom swizzle); pass-2 V boxes
+  // are K-major operands and the C boxes take the staged reduce-add (plain
+  // 128-byte swizzle)
+  const bool ok = tma::encode_f32_sw128(&maps->c1, H, 3, cdims, cstr, 32, R1, true) &&
+                  tma::encode_f32_sw128(&maps->c2, H, 3, cdims, cstr, 32, R2, false) &&
+                  tma::encode_f32_sw128(&maps->v1, Vs, 4, vdims, vstr, 32, R1, true) &&
+                  tma::encode_f32_sw128(&maps->v2, Vs, 4, vdims, vstr, 32, R2, false);
+  return ok ? QRB_OK : QRB_ERR_UNSUPPORTED;
+}
+
+int launch_larfb_tma(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
+                     int64_t count, int j0, int col0, int col_end, int n, int vbuf,
+                     cudaStream_t stream) {
+  if (count <= 0 || col_end <= col0) return QRB_OK;
+  if (j0 < 0 || j0 + KR > n || col0 % 4 != 0 || m0 < 0 || m0 + count > 0x7fffffffLL)
+    return QRB_ERR_UNSUPPORTED;
+  if (col_end != n && (col_end - col0) % 32 != 0) return QRB_ERR_UNSUPPORTED;
+  static bool attr_set[64] = {};
+  static int* err_ptr[64] = {};
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(k_larfb_tma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)SMEM_BYTES) != cudaSuccess)
+      return QRB_ERR_LAUNCH;
+    if (device_error_ptr(&err_ptr[dev]) != QRB_OK) return QRB_ERR_DEVICE;
+    if (cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms[dev] <= 0)
+      return QRB_ERR_DEVICE;
+    attr_set[dev] = true;
+  }
+  const int64_t ntc = (col_end - col0 + TCOLS - 1) / TCOLS;
+  const int64_t tiles = ntc * count;
+  if (tiles > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
+  const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);  // persistent: <= one CTA per SM
+  k_larfb_tma<<<grid, NTH, SMEM_BYTES, stream>>>(maps.c1, maps.c2, maps.v1, maps.v2, T, sTb,
+                                                 (int)m0, (int)tiles, (int)ntc, j0, col0,
+                                                 col_end, n, vbuf, err_ptr[dev],
+                                                 device_wait_limit(), test_skip_mma() ? 1 : 0);
+  note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
+}
+
+}  // namespace qrb

@@ -11,6 +11,7 @@ namespace qrb {
 namespace tc {
 
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 2 GHz
+constexpr unsigned kFullMask = 0xffffffffu;
 
 // Instruction descriptors (kind::tf32, FP32 accumulate, dense).
 constexpr uint32_t idesc(int M, int N, bool a_mn, bool b_mn) {

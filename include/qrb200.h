@@ -60,10 +60,13 @@ QRB_API const char* qrb_status_string(int status);
 /* Largest n that qrb_geqrf_f32 accepts. */
 QRB_API int32_t qrb_max_n(void);
 
-/* Bytes of device workspace to give qrb_geqrf_f32 for (batch, n): four
- * 32 x 32 units (16 KiB) per matrix when n > 32, 0 otherwise. A quarter of it
- * (one T factor per matrix) is the minimum accepted; half enables the panel
- * look-ahead ("lookahead" below), all of it two-level blocking ("two_level"). */
+/* Bytes of device workspace to give qrb_geqrf_f32 for (batch, n): 0 for
+ * n <= 32; otherwise four 32 x 32 units (16 KiB) per matrix, plus, for
+ * n >= 129 with n % 4 == 0, the split reflectors of the tensor-core trailing
+ * update (two buffers of n x 32 high parts and n x 32 remainders, 512 * n
+ * bytes per matrix). One 32 x 32 unit per matrix is the minimum accepted;
+ * two enable the panel look-ahead ("lookahead" below), four two-level
+ * blocking ("two_level"), the whole amount the tensor-core update. */
 QRB_API size_t qrb_workspace_bytes(int64_t batch, int32_t n);
 
 /*
@@ -75,6 +78,7 @@ QRB_API size_t qrb_workspace_bytes(int64_t batch, int32_t n);
  *              3 = blocked panel route;
  *   bits 4-7   blocked trailing update: 0 = FP32 FFMA; 1 = tcgen05 3xTF32 with
  *              operands staged by the CUDA cores; 2 = FFMA then tcgen05;
+ *              3 = tcgen05 3xTF32 fed by TMA;
  *   bit 8      panel look-ahead on a second stream;
  *   bit 9      two-level (64-reflector) blocking;
  *   bits 12-15 batch groups on internal streams.
@@ -269,11 +273,23 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *   "sync_check"  1: every compute call synchronises its stream and reports
  *                 asynchronous kernel faults as QRB_ERR_LAUNCH and device-side
  *                 wait timeouts as QRB_ERR_DEVICE_WAIT (debug mode).
- *   "larfb_kind"  trailing update: 0 (default) = FP32 FFMA; 1 = tcgen05
- *                 tensor cores in 3xTF32 for both products; 2 = FFMA for
- *                 V^T C and tcgen05 3xTF32 for C -= V W'. Kinds 1 and 2 apply
- *                 to 32-reflector blocks with 16-byte aligned row-major
- *                 operands; FFMA elsewhere.
+ *   "larfb_kind"  trailing update of the blocked route: -1 (default) =
+ *                 automatic (3 where it applies, else 0); 0 = FP32 FFMA;
+ *                 1 = tcgen05 3xTF32 for both products with operands staged
+ *                 by the CUDA cores; 2 = FFMA for V^T C and tcgen05 3xTF32 for
+ *                 C -= V W'; 3 = tcgen05 3xTF32 fed by TMA (n >= 129,
+ *                 n % 4 == 0 and the full qrb_workspace_bytes, else FFMA).
+ *                 Kinds 1 and 2 apply to 32-reflector blocks with 16-byte
+ *                 aligned row-major operands; FFMA elsewhere.
+ *   "wait_limit"  clock cycles a kernel's bounded device-side wait lasts
+ *                 before it gives up (default 2e9, about one second).
+ *   "wait_probe"  value = a cycle limit: runs one probe kernel (synchronously,
+ *                 on the legacy stream) whose bounded wait nothing completes,
+ *                 so it times out and sets "device_error" (test only).
+ *   "test_skip_mma" 1: the TMA-fed update withholds its first MMAs, so its
+ *                 bounded waits run out, it abandons the call, sets
+ *                 "device_error" and frees its resources (test only; results
+ *                 of such calls are wrong).
  *   "device_error" read: 1 if a kernel's bounded device-side wait timed out
  *                 since the last reset (synchronous); set to 0 to reset.
  *   "groups"      1..4: batches of 4 or more matrices with n > 32 are split

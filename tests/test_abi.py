@@ -60,6 +60,11 @@ def test_workspace_bytes():
     assert L.qrb_workspace_bytes(4096, 32) == 0
     assert L.qrb_workspace_bytes(8, 64) == 4 * 8 * 32 * 32 * 4
     assert L.qrb_workspace_bytes(0, 512) == 0
+    # from n = 129 with n % 4 == 0: plus two buffers of split reflectors
+    # (hi and lo, n x 32 each) for the tensor-core update
+    assert L.qrb_workspace_bytes(8, 128) == 4 * 8 * 32 * 32 * 4
+    assert L.qrb_workspace_bytes(8, 130) == 4 * 8 * 32 * 32 * 4
+    assert L.qrb_workspace_bytes(8, 4096) == 4 * 8 * 32 * 32 * 4 + 4 * 8 * 4096 * 32 * 4
 
 
 def test_host_entry_workspace_and_validation_without_gpu():
@@ -183,12 +188,24 @@ def test_config_keys():
     _lib.set_config("sync_check", 0)
     _lib.set_config("launches", 0)
     assert _lib.get_config("launches") == 0
-    assert _lib.get_config("larfb_kind") in (0, 1, 2)
-    _lib.set_config("larfb_kind", 2)
-    assert _lib.get_config("larfb_kind") == 2
-    _lib.set_config("larfb_kind", 0)
+    assert _lib.get_config("larfb_kind") == -1  # automatic
+    for v in (0, 1, 2, 3, -1):
+        _lib.set_config("larfb_kind", v)
+        assert _lib.get_config("larfb_kind") == v
+    for bad in (4, -2):
+        with pytest.raises(_lib.QRBError):
+            _lib.set_config("larfb_kind", bad)
+    assert _lib.get_config("wait_limit") == 2_000_000_000
+    _lib.set_config("wait_limit", 5000)
+    assert _lib.get_config("wait_limit") == 5000
+    _lib.set_config("wait_limit", 2_000_000_000)
     with pytest.raises(_lib.QRBError):
-        _lib.set_config("larfb_kind", 3)
+        _lib.set_config("wait_limit", 10)
+    assert _lib.get_config("test_skip_mma") == 0
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("test_skip_mma", 2)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("wait_probe", 10)
     assert _lib.get_config("host_direct") in (0, 1, 2, 3)
     _lib.set_config("host_direct", 0)
     assert _lib.get_config("host_direct") == 0
@@ -277,6 +294,11 @@ def test_route_is_a_function_of_batch_n_and_workspace():
     assert L.qrb_route(8, 4096, 0) == 0  # the blocked route needs workspace
     code = L.qrb_route(8, 4096, ws)
     assert code & 0xF == 3 and (code >> 12) & 0xF == 4
+    # the tensor-core update needs the split-reflector part of the workspace
+    # (and, on a machine without a CUDA driver, the TMA encoder: FFMA then)
+    assert (code >> 4) & 0xF in (0, 3)
+    assert (L.qrb_route(8, 4096, 4 * 8 * 32 * 32 * 4) >> 4) & 0xF == 0
+    assert (L.qrb_route(8, 130, L.qrb_workspace_bytes(8, 130)) >> 4) & 0xF == 0
     assert L.qrb_route(8, 4096, ws) == code  # no hidden state between queries
     assert api.route(640, 512).startswith("blocked:")
     assert api.route(4096, 32) == "fused_warp"

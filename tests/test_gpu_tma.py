@@ -1,0 +1,215 @@
+"""The TMA-fed tcgen05 (3xTF32) trailing update inside the blocked route.
+
+Parity: every factorization passes the FP64 gates; H and tau agree with the
+FP64 oracle within 1e-4 of max|H|, the bar of the other kernel tests, and with
+CPU LAPACK within the north-star 1e-3; against FP64 LAPACK the tensor-core
+route stays within 1e-4 (H) as the FFMA route does. The look-ahead split and
+the batch groups leave the bits unchanged, the route falls back to FFMA where
+the update cannot run (n % 4 != 0, too little workspace), and the bounded
+device-side waits time out into an error status, not a hang.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpumode_qr_b200 import _lib, api, checker
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+RTOL = 1e-4
+
+
+def _hooks(**kv):
+    old = {k: _lib.get_config(k) for k in kv}
+    for k, v in kv.items():
+        _lib.set_config(k, v)
+    return old
+
+
+def _restore(old):
+    for k, v in old.items():
+        _lib.set_config(k, v)
+
+
+@pytest.mark.parametrize("b,n", [(3, 160), (2, 256), (5, 300), (3, 512), (2, 1024)])
+def test_tma_route_matches_the_fp64_oracle(b, n):
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(7 * n + b))
+    assert "tcgen05_tma" in api.route(b, n)
+    H, tau = api.geqrf(A.to(DEV))
+    torch.cuda.synchronize()
+    assert checker.check(A, H.cpu(), tau.cpu()).passed
+    k = min(b, 2)
+    Ho, to = oracle.geqr2(A[:k].numpy(), f64=True)
+    par = checker.parity(H[:k].cpu(), tau[:k].cpu(), Ho, to)
+    assert par.ok(RTOL), par
+    assert (tau[:, -1] == 0).all()
+    assert _lib.get_config("device_error") == 0
+
+
+@pytest.mark.parametrize("n", [132, 256, 384, 640, 1000, 1028, 2048])
+def test_tma_route_agrees_with_ffma(n):
+    # Both FP32 routes against FP64 LAPACK on the same inputs: the tensor-core
+    # route stays within 1e-4 of max|H| (and tau within 5e-4) of FP64, as
+    # FFMA does; the two agree with each other in H within 1e-4. tau of the
+    # last columns is the most rounding-sensitive output at large n (FFMA
+    # itself sits ~1e-4 from LAPACK there), so their mutual tau bar is the
+    # north-star 1e-3.
+    b = 4 if n <= 1028 else 2
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(n)).to(DEV)
+    old = _hooks(larfb_kind=0)
+    try:
+        Hf, tf = api.geqrf(A)
+        _lib.set_config("larfb_kind", 3)
+        Ht, tt = api.geqrf(A)
+        torch.cuda.synchronize()
+    finally:
+        _restore(old)
+    assert checker.check(A, Ht, tt).passed
+    H64, t64 = torch.geqrf(A.cpu().double())
+    pf = checker.parity(Hf.cpu(), tf.cpu(), H64.float(), t64.float())
+    pt = checker.parity(Ht.cpu(), tt.cpu(), H64.float(), t64.float())
+    print(f"n={n}: tensor-core route vs FP64 {pt}; FFMA vs FP64 {pf}")
+    assert pf.h_rel < RTOL and pt.h_rel < RTOL and pt.col_rel < RTOL, (n, pt, pf)
+    assert pt.tau_rel < 5e-4, (n, pt, pf)
+    par = checker.parity(Ht.cpu(), tt.cpu(), Hf.cpu(), tf.cpu())
+    assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 1e-3, (n, par)
+
+
+def test_tma_route_matches_lapack_on_config_3_shape():
+    # config 3's matrix type (Haar, cond 1e2) on a slice of its batch
+    from gpumode_qr_b200 import inputs
+
+    cfg = inputs.config(3)
+    A = inputs.make_config_input(cfg, 16)
+    H, tau = api.geqrf(A.to(DEV))
+    Hl, tl = oracle.lapack_geqrf(A)
+    par = checker.parity(H.cpu(), tau.cpu(), torch.from_numpy(Hl), torch.from_numpy(tl))
+    assert par.ok(), par
+    assert checker.check(A, H.cpu(), tau.cpu()).passed
+
+
+def test_tma_lookahead_and_groups_leave_bits_unchanged():
+    A = torch.randn(8, 512, 512, generator=torch.Generator().manual_seed(3)).to(DEV)
+    outs = []
+    old = _hooks(lookahead=0, groups=1)
+    try:
+        for la, g in ((0, 1), (1, 1), (0, 4), (1, 4), (1, 2)):
+            _lib.set_config("lookahead", la)
+            _lib.set_config("groups", g)
+            assert "tcgen05_tma" in api.route(8, 512)
+            outs.append(api.geqrf(A))
+        torch.cuda.synchronize()
+    finally:
+        _restore(old)
+    for H, tau in outs[1:]:
+        assert torch.equal(H, outs[0][0]) and torch.equal(tau, outs[0][1])
+
+
+def test_tma_route_in_place_and_strided_inputs():
+    n = 256
+    g = torch.Generator().manual_seed(11)
+    A = torch.randn(3, n, n, generator=g).to(DEV)
+    H_ref, t_ref = api.geqrf(A)
+    # in place: H is A itself
+    Ai = A.clone()
+    tau = torch.empty(3, n, device=DEV)
+    api.geqrf_out(Ai, Ai, tau)
+    assert torch.equal(Ai, H_ref) and torch.equal(tau, t_ref)
+    # A viewed with a larger batch stride (the copy into H runs per matrix)
+    big = torch.zeros(3, n + 8, n, device=DEV)
+    big[:, :n] = A
+    H2, t2 = api.geqrf(big[:, :n])
+    assert torch.equal(H2, H_ref) and torch.equal(t2, t_ref)
+    # a row stride larger than n
+    wide = torch.zeros(3, n, n + 4, device=DEV)
+    wide[:, :, :n] = A
+    H3, t3 = api.geqrf(wide[:, :, :n])
+    assert torch.equal(H3, H_ref) and torch.equal(t3, t_ref)
+
+
+@pytest.mark.parametrize("n", [130, 258])
+def test_rows_not_16_byte_aligned_use_ffma(n):
+    assert "ffma" in api.route(3, n)
+    A = torch.randn(3, n, n, generator=torch.Generator().manual_seed(n))
+    H, tau = api.geqrf(A.to(DEV))
+    assert checker.check(A, H.cpu(), tau.cpu()).passed
+
+
+def test_too_little_workspace_uses_ffma():
+    b, n = 2, 256
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(5)).to(DEV)
+    H_ref, t_ref = api.geqrf(A)
+    small = 4 * b * 32 * 32 * 4  # the T factors only
+    assert "ffma" in api.route(b, n, small)
+    H = torch.empty_like(A)
+    tau = torch.empty(b, n, device=DEV)
+    ws = torch.empty(small, dtype=torch.uint8, device=DEV)
+    _lib.check(_lib.lib().qrb_geqrf_f32(A.data_ptr(), A.stride(0), A.stride(1), H.data_ptr(),
+                                        tau.data_ptr(), b, n, ws.data_ptr(), small,
+                                        torch.cuda.current_stream().cuda_stream))
+    par = checker.parity(H.cpu(), tau.cpu(), H_ref.cpu(), t_ref.cpu())
+    assert par.ok(RTOL), par
+
+
+def test_tma_many_tiles_per_cta():
+    # more tiles than SMs: each persistent CTA walks several (matrix, column
+    # tile) items, including the column-limited tiles of the look-ahead
+    b, n = 40, 768
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(12))
+    old = _hooks(lookahead=1)
+    try:
+        H, tau = api.geqrf(A.to(DEV))
+        torch.cuda.synchronize()
+    finally:
+        _restore(old)
+    assert checker.check(A[:4], H[:4].cpu(), tau[:4].cpu()).passed
+    Hl, tl = oracle.lapack_geqrf(A[:4])
+    par = checker.parity(H[:4].cpu(), tau[:4].cpu(), torch.from_numpy(Hl), torch.from_numpy(tl))
+    assert par.ok(), par
+    assert _lib.get_config("device_error") == 0
+
+
+def test_bounded_wait_probe_times_out_into_the_error_flag():
+    _lib.set_config("device_error", 0)
+    _lib.set_config("wait_probe", 2_000_000)  # ~1 ms; nothing completes the barrier
+    assert _lib.get_config("device_error") == 1
+    _lib.set_config("device_error", 0)
+    A = torch.randn(2, 256, 256, generator=torch.Generator().manual_seed(1))
+    H, tau = api.geqrf(A.to(DEV))  # the context is still usable
+    assert checker.check(A, H.cpu(), tau.cpu()).passed
+
+
+def test_tma_update_abandons_a_call_whose_waits_run_out():
+    # the update withholds its MMAs: its bounded waits run out, it sets the
+    # error flag, waits for its own copies, frees TMEM and returns; with
+    # sync_check the call reports QRB_ERR_DEVICE_WAIT, and the next call works
+    A = torch.randn(2, 256, 256, generator=torch.Generator().manual_seed(2)).to(DEV)
+    _lib.set_config("device_error", 0)
+    old = _hooks(wait_limit=2_000_000, test_skip_mma=1, sync_check=1)
+    try:
+        with pytest.raises(_lib.QRBError) as exc:
+            api.geqrf(A)
+        assert exc.value.status == 7
+    finally:
+        _restore(old)
+    assert _lib.get_config("device_error") == 1
+    _lib.set_config("device_error", 0)
+    H, tau = api.geqrf(A)
+    torch.cuda.synchronize()
+    assert checker.check(A, H, tau).passed
+    assert _lib.get_config("device_error") == 0
+
+
+def test_tma_route_nan_input_propagates():
+    A = torch.randn(2, 256, 256, generator=torch.Generator().manual_seed(4))
+    A[1, 100, 7] = float("nan")
+    H, tau = api.geqrf(A.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.isfinite(H[0]).all()
+    assert not torch.isfinite(H[1]).all()
+    assert np.isfinite(tau[0].cpu().numpy()).all()
+    assert _lib.get_config("device_error") == 0
