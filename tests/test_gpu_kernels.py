@@ -321,17 +321,18 @@ def test_two_level_blocking_matches_one_level(n, groups):
     # n % 4 != 0 takes the aligned-operand fallback (two 32-wide updates).
     b = 4
     A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(2 * n + groups)).to(DEV)
-    old = {k: _lib.get_config(k) for k in ("two_level", "groups", "mid_fused")}
+    old = {k: _lib.get_config(k) for k in ("two_level", "groups", "mid_fused", "larfb_kind")}
     outs = {}
     try:
         _lib.set_config("groups", groups)
         _lib.set_config("mid_fused", 0)
+        _lib.set_config("larfb_kind", 0)  # two-level blocking runs on the FFMA update
         for tl in (0, 1):
             _lib.set_config("two_level", tl)
             outs[tl] = api.geqrf(A)
             torch.cuda.synchronize()
         # a two-factor workspace cannot hold the 64 x 64 factor: one-level route
-        ws_two = api.workspace_bytes(b, n) // 2
+        ws_two = 2 * b * 32 * 32 * 4
         ws = torch.empty(ws_two, dtype=torch.uint8, device=DEV)
         H = torch.empty_like(A)
         tau = torch.empty(b, n, device=DEV)
