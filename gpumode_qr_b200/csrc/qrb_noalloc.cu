@@ -21,7 +21,8 @@
 // order them, or use qrb_geqrf_f32 with separate workspaces.
 //
 // The device address of the array is looked up once per device, by the first
-// call made on that device (cudaGetSymbolAddress with that device current). A
+// call made on that device (cudaGetSymbolAddress with that device current); a
+// lookup that fails is retried by the next call. A
 // host-side use of the array's name would only be a host stand-in, never the
 // device address, so only the looked-up pointer is ever handed to kernels.
 // Make that first call before any stream capture begins.
@@ -38,27 +39,29 @@ constexpr int64_t kNoAllocMaxBatch = int64_t(kNoAllocScratchBytes) / kTBytesPerM
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_once[kMaxDevices];
-void* g_scratch_ptr[kMaxDevices] = {};
-cudaError_t g_scratch_err[kMaxDevices] = {};
+std::mutex g_lookup_mu;
+void* g_scratch_ptr[kMaxDevices] = {};  // set only after a successful lookup
 
-// Device address of the scratch array on the current device (looked up on the
-// first call per device), or nullptr with *err set.
+// Device address of the scratch array on the current device, looked up by the
+// first call on that device that succeeds in doing so; a failed lookup (for
+// example one attempted during a stream capture) is not remembered, its CUDA
+// error is cleared, and the next call tries again. nullptr with *status set
+// on failure.
 void* scratch_for_current_device(int* status) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     *status = QRB_ERR_DEVICE;
     return nullptr;
   }
-  std::call_once(g_once[dev], [dev] {
+  std::lock_guard<std::mutex> lock(g_lookup_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    g_scratch_err[dev] = e;
-    g_scratch_ptr[dev] = (e == cudaSuccess) ? p : nullptr;
-  });
-  if (g_scratch_err[dev] != cudaSuccess || g_scratch_ptr[dev] == nullptr) {
-    *status = QRB_ERR_DEVICE;
-    return nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();
+      *status = QRB_ERR_DEVICE;
+      return nullptr;
+    }
+    g_scratch_ptr[dev] = p;
   }
   *status = QRB_OK;
   return g_scratch_ptr[dev];
