@@ -87,6 +87,9 @@ struct TmaRoute {
     return Vs + ((int64_t)(2 * buf) * batch_total + m0) * n * qrb::kPanelW;
   }
   int64_t plane(int n) const { return batch_total * n * qrb::kPanelW; }
+  // two-level blocks: hi plane [batch][n][64] at this group's first matrix
+  float* vsplit64(int n) const { return Vs + m0 * n * 2 * qrb::kPanelW; }
+  int64_t plane64(int n) const { return batch_total * n * 2 * qrb::kPanelW; }
 };
 
 // The blocked factorization of one contiguous group of matrices on `s`:
@@ -200,7 +203,7 @@ int blocked_qr_lookahead(const float* A, int64_t strideA_b, int64_t strideA_row,
 // Where the 64-wide update's operands are not 16-byte aligned, the two panels
 // are applied one after the other instead (the same product).
 int blocked_qr2(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
-                float* T64, int64_t batch, int n, cudaStream_t s) {
+                float* T64, int64_t batch, int n, cudaStream_t s, const TmaRoute* tr = nullptr) {
   const int64_t nn = (int64_t)n * n;
   constexpr int W = qrb::kPanelW;
   constexpr int K2 = 2 * W;
@@ -209,25 +212,36 @@ int blocked_qr2(const float* A, int64_t strideA_b, int64_t strideA_row, float* H
   float* T2 = T64 + W * K2 + W;
   for (int j0 = 0; j0 < n; j0 += K2) {
     const int r = n - j0;
-    const float* src = (j0 == 0) ? A : H;
-    const int64_t sb = (j0 == 0) ? strideA_b : nn;
-    const int64_t ld = (j0 == 0) ? strideA_row : n;
+    const bool first = j0 == 0 && tr == nullptr;
+    const float* src = first ? A : H;
+    const int64_t sb = first ? strideA_b : nn;
+    const int64_t ld = first ? strideA_row : n;
     float* Hp = H + (int64_t)j0 * n + j0;
     const float* Sp = src + (int64_t)j0 * ld + j0;
     const int w1 = r < W ? r : W;
+    // tensor-core route: both panels write their split reflectors into one
+    // 64-wide plane when a 64-reflector update follows
+    const bool big = tr != nullptr && r > K2;
+    float* vs = big ? tr->vsplit64(n) : nullptr;
+    const int64_t vpl = tr != nullptr ? tr->plane64(n) : 0;
     int rc = qrb::launch_panel(Sp, sb, ld, Hp, nn, n, tau + j0, n, T1, tsb, K2, nullptr, batch,
-                               r, w1, s);
+                               r, w1, s, vs, (int64_t)n * K2, vpl, j0, K2, big);
     if (rc != QRB_OK || r <= W) return rc;
     const int w2 = r - W < W ? r - W : W;
     rc = larfb_any(Hp, nn, n, T1, tsb, K2, Sp + W, sb, ld, Hp + W, nn, n, batch, r, W, w2, s);
     if (rc != QRB_OK) return rc;
     float* Hq = Hp + (int64_t)W * n + W;
     rc = qrb::launch_panel(Hq, nn, n, Hq, nn, n, tau + j0 + W, n, T2, tsb, K2, nullptr, batch,
-                           r - W, w2, s);
+                           r - W, w2, s, big ? vs + W : nullptr, (int64_t)n * K2, vpl, j0 + W, K2,
+                           false);
     if (rc != QRB_OK) return rc;
     const int c = r - K2;
     if (c <= 0) continue;
-    if (qrb::larfb64_supported(Hp, nn, n, Sp + K2, sb, ld, Hp + K2, nn, n, c)) {
+    if (big) {
+      rc = qrb::launch_t64(Hp, nn, n, T64, tsb, batch, r, s);
+      if (rc == QRB_OK)
+        rc = qrb::launch_larfb_tma(*tr->maps, T64, tsb, tr->m0, batch, j0, j0 + K2, n, n, 0, s);
+    } else if (qrb::larfb64_supported(Hp, nn, n, Sp + K2, sb, ld, Hp + K2, nn, n, c)) {
       rc = qrb::launch_t64(Hp, nn, n, T64, tsb, batch, r, s);
       if (rc != QRB_OK) return rc;
       rc = qrb::launch_larfb64(Hp, nn, n, T64, tsb, Sp + K2, sb, ld, Hp + K2, nn, n, batch, r,
@@ -370,7 +384,6 @@ Plan make_plan(int64_t batch, int n, const FactorScratch& ws) {
   // 64 x 64 factor per matrix, the look-ahead a second 32 x 32 one; two-level
   // takes precedence.
   p.two_level = ws.T64 != nullptr && g_two_level.load() == 1;
-  if (p.two_level && p.larfb == kLarfbTma) p.larfb = kLarfbFfma;  // two-level runs on FFMA
   const int64_t la_mode = g_lookahead.load();
   p.lookahead = !p.two_level && ws.T2 != nullptr &&
                 (la_mode == 1 || (la_mode == 2 && n >= kLookaheadMinN));
@@ -422,7 +435,7 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
       strideA_b = nn;
       strideA_row = n;
     }
-    const int rc = make_larfb_maps(&maps, H, ws.Vs, batch, n);
+    const int rc = make_larfb_maps(&maps, H, ws.Vs, batch, n, tl ? 64 : 32);
     if (rc != QRB_OK) return rc;
   }
   auto route_of = [&](int64_t m0) {
@@ -434,8 +447,10 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     return r;
   };
   if (groups <= 1 && !la) {
-    if (tl) return blocked_qr2(A, strideA_b, strideA_row, H, tau, ws.T64, batch, n, s);
     const TmaRoute r0 = route_of(0);
+    if (tl)
+      return blocked_qr2(A, strideA_b, strideA_row, H, tau, ws.T64, batch, n, s,
+                         tma ? &r0 : nullptr);
     return blocked_qr(A, strideA_b, strideA_row, H, tau, ws.T, batch, n, s, tma ? &r0 : nullptr);
   }
   SideStreams* ss = side_streams();
@@ -463,7 +478,7 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     const TmaRoute rg = route_of(b0);
     if (tl)
       rc = blocked_qr2(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
-                       ws.T64 + b0 * 4 * tper, b1 - b0, n, gs);
+                       ws.T64 + b0 * 4 * tper, b1 - b0, n, gs, tma ? &rg : nullptr);
     else if (la)
       rc = blocked_qr_lookahead(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn,
                                 tau + b0 * n, ws.T + b0 * tper, ws.T2 + b0 * tper, b1 - b0, n,

@@ -100,13 +100,16 @@ bool mid_fused_always();
 // unit-lower reflectors (r x w, contiguous per matrix).
 // Vsplit, when non-null (w == 32 only), receives the unit-lower reflectors
 // split into a TF32 high part (row vs_row0 + i of matrix m at
-// Vsplit + m * vs_mat + (vs_row0 + i) * 32) and the TF32-rounded remainder
-// (vs_plane floats further on): the operands of the tensor-core update.
+// Vsplit + m * vs_mat + (vs_row0 + i) * vs_ld, 32 floats) and the
+// TF32-rounded remainder (vs_plane floats further on): the operands of the
+// tensor-core update. vs_zero also writes zeros into the 32 floats after each
+// of the first 32 rows (where a second panel's reflectors vanish).
 int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
                  int64_t sb_dst, int64_t ld_dst, float* tau_out, int64_t tau_sb,
                  float* T_out, int64_t T_sb, int t_ld, float* V_out,
                  int64_t batch, int r, int w, cudaStream_t stream, float* Vsplit = nullptr,
-                 int64_t vs_mat = 0, int64_t vs_plane = 0, int vs_row0 = 0);
+                 int64_t vs_mat = 0, int64_t vs_plane = 0, int vs_row0 = 0, int vs_ld = 32,
+                 bool vs_zero = false);
 
 // C_dst <- C_src - V T^T V^T C_src for r x c blocks, k <= 32 reflectors whose
 // strictly-lower part is read from V (unit diagonal implied). T is 32 x 32 per

@@ -84,7 +84,6 @@ bool encode_f32_sw128(CUtensorMap* map, const void* base, int rank, const uint64
 
 namespace {
 
-constexpr int KR = 32;        // reflectors per block
 constexpr int TCOLS = 128;    // columns of C per tile
 constexpr int NWORK = 8;      // worker warps
 constexpr int NTH = 32 * (2 + NWORK);
@@ -94,44 +93,49 @@ constexpr int R2 = 128;       // rows per pass-2 chunk (MMA M)
 constexpr uint32_t BOX1 = R1 * 128;   // one {32 x R1} FP32 box, 4 KiB
 constexpr uint32_t CST = 4 * BOX1;    // C part of a pass-1 stage: 4 boxes = 128 columns
 constexpr uint32_t BOX2 = R2 * 128;   // one {32 x 128} box, 16 KiB
-
-// Shared-memory map (bytes from a 1024-aligned base). A pass-1 stage holds the
-// C chunk (hi after the split), the V hi and lo boxes and the C lo buffer.
-// Pass 2 reuses the pass-1 region once every pass-1 MMA of the tile is done.
-constexpr uint32_t ST1 = CST + 2 * BOX1 + CST;    // 40 KiB
-constexpr uint32_t OFF_S1_VH = CST;
-constexpr uint32_t OFF_S1_VL = CST + BOX1;
-constexpr uint32_t OFF_S1_CL = CST + 2 * BOX1;
-constexpr uint32_t REGION = S1 * ST1;             // 160 KiB
-constexpr uint32_t OFF_V2 = 0;                    // pass 2: 2 stages x (V hi, V lo) boxes
-constexpr uint32_t OFF_STG = 4 * BOX2;            // pass 2: 4 staging boxes (-V W')
-constexpr uint32_t OFF_BH = 8 * BOX2;             // W' hi, K-major, 128 rows x 128 B
-constexpr uint32_t OFF_BL = OFF_BH + TCOLS * 128; // W' lo
-static_assert(OFF_BL + TCOLS * 128 <= REGION, "pass-2 buffers must fit the pass-1 region");
-constexpr uint32_t OFF_T = REGION;                // T, 32 x 33 floats
-constexpr int T_LD = KR + 1;
-constexpr uint32_t OFF_BAR = OFF_T + ((KR * T_LD * 4 + 127) / 128) * 128;
 // mbarriers
 constexpr int B_FULL1 = 0, B_SPLIT1 = B_FULL1 + S1, B_EMPTY1 = B_SPLIT1 + S1,
               B_D1FULL = B_EMPTY1 + S1, B_B2READY = B_D1FULL + 1, B_V2FULL = B_B2READY + 1,
               B_V2EMPTY = B_V2FULL + 2, B_ACCFULL = B_V2EMPTY + 2, B_ACCEMPTY = B_ACCFULL + 2,
               B_TILEDONE = B_ACCEMPTY + 2, B_FIN = B_TILEDONE + 1, NBAR = B_FIN + 1;
-constexpr uint32_t OFF_TMEMV = OFF_BAR + NBAR * 8;
-constexpr uint32_t OFF_ABORT = OFF_TMEMV + 4;
-constexpr uint32_t SMEM_USED = OFF_ABORT + 12;
-constexpr size_t SMEM_BYTES = SMEM_USED + 1024;   // slack for aligning the base
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-
-// TMEM columns: pass 1 accumulates into NP1 partial accumulators of 32
-// columns (chunk ch into partial ch % NP1), summed in FP32 afterwards: the
-// tensor core's accumulation inside an MMA is not rounded to nearest at every
-// add, so one accumulator over thousands of rows drifts ~5x further from FP64
-// than FFMA; eight shorter chains keep it at FFMA's level. D2 buffers at 256
-// and 384.
-constexpr int NP1 = 8;
 constexpr uint32_t TM_COLS = 512;
-constexpr uint32_t TM_D2 = 256;
-constexpr uint32_t IDESC1 = tc::idesc(TCOLS, KR, /*a_mn=*/true, /*b_mn=*/true);
+constexpr uint32_t TM_D2 = 256;   // two pass-2 accumulators of 128 columns at 256 and 384
+
+// Layout for a block of KR reflectors (32, or 64 for two-level blocking).
+//   Shared memory (bytes from a 1024-aligned base): a pass-1 stage holds the
+//   C chunk (hi after the split), the V hi and lo boxes (KR / 32 boxes each)
+//   and the C lo buffer. Pass 2 reuses the pass-1 region once every pass-1
+//   MMA of the tile is done: NV2 stages of V (hi and lo), 4 staging boxes for
+//   -V W', and W' hi / lo as the K-major B operand.
+//   TMEM: pass 1 accumulates into NP1 partial accumulators of KR columns
+//   (chunk ch into partial ch % NP1), summed in FP32 afterwards: the tensor
+//   core's accumulation inside an MMA is not rounded to nearest at every add,
+//   so one accumulator over thousands of rows drifts ~5x further from FP64
+//   than FFMA; short chains keep it at FFMA's level.
+template <int KR>
+struct Lay {
+  static constexpr int NA = KR / 32;                       // 32-wide atoms of V / of K
+  static constexpr uint32_t VB1 = NA * BOX1;
+  static constexpr uint32_t ST1 = CST + 2 * VB1 + CST;
+  static constexpr uint32_t S1_VH = CST, S1_VL = CST + VB1, S1_CL = CST + 2 * VB1;
+  static constexpr uint32_t REGION = S1 * ST1;
+  static constexpr int NV2 = KR == 32 ? 2 : 1;
+  static constexpr uint32_t V2ST = 2 * NA * BOX2;
+  static constexpr uint32_t OFF_STG = NV2 * V2ST;
+  static constexpr uint32_t B2B = NA * TCOLS * 128;
+  static constexpr uint32_t OFF_BH = OFF_STG + 4 * BOX2;
+  static constexpr uint32_t OFF_BL = OFF_BH + B2B;
+  static constexpr uint32_t OFF_T = REGION;
+  static constexpr int T_LD = KR + 1;
+  static constexpr uint32_t OFF_BAR = OFF_T + ((KR * T_LD * 4 + 127) / 128) * 128;
+  static constexpr uint32_t OFF_TMEMV = OFF_BAR + NBAR * 8;
+  static constexpr uint32_t OFF_ABORT = OFF_TMEMV + 4;
+  static constexpr size_t SMEM_BYTES = OFF_ABORT + 12 + 1024;  // slack for aligning the base
+  static constexpr int NP1 = 256 / KR;
+  static constexpr uint32_t IDESC1 = tc::idesc(TCOLS, KR, /*a_mn=*/true, /*b_mn=*/true);
+  static_assert(OFF_BL + B2B <= REGION, "pass-2 buffers must fit the pass-1 region");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
 constexpr uint32_t IDESC2 = tc::idesc(R2, TCOLS, /*a_mn=*/false, /*b_mn=*/false);
 
 // Shared-memory matrix descriptors (sm_100 version field 1) for the two
@@ -158,7 +162,7 @@ __device__ __forceinline__ uint64_t sdesc_mn32(uint32_t saddr, uint32_t lbo) {
 }
 
 // 32 consecutive TMEM columns of this warp's lane quarter (no wait).
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float (&v)[32]) {
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float* v) {
   uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -199,20 +203,24 @@ __device__ __forceinline__ bool workers_sync_or(bool v) {
   return r != 0;
 }
 
+// vw_hi / vw_lo: plane coordinates of the V hi / lo boxes in the V map.
+template <int KR>
 __global__ void __launch_bounds__(NTH, 1)
 k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUtensorMap mC2,
             const __grid_constant__ CUtensorMap mV1, const __grid_constant__ CUtensorMap mV2,
             const float* __restrict__ T, int64_t sTb, int m0, int ntiles, int ntc, int j0,
-            int col0, int col_end, int n, int vbuf, int* __restrict__ err, long long wait_limit,
-            int skip_mma) {
+            int col0, int col_end, int n, int vw_hi, int vw_lo, int* __restrict__ err,
+            long long wait_limit, int skip_mma) {
+  using L = Lay<KR>;
+  constexpr int NA = L::NA, NV2 = L::NV2, NP1 = L::NP1;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = tma::smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* sm = smem_raw + (base - raw);
-  float* Ts = reinterpret_cast<float*>(sm + OFF_T);
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_TMEMV);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + OFF_ABORT);
-  const uint32_t bar0 = base + OFF_BAR;
+  float* Ts = reinterpret_cast<float*>(sm + L::OFF_T);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::OFF_TMEMV);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + L::OFF_ABORT);
+  const uint32_t bar0 = base + L::OFF_BAR;
   auto BAR = [&](int i) { return bar0 + 8u * (uint32_t)i; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -239,7 +247,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     base + OFF_TMEMV),
+                     base + L::OFF_TMEMV),
                  "r"(TM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -258,7 +266,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         const int m = m0 + t / ntc;
         const int tc0 = col0 + (t % ntc) * TCOLS;
         const int nbox = min(4, (col_end - tc0 + 31) / 32);
-        const uint32_t tx1 = (uint32_t)nbox * BOX1 + 2 * BOX1;
+        const uint32_t tx1 = (uint32_t)nbox * BOX1 + 2 * L::VB1;
         // the previous tile's pass 2 has released the shared buffers
         if (it > 0 && *s_abort == 0)
           tma::mbar_wait_or_abort(BAR(B_TILEDONE), (uint32_t)((it - 1) & 1), wait_limit, s_abort);
@@ -269,30 +277,36 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
               !tma::mbar_wait_or_abort(BAR(B_EMPTY1 + s), (uint32_t)((u - 1) & 1), wait_limit,
                                        s_abort))
             continue;
-          const uint32_t st = base + (uint32_t)s * ST1, fb = BAR(B_FULL1 + s);
+          const uint32_t st = base + (uint32_t)s * L::ST1, fb = BAR(B_FULL1 + s);
           const int y = j0 + ch * R1;
           tma::mbar_expect_tx(fb, tx1);
           for (int bq = 0; bq < nbox; ++bq)
             tma::load_3d(st + bq * BOX1, &mC1, fb, tc0 + 32 * bq, y, m);
-          tma::load_4d(st + OFF_S1_VH, &mV1, fb, 0, y, m, 2 * vbuf);
-          tma::load_4d(st + OFF_S1_VL, &mV1, fb, 0, y, m, 2 * vbuf + 1);
+#pragma unroll
+          for (int a = 0; a < NA; ++a) {
+            tma::load_4d(st + L::S1_VH + a * BOX1, &mV1, fb, 32 * a, y, m, vw_hi);
+            tma::load_4d(st + L::S1_VL + a * BOX1, &mV1, fb, 32 * a, y, m, vw_lo);
+          }
           last1[s] = u;
         }
         // pass 2 reuses the pass-1 region: wait until every pass-1 MMA is done
         if (*s_abort == 0)
           tma::mbar_wait_or_abort(BAR(B_D1FULL), (uint32_t)(it & 1), wait_limit, s_abort);
         for (int p = 0; p < nch2; ++p, ++g2) {
-          const int v = g2 & 1, u = g2 >> 1;
+          const int v = g2 % NV2, u = g2 / NV2;
           if (*s_abort != 0) continue;
           if (u > 0 &&
               !tma::mbar_wait_or_abort(BAR(B_V2EMPTY + v), (uint32_t)((u - 1) & 1), wait_limit,
                                        s_abort))
             continue;
-          const uint32_t st = base + OFF_V2 + (uint32_t)v * 2 * BOX2, fb = BAR(B_V2FULL + v);
+          const uint32_t st = base + (uint32_t)v * L::V2ST, fb = BAR(B_V2FULL + v);
           const int y = j0 + p * R2;
-          tma::mbar_expect_tx(fb, 2 * BOX2);
-          tma::load_4d(st, &mV2, fb, 0, y, m, 2 * vbuf);
-          tma::load_4d(st + BOX2, &mV2, fb, 0, y, m, 2 * vbuf + 1);
+          tma::mbar_expect_tx(fb, L::V2ST);
+#pragma unroll
+          for (int a = 0; a < NA; ++a) {
+            tma::load_4d(st + a * BOX2, &mV2, fb, 32 * a, y, m, vw_hi);
+            tma::load_4d(st + (NA + a) * BOX2, &mV2, fb, 32 * a, y, m, vw_lo);
+          }
           last2[v] = u;
         }
       }
@@ -301,7 +315,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         for (int s = 0; s < S1; ++s)
           if (last1[s] >= 0)
             tma::mbar_wait_bounded(BAR(B_FULL1 + s), (uint32_t)(last1[s] & 1), wait_limit);
-        for (int v = 0; v < 2; ++v)
+        for (int v = 0; v < NV2; ++v)
           if (last2[v] >= 0)
             tma::mbar_wait_bounded(BAR(B_V2FULL + v), (uint32_t)(last2[v] & 1), wait_limit);
       }
@@ -317,17 +331,17 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
           if (!tma::mbar_wait_or_abort(BAR(B_SPLIT1 + s), (uint32_t)(u & 1), wait_limit, s_abort))
             continue;
           tc::fence_after();
-          const uint32_t st = base + (uint32_t)s * ST1;
-          const uint32_t d1 = tmem + 32u * (uint32_t)(ch % NP1);
+          const uint32_t st = base + (uint32_t)s * L::ST1;
+          const uint32_t d1 = tmem + (uint32_t)KR * (uint32_t)(ch % NP1);
 #pragma unroll
           for (int ks = 0; ks < R1 / 8; ++ks) {
             const uint64_t ah = sdesc_mn32(st + ks * 1024, BOX1);
-            const uint64_t al = sdesc_mn32(st + OFF_S1_CL + ks * 1024, BOX1);
-            const uint64_t bh = sdesc_mn32(st + OFF_S1_VH + ks * 1024, BOX1);
-            const uint64_t bl = sdesc_mn32(st + OFF_S1_VL + ks * 1024, BOX1);
-            tc::mma_tf32(d1, ah, bh, IDESC1, (ch >= NP1 || ks != 0) ? 1u : 0u);
-            tc::mma_tf32(d1, ah, bl, IDESC1, 1u);
-            tc::mma_tf32(d1, al, bh, IDESC1, 1u);
+            const uint64_t al = sdesc_mn32(st + L::S1_CL + ks * 1024, BOX1);
+            const uint64_t bh = sdesc_mn32(st + L::S1_VH + ks * 1024, BOX1);
+            const uint64_t bl = sdesc_mn32(st + L::S1_VL + ks * 1024, BOX1);
+            tc::mma_tf32(d1, ah, bh, L::IDESC1, (ch >= NP1 || ks != 0) ? 1u : 0u);
+            tc::mma_tf32(d1, ah, bl, L::IDESC1, 1u);
+            tc::mma_tf32(d1, al, bh, L::IDESC1, 1u);
           }
           tc::mma_commit(BAR(B_EMPTY1 + s));
         }
@@ -336,28 +350,30 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         if (*s_abort == 0)
           tma::mbar_wait_or_abort(BAR(B_B2READY), (uint32_t)(it & 1), wait_limit, s_abort);
         for (int p = 0; p < nch2; ++p, ++g2) {
-          const int v = g2 & 1, u = g2 >> 1;
+          const int v = g2 % NV2, u = g2 / NV2;
+          const int ab = g2 & 1, ua = g2 >> 1;  // TMEM accumulator
           if (*s_abort != 0) continue;
           if (!tma::mbar_wait_or_abort(BAR(B_V2FULL + v), (uint32_t)(u & 1), wait_limit, s_abort))
             continue;
-          if (u > 0 && !tma::mbar_wait_or_abort(BAR(B_ACCEMPTY + v), (uint32_t)((u - 1) & 1),
-                                                wait_limit, s_abort))
+          if (ua > 0 && !tma::mbar_wait_or_abort(BAR(B_ACCEMPTY + ab), (uint32_t)((ua - 1) & 1),
+                                                 wait_limit, s_abort))
             continue;
           tc::fence_after();
-          const uint32_t va = base + OFF_V2 + (uint32_t)v * 2 * BOX2, vl = va + BOX2;
-          const uint32_t d = tmem + TM_D2 + 128u * (uint32_t)v;
+          const uint32_t va = base + (uint32_t)v * L::V2ST;
+          const uint32_t d = tmem + TM_D2 + 128u * (uint32_t)ab;
 #pragma unroll
           for (int ks = 0; ks < KR / 8; ++ks) {
-            const uint64_t ah = sdesc_kmajor(va + 32 * ks);
-            const uint64_t al = sdesc_kmajor(vl + 32 * ks);
-            const uint64_t bh = sdesc_kmajor(base + OFF_BH + 32 * ks);
-            const uint64_t bl = sdesc_kmajor(base + OFF_BL + 32 * ks);
+            const uint32_t ka = (uint32_t)(ks >> 2), ko = 32u * (uint32_t)(ks & 3);
+            const uint64_t ah = sdesc_kmajor(va + ka * BOX2 + ko);
+            const uint64_t al = sdesc_kmajor(va + (NA + ka) * BOX2 + ko);
+            const uint64_t bh = sdesc_kmajor(base + L::OFF_BH + ka * TCOLS * 128 + ko);
+            const uint64_t bl = sdesc_kmajor(base + L::OFF_BL + ka * TCOLS * 128 + ko);
             tc::mma_tf32(d, ah, bh, IDESC2, ks != 0 ? 1u : 0u);
             tc::mma_tf32(d, ah, bl, IDESC2, 1u);
             tc::mma_tf32(d, al, bh, IDESC2, 1u);
           }
           tc::mma_commit(BAR(B_V2EMPTY + v));
-          tc::mma_commit(BAR(B_ACCFULL + v));
+          tc::mma_commit(BAR(B_ACCFULL + ab));
         }
       }
       if (*s_abort != 0) {  // every MMA issued so far has completed before TMEM is freed
@@ -378,7 +394,8 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
       const int tc0 = col0 + (t % ntc) * TCOLS;
       const int nbox = min(4, (col_end - tc0 + 31) / 32);
       const float* Tm = T + (int64_t)ml * sTb;
-      for (int e = wt; e < KR * KR; e += 32 * NWORK) Ts[(e >> 5) * T_LD + (e & 31)] = __ldg(Tm + e);
+      for (int e = wt; e < KR * KR; e += 32 * NWORK)
+        Ts[(e / KR) * L::T_LD + (e % KR)] = __ldg(Tm + e);
       workers_sync_or(false);  // T in shared memory for the W' step below
 
       // ---- pass 1: split each chunk's C boxes into hi (in place) and lo ----
@@ -390,8 +407,8 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         // that last read this stage's lo buffer are done)
         if (!tma::mbar_wait_or_abort(BAR(B_FULL1 + s), (uint32_t)(u & 1), wait_limit, s_abort))
           continue;
-        float4* c4 = reinterpret_cast<float4*>(sm + (uint32_t)s * ST1);
-        float4* l4 = reinterpret_cast<float4*>(sm + (uint32_t)s * ST1 + OFF_S1_CL);
+        float4* c4 = reinterpret_cast<float4*>(sm + (uint32_t)s * L::ST1);
+        float4* l4 = reinterpret_cast<float4*>(sm + (uint32_t)s * L::ST1 + L::S1_CL);
         for (int e = wt; e < units; e += 32 * NWORK) {
           float4 hi, lo;
           tc::split4(c4[e], hi, lo);
@@ -403,49 +420,56 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         if (lane == 0) tma::mbar_arrive(BAR(B_SPLIT1 + s));
       }
 
-      // ---- W' = T^T W ----
+      // ---- W' = T^T W (this thread: tile column `row`, reflectors of half h) ----
       bool skip = *s_abort != 0 ||
                   !tma::mbar_wait_or_abort(BAR(B_D1FULL), (uint32_t)(it & 1), wait_limit, s_abort);
       skip = __any_sync(tc::kFullMask, skip);  // tcgen05.ld below is warp-collective
       if (!skip) {
         tc::fence_after();
-        float w[32], wp[32];
+        float w[KR], wp[32];
         const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
-        tmem_ld32_nowait(tl, w);
+#pragma unroll
+        for (int a = 0; a < NA; ++a) tmem_ld32_nowait(tl + 32u * a, w + 32 * a);
         tmem_wait_ld();
         const int np = nch1 < NP1 ? nch1 : NP1;
         for (int pp = 1; pp < np; ++pp) {
-          tmem_ld32_nowait(tl + 32u * (uint32_t)pp, wp);
-          tmem_wait_ld();
 #pragma unroll
-          for (int b = 0; b < 32; ++b) w[b] += wp[b];
+          for (int a = 0; a < NA; ++a) {
+            tmem_ld32_nowait(tl + (uint32_t)(KR * pp + 32 * a), wp);
+            tmem_wait_ld();
+#pragma unroll
+            for (int b = 0; b < 32; ++b) w[32 * a + b] += wp[b];
+          }
         }
-        float o[16];
-        if (h == 0) {  // W'[a] for a < 16: T[b][a] = 0 for b > a
+        constexpr int HALF = KR / 2;
+        float o[HALF];
+        if (h == 0) {  // W'[a] for a < KR/2: T[b][a] = 0 for b > a
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < HALF; ++i) {
             float acc = 0.f;
 #pragma unroll
-            for (int b = 0; b < 16; ++b) acc = fmaf(Ts[b * T_LD + i], w[b], acc);
+            for (int b = 0; b < HALF; ++b) acc = fmaf(Ts[b * L::T_LD + i], w[b], acc);
             o[i] = acc;
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < HALF; ++i) {
             float acc = 0.f;
 #pragma unroll
-            for (int b = 0; b < 32; ++b) acc = fmaf(Ts[b * T_LD + 16 + i], w[b], acc);
+            for (int b = 0; b < KR; ++b) acc = fmaf(Ts[b * L::T_LD + HALF + i], w[b], acc);
             o[i] = acc;
           }
         }
-        // B operand of pass 2, K-major: row = tile column, 128 bytes = 32 reflectors
+        // B operand of pass 2, K-major: row = tile column, K atoms of 32
+        // reflectors (128 bytes) each
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < HALF / 4; ++j) {
+          const int a0 = h * HALF + 4 * j;
           float4 hi, lo;
           tc::split4(make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]), hi, lo);
-          const uint32_t off = sw128(row, 4 * h + j);
-          *reinterpret_cast<float4*>(sm + OFF_BH + off) = hi;
-          *reinterpret_cast<float4*>(sm + OFF_BL + off) = lo;
+          const uint32_t off = (uint32_t)(a0 >> 5) * TCOLS * 128 + sw128(row, (a0 & 31) >> 2);
+          *reinterpret_cast<float4*>(sm + L::OFF_BH + off) = hi;
+          *reinterpret_cast<float4*>(sm + L::OFF_BL + off) = lo;
         }
         tma::fence_proxy_async();
         tc::fence_before();
@@ -455,37 +479,38 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
 
       // ---- pass 2 epilogues: C += -(V W') by TMA reduce-add ----
       for (int p = 0; p < nch2; ++p, ++g2) {
-        const int v = g2 & 1, u = g2 >> 1;
+        const int ab = g2 & 1, ua = g2 >> 1;
         bool sk = *s_abort != 0 ||
-                  !tma::mbar_wait_or_abort(BAR(B_ACCFULL + v), (uint32_t)(u & 1), wait_limit,
+                  !tma::mbar_wait_or_abort(BAR(B_ACCFULL + ab), (uint32_t)(ua & 1), wait_limit,
                                            s_abort);
         sk = __any_sync(tc::kFullMask, sk);
         float d0[32], d1[32];
         if (!sk) {
           tc::fence_after();
           const uint32_t ta =
-              tmem + ((uint32_t)(32 * q) << 16) + TM_D2 + 128u * (uint32_t)v + 64u * (uint32_t)h;
+              tmem + ((uint32_t)(32 * q) << 16) + TM_D2 + 128u * (uint32_t)ab + 64u * (uint32_t)h;
           tmem_ld32_nowait(ta, d0);
           tmem_ld32_nowait(ta + 32, d1);
           tmem_wait_ld();
           tc::fence_before();
           __syncwarp();
-          if (lane == 0) tma::mbar_arrive(BAR(B_ACCEMPTY + v));
+          if (lane == 0) tma::mbar_arrive(BAR(B_ACCEMPTY + ab));
         }
         if (issuer) tma::bulk_wait_read_all();  // the previous reduce has read the staging tile
         if (workers_sync_or(sk || *s_abort != 0)) continue;
 #pragma unroll
         for (int uu = 0; uu < 8; ++uu) {
-          *reinterpret_cast<float4*>(sm + OFF_STG + (2 * h) * BOX2 + sw128(row, uu)) =
+          *reinterpret_cast<float4*>(sm + L::OFF_STG + (2 * h) * BOX2 + sw128(row, uu)) =
               make_float4(-d0[4 * uu], -d0[4 * uu + 1], -d0[4 * uu + 2], -d0[4 * uu + 3]);
-          *reinterpret_cast<float4*>(sm + OFF_STG + (2 * h + 1) * BOX2 + sw128(row, uu)) =
+          *reinterpret_cast<float4*>(sm + L::OFF_STG + (2 * h + 1) * BOX2 + sw128(row, uu)) =
               make_float4(-d1[4 * uu], -d1[4 * uu + 1], -d1[4 * uu + 2], -d1[4 * uu + 3]);
         }
         tma::fence_proxy_async();
         workers_sync_or(false);
         if (issuer) {
           for (int bq = 0; bq < nbox; ++bq)
-            tma::reduce_add_3d(&mC2, base + OFF_STG + bq * BOX2, tc0 + 32 * bq, j0 + R2 * p, m);
+            tma::reduce_add_3d(&mC2, base + L::OFF_STG + bq * BOX2, tc0 + 32 * bq, j0 + R2 * p,
+                               m);
           tma::bulk_commit();
         }
       }
@@ -528,19 +553,22 @@ int launch_wait_probe(long long limit, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
 }
 
-bool larfb_tma_supported(int n) { return n % 4 == 0 && n > KR && tma::encoder() != nullptr; }
+bool larfb_tma_supported(int n) { return n % 4 == 0 && n > 32 && tma::encoder() != nullptr; }
 
-int make_larfb_maps(LarfbMaps* maps, const float* H, const float* Vs, int64_t batch, int n) {
+int make_larfb_maps(LarfbMaps* maps, const float* H, const float* Vs, int64_t batch, int n,
+                    int kr) {
   if (maps == nullptr || H == nullptr || Vs == nullptr || batch <= 0 || n % 4 != 0 ||
-      batch > 0x7fffffffLL)
+      batch > 0x7fffffffLL || (kr != 32 && kr != 64))
     return QRB_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(H) & 15) != 0 || (reinterpret_cast<uintptr_t>(Vs) & 15) != 0)
     return QRB_ERR_UNSUPPORTED;
-  const uint64_t nn = (uint64_t)n;
+  const uint64_t nn = (uint64_t)n, k = (uint64_t)kr;
   const uint64_t cdims[3] = {nn, nn, (uint64_t)batch};
   const uint64_t cstr[2] = {nn * 4, nn * nn * 4};
-  const uint64_t vdims[4] = {(uint64_t)KR, nn, (uint64_t)batch, 4};
-  const uint64_t vstr[3] = {KR * 4, nn * KR * 4, (uint64_t)batch * nn * KR * 4};
+  // the split reflectors: 4 planes of [batch][n][32] (two V buffers x hi / lo)
+  // for 32-reflector blocks, 2 planes of [batch][n][64] (hi / lo) for 64
+  const uint64_t vdims[4] = {k, nn, (uint64_t)batch, kr == 32 ? 4u : 2u};
+  const uint64_t vstr[3] = {k * 4, nn * k * 4, (uint64_t)batch * nn * k * 4};
   // pass-1 boxes are MN-major operands (32-byte-atom swizzle); pass-2 V boxes
   // are K-major operands and the C boxes take the staged reduce-add (plain
   // 128-byte swizzle)
@@ -548,24 +576,23 @@ int make_larfb_maps(LarfbMaps* maps, const float* H, const float* Vs, int64_t ba
                   tma::encode_f32_sw128(&maps->c2, H, 3, cdims, cstr, 32, R2, false) &&
                   tma::encode_f32_sw128(&maps->v1, Vs, 4, vdims, vstr, 32, R1, true) &&
                   tma::encode_f32_sw128(&maps->v2, Vs, 4, vdims, vstr, 32, R2, false);
+  maps->kr = kr;
   return ok ? QRB_OK : QRB_ERR_UNSUPPORTED;
 }
 
-int launch_larfb_tma(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
-                     int64_t count, int j0, int col0, int col_end, int n, int vbuf,
-                     cudaStream_t stream) {
-  if (count <= 0 || col_end <= col0) return QRB_OK;
-  if (j0 < 0 || j0 + KR > n || col0 % 4 != 0 || m0 < 0 || m0 + count > 0x7fffffffLL)
-    return QRB_ERR_UNSUPPORTED;
-  if (col_end != n && (col_end - col0) % 32 != 0) return QRB_ERR_UNSUPPORTED;
+namespace {
+template <int KR>
+int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0, int64_t count,
+                 int j0, int col0, int col_end, int n, int vw_hi, int vw_lo,
+                 cudaStream_t stream) {
   static bool attr_set[64] = {};
   static int* err_ptr[64] = {};
   static int sms[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(k_larfb_tma, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)SMEM_BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(k_larfb_tma<KR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)Lay<KR>::SMEM_BYTES) != cudaSuccess)
       return QRB_ERR_LAUNCH;
     if (device_error_ptr(&err_ptr[dev]) != QRB_OK) return QRB_ERR_DEVICE;
     if (cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
@@ -577,12 +604,28 @@ int launch_larfb_tma(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t
   const int64_t tiles = ntc * count;
   if (tiles > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
   const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);  // persistent: <= one CTA per SM
-  k_larfb_tma<<<grid, NTH, SMEM_BYTES, stream>>>(maps.c1, maps.c2, maps.v1, maps.v2, T, sTb,
-                                                 (int)m0, (int)tiles, (int)ntc, j0, col0,
-                                                 col_end, n, vbuf, err_ptr[dev],
-                                                 device_wait_limit(), test_skip_mma() ? 1 : 0);
+  k_larfb_tma<KR><<<grid, NTH, Lay<KR>::SMEM_BYTES, stream>>>(
+      maps.c1, maps.c2, maps.v1, maps.v2, T, sTb, (int)m0, (int)tiles, (int)ntc, j0, col0,
+      col_end, n, vw_hi, vw_lo, err_ptr[dev], device_wait_limit(), test_skip_mma() ? 1 : 0);
   note_launches(1);
   return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
+}
+}  // namespace
+
+int launch_larfb_tma(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
+                     int64_t count, int j0, int col0, int col_end, int n, int vbuf,
+                     cudaStream_t stream) {
+  if (count <= 0 || col_end <= col0) return QRB_OK;
+  const int kr = maps.kr;
+  if (j0 < 0 || j0 + kr > n || col0 % 4 != 0 || m0 < 0 || m0 + count > 0x7fffffffLL)
+    return QRB_ERR_UNSUPPORTED;
+  if (col_end != n && (col_end - col0) % 32 != 0) return QRB_ERR_UNSUPPORTED;
+  if (kr == 32)
+    return launch_tma_t<32>(maps, T, sTb, m0, count, j0, col0, col_end, n, 2 * vbuf, 2 * vbuf + 1,
+                            stream);
+  if (kr == 64 && vbuf == 0)
+    return launch_tma_t<64>(maps, T, sTb, m0, count, j0, col0, col_end, n, 0, 1, stream);
+  return QRB_ERR_UNSUPPORTED;
 }
 
 }  // namespace qrb

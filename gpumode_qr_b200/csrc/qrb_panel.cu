@@ -77,8 +77,8 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
         float* __restrict__ dst, int64_t sb_dst, int64_t ld_dst,
         float* __restrict__ tau_out, int64_t tau_sb, float* __restrict__ T_out,
         int64_t T_sb, int t_ld, float* __restrict__ V_out, float* __restrict__ Vsplit,
-        int64_t vs_mat, int64_t vs_plane, int vs_row0, int r, int w, int cs, int vec_src,
-        int vec_dst) {
+        int64_t vs_mat, int64_t vs_plane, int vs_row0, int vs_ld, int vs_zero, int r, int w,
+        int cs, int vec_src, int vec_dst) {
   __shared__ float red[2][kMaxThreads / 32][W];  // [parity][warp][slot]
   __shared__ float xch[2][2][W];                 // [parity][0 = CTA slot sums, 1 = row j]
   __shared__ __align__(16) float fbuf[kMaxThreads / 32][W];  // per-warp tau_j * d_k
@@ -233,7 +233,7 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
         if (c < w) vrow[c] = (i > c) ? o[c] : (i == c ? 1.f : 0.f);
     }
     if (Vsplit != nullptr) {  // the unit-lower reflectors, TF32-split for the tensor cores
-      float* vh = Vsplit + m * vs_mat + (int64_t)(vs_row0 + i) * W;
+      float* vh = Vsplit + m * vs_mat + (int64_t)(vs_row0 + i) * vs_ld;
       float* vl = vh + vs_plane;
 #pragma unroll
       for (int c4 = 0; c4 < W / 4; ++c4) {
@@ -247,6 +247,13 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
         tc::split4(make_float4(v[0], v[1], v[2], v[3]), hi, lo);
         reinterpret_cast<float4*>(vh)[c4] = hi;
         reinterpret_cast<float4*>(vl)[c4] = lo;
+      }
+      if (vs_zero && i < W) {  // the next panel's reflectors are zero in these rows
+#pragma unroll
+        for (int c4 = 0; c4 < W / 4; ++c4) {
+          reinterpret_cast<float4*>(vh + W)[c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+          reinterpret_cast<float4*>(vl + W)[c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
     }
   }
@@ -284,8 +291,8 @@ int launch_panel_rpt(const float* src, int64_t sb_src, int64_t ld_src,
                      float* dst, int64_t sb_dst, int64_t ld_dst, float* tau_out,
                      int64_t tau_sb, float* T_out, int64_t T_sb, int t_ld,
                      float* V_out, float* Vsplit, int64_t vs_mat, int64_t vs_plane,
-                     int vs_row0, int64_t batch, int r, int w, int cs, int nt,
-                     cudaStream_t stream) {
+                     int vs_row0, int vs_ld, int vs_zero, int64_t batch, int r, int w, int cs,
+                     int nt, cudaStream_t stream) {
   const bool vec_src = w == W && ld_src % 4 == 0 && sb_src % 4 == 0 &&
                        (reinterpret_cast<uintptr_t>(src) & 15) == 0;
   const bool vec_dst = w == W && ld_dst % 4 == 0 && sb_dst % 4 == 0 &&
@@ -304,8 +311,8 @@ int launch_panel_rpt(const float* src, int64_t sb_src, int64_t ld_src,
   cfg.numAttrs = cs > 1 ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(
       &cfg, k_panel<RPT>, src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
-      tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, r, w, cs,
-      (int)vec_src, (int)vec_dst);
+      tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, vs_ld, vs_zero, r, w,
+      cs, (int)vec_src, (int)vec_dst);
   note_launches(1);
   return e == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
 }
@@ -348,9 +355,10 @@ int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
                  int64_t sb_dst, int64_t ld_dst, float* tau_out, int64_t tau_sb,
                  float* T_out, int64_t T_sb, int t_ld, float* V_out,
                  int64_t batch, int r, int w, cudaStream_t stream, float* Vsplit,
-                 int64_t vs_mat, int64_t vs_plane, int vs_row0) {
+                 int64_t vs_mat, int64_t vs_plane, int vs_row0, int vs_ld, bool vs_zero) {
   if (r < 1 || w < 1 || w > W) return QRB_ERR_UNSUPPORTED;
-  if (Vsplit != nullptr && (w != W || (reinterpret_cast<uintptr_t>(Vsplit) & 15) != 0))
+  if (Vsplit != nullptr && (w != W || (reinterpret_cast<uintptr_t>(Vsplit) & 15) != 0 ||
+                            vs_ld % 4 != 0 || vs_ld < (vs_zero ? 2 * W : W)))
     return QRB_ERR_UNSUPPORTED;
   int rpt, cs, nt;
   panel_shape(r, &rpt, &cs, &nt);
@@ -358,14 +366,14 @@ int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
   if (batch * cs > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
   if (rpt == 1)
     return launch_panel_rpt<1>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
-                               tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, batch, r, w, cs,
+                               tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, vs_ld, (int)vs_zero, batch, r, w, cs,
                                nt, stream);
   if (rpt == 2)
     return launch_panel_rpt<2>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
-                               tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, batch, r, w, cs,
+                               tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, vs_ld, (int)vs_zero, batch, r, w, cs,
                                nt, stream);
   return launch_panel_rpt<4>(src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
-                             tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, batch, r, w, cs,
+                             tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, vs_ld, (int)vs_zero, batch, r, w, cs,
                              nt, stream);
 }
 

@@ -213,3 +213,25 @@ def test_tma_route_nan_input_propagates():
     assert not torch.isfinite(H[1]).all()
     assert np.isfinite(tau[0].cpu().numpy()).all()
     assert _lib.get_config("device_error") == 0
+
+
+@pytest.mark.parametrize("b,n,groups", [(3, 160, 1), (4, 300, 2), (3, 512, 1), (8, 640, 4),
+                                        (2, 1028, 1), (2, 2048, 2)])
+def test_two_level_tensor_core_route(b, n, groups):
+    # two 32-column panels per 64-reflector block (T 64 x 64 from the panels'
+    # factors and their cross block), the 64-reflector update on the tensor
+    # cores: FP64 gates, and within 1e-4 of FP64 LAPACK like the one-level route
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(17 * n + b))
+    old = _hooks(two_level=1, groups=groups)
+    try:
+        route = api.route(b, n)
+        H, tau = api.geqrf(A.to(DEV))
+        torch.cuda.synchronize()
+    finally:
+        _restore(old)
+    assert "tcgen05_tma" in route and "two_level" in route, route
+    assert checker.check(A, H.cpu(), tau.cpu()).passed
+    H64, t64 = torch.geqrf(A.double())
+    par = checker.parity(H.cpu(), tau.cpu(), H64.float(), t64.float())
+    assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 5e-4, par
+    assert _lib.get_config("device_error") == 0
