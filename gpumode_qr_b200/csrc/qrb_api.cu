@@ -22,11 +22,14 @@ std::atomic<int64_t> g_host_ramp{0};
 std::atomic<int64_t> g_fused_cpl{0};
 std::atomic<int64_t> g_mid_fused{1};
 std::atomic<int64_t> g_lookahead{2};  // 0 off, 1 on, 2 from kLookaheadMinN
-std::atomic<int64_t> g_two_level{0};  // 0 off, 1 on
+std::atomic<int64_t> g_two_level{2};  // 0 off, 1 on, 2 automatic
 std::atomic<int64_t> g_panel_rpt{0};
 std::atomic<int64_t> g_gram_tile{0};
 std::atomic<int64_t> g_wait_limit{2000000000LL};  // clock cycles, about 1 s
 std::atomic<int64_t> g_skip_mma{0};
+std::atomic<int64_t> g_tma_ctas{0};        // 0 = one per SM
+std::atomic<int64_t> g_narrow{1};          // narrow cluster kernel for the next panel's columns
+std::atomic<int64_t> g_panel_priority{1};  // look-ahead stream at the highest priority
 
 // Host-side fault injection: consume one pending injected failure.
 bool take_injected_failure() {
@@ -91,6 +94,29 @@ struct TmaRoute {
   float* vsplit64(int n) const { return Vs + m0 * n * 2 * qrb::kPanelW; }
   int64_t plane64(int n) const { return batch_total * n * 2 * qrb::kPanelW; }
 };
+
+// The look-ahead's update on the tensor-core route: columns [col0, n) of rows
+// [j0, n) with the 32 reflectors of the panel at (j0, j0) and its factor T
+// (row stride t_ld). cols = 32: only the first (at most) 32 columns, which the
+// next panel needs first, by the narrow cluster kernel (the TMA-fed kernel
+// where the narrow one does not apply or is switched off); cols < 0: the
+// columns after them, by the TMA-fed kernel.
+int tma_update(const TmaRoute& tr, float* H, const float* T, int64_t sTb, int t_ld,
+               int64_t batch, int n, int j0, int col0, int vbuf, int cols, cudaStream_t s) {
+  const int W = qrb::kPanelW;
+  const int64_t nn = (int64_t)n * n;
+  const int c = n - col0, r = n - j0;
+  const int ca = c < W ? c : W;
+  const float* V = H + (int64_t)j0 * n + j0;
+  float* C = H + (int64_t)j0 * n + col0;
+  if (cols == W) {
+    if (g_narrow.load() != 0 && qrb::larfb_narrow_supported(V, nn, n, C, nn, n, W, ca))
+      return qrb::launch_larfb_narrow(V, nn, n, T, sTb, t_ld, C, nn, n, batch, r, ca, s);
+    return qrb::launch_larfb_tma(*tr.maps, T, sTb, tr.m0, batch, j0, col0, col0 + ca, n, vbuf, s);
+  }
+  if (c <= ca) return QRB_OK;
+  return qrb::launch_larfb_tma(*tr.maps, T, sTb, tr.m0, batch, j0, col0 + ca, n, n, vbuf, s);
+}
 
 // The blocked factorization of one contiguous group of matrices on `s`:
 // per 32-column panel one panel kernel (reflectors, tau, T) and one trailing
@@ -169,8 +195,7 @@ int blocked_qr_lookahead(const float* A, int64_t strideA_b, int64_t strideA_row,
     // part a on sp, after part b of the previous step
     if (cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
     rc = tr != nullptr
-             ? qrb::launch_larfb_tma(*tr->maps, T, (int64_t)W * W, tr->m0, batch, j0, j0 + w,
-                                     j0 + w + ca, n, buf, sp)
+             ? tma_update(*tr, H, T, (int64_t)W * W, W, batch, n, j0, j0 + w, buf, W, sp)
              : larfb_any(Hp, nn, n, T, (int64_t)W * W, W, ca_src, sbt, ld, Hp + w, nn, n, batch,
                          r, w, ca, sp);
     if (rc != QRB_OK) break;
@@ -178,8 +203,7 @@ int blocked_qr_lookahead(const float* A, int64_t strideA_b, int64_t strideA_row,
     if (cudaStreamWaitEvent(sb, evP, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
     if (cbw > 0) {
       rc = tr != nullptr
-               ? qrb::launch_larfb_tma(*tr->maps, T, (int64_t)W * W, tr->m0, batch, j0,
-                                       j0 + w + ca, n, n, buf, sb)
+               ? tma_update(*tr, H, T, (int64_t)W * W, W, batch, n, j0, j0 + w, buf, -1, sb)
                : larfb_any(Hp, nn, n, T, (int64_t)W * W, W, ca_src + ca, sbt, ld, Hp + w + ca,
                            nn, n, batch, r, w, cbw, sb);
       if (rc != QRB_OK) break;
@@ -228,7 +252,11 @@ int blocked_qr2(const float* A, int64_t strideA_b, int64_t strideA_row, float* H
                                r, w1, s, vs, (int64_t)n * K2, vpl, j0, K2, big);
     if (rc != QRB_OK || r <= W) return rc;
     const int w2 = r - W < W ? r - W : W;
-    rc = larfb_any(Hp, nn, n, T1, tsb, K2, Sp + W, sb, ld, Hp + W, nn, n, batch, r, W, w2, s);
+    rc = tr != nullptr && g_narrow.load() != 0 &&
+                 qrb::larfb_narrow_supported(Hp, nn, n, Hp + W, nn, n, W, w2)
+             ? qrb::launch_larfb_narrow(Hp, nn, n, T1, tsb, K2, Hp + W, nn, n, batch, r, w2, s)
+             : larfb_any(Hp, nn, n, T1, tsb, K2, Sp + W, sb, ld, Hp + W, nn, n, batch, r, W, w2,
+                         s);
     if (rc != QRB_OK) return rc;
     float* Hq = Hp + (int64_t)W * n + W;
     rc = qrb::launch_panel(Hq, nn, n, Hq, nn, n, tau + j0 + W, n, T2, tsb, K2, nullptr, batch,
@@ -267,6 +295,7 @@ struct SideStreams {
   cudaEvent_t join[kMaxGroups] = {};
   // look-ahead: per group a panel stream and its events
   cudaStream_t sp[kMaxGroups] = {};
+  cudaStream_t spl[kMaxGroups] = {};  // the same at the default priority (test hook)
   cudaEvent_t evP[kMaxGroups] = {}, evB[kMaxGroups] = {}, joinP[kMaxGroups] = {};
   bool ok = false;
 };
@@ -281,10 +310,17 @@ SideStreams* side_streams() {
   std::call_once(g_side_once[dev], [ss] {
     bool ok = cudaEventCreateWithFlags(&ss->fork, cudaEventDisableTiming) == cudaSuccess;
     const unsigned ef = cudaEventDisableTiming;
+    // The look-ahead streams (panel and next-panel update: the critical path)
+    // get the highest priority, so that their CTAs are placed first whenever
+    // trailing-update CTAs leave SMs free.
+    int least = 0, greatest = 0;
+    ok = ok && cudaDeviceGetStreamPriorityRange(&least, &greatest) == cudaSuccess;
     for (int g = 0; g < kMaxGroups && ok; ++g) {
       ok = cudaStreamCreateWithFlags(&ss->s[g], cudaStreamNonBlocking) == cudaSuccess &&
            cudaEventCreateWithFlags(&ss->join[g], ef) == cudaSuccess &&
-           cudaStreamCreateWithFlags(&ss->sp[g], cudaStreamNonBlocking) == cudaSuccess &&
+           cudaStreamCreateWithPriority(&ss->sp[g], cudaStreamNonBlocking, greatest) ==
+               cudaSuccess &&
+           cudaStreamCreateWithFlags(&ss->spl[g], cudaStreamNonBlocking) == cudaSuccess &&
            cudaEventCreateWithFlags(&ss->evP[g], ef) == cudaSuccess &&
            cudaEventCreateWithFlags(&ss->evB[g], ef) == cudaSuccess &&
            cudaEventCreateWithFlags(&ss->joinP[g], ef) == cudaSuccess;
@@ -317,6 +353,7 @@ int64_t host_direct_blocks() {
 int finish_call(int rc, cudaStream_t stream) { return finish(rc, stream); }
 long long device_wait_limit() { return (long long)g_wait_limit.load(); }
 bool test_skip_mma() { return g_skip_mma.load() != 0; }
+int tma_cta_cap() { return (int)g_tma_ctas.load(); }
 
 size_t vsplit_bytes(int64_t batch, int n) {
   if (batch <= 0 || n < kTmaMinN || n % 4 != 0) return 0;
@@ -372,21 +409,35 @@ Plan make_plan(int64_t batch, int n, const FactorScratch& ws) {
     p.larfb = tma_ok ? kLarfbTma : kLarfbFfma;
   else
     p.larfb = (kind == kLarfbTma && !tma_ok) ? kLarfbFfma : (int)kind;
-  // Automatic: 4 groups from n = 1024 on (measured on B200: 30.6 vs 32.8 ms for
-  // 8 x 4096^2), else 2; at most half the batch.
+  // Automatic blocking for the tensor-core update, from a sweep on B200 over
+  // n = 256 .. 4096 and batch 8 .. 640: where batch * n^2 > 2^27 the update's
+  // HBM traffic dominates and two-level blocking (each trailing column read
+  // once per 64 reflectors) wins (85.8 vs 126 ms at 64 x 4096^2, 21.2 vs
+  // 25.0 ms at 640 x 1024^2); below that, from n = 1024, the panels' latency
+  // chain dominates and the look-ahead in two batch groups wins (2.55 vs
+  // 3.22 ms at 8 x 1024^2, 21.1 vs 25.3 ms at 8 x 4096^2); smaller n takes
+  // neither (the look-ahead's extra launches cost more than they hide). The
+  // FFMA update keeps its own rule: the look-ahead from n = 4096, two-level
+  // blocking only on request.
+  const bool tma_route = p.larfb == kLarfbTma;
+  const bool heavy = (double)batch * n * n > (double)(int64_t(1) << 27);
+  const int64_t tl_mode = g_two_level.load();
+  const int64_t la_mode = g_lookahead.load();
+  const bool tl_auto = tma_route && heavy;
+  p.two_level = ws.T64 != nullptr && (tl_mode == 1 || (tl_mode == 2 && tl_auto));
+  const bool la_auto = tma_route ? (!heavy && n >= 1024) : n >= kLookaheadMinN;
+  p.lookahead = !p.two_level && ws.T2 != nullptr && (la_mode == 1 || (la_mode == 2 && la_auto));
+  // Groups: automatic 4 from n = 1024 (measured on B200: 30.6 vs 32.8 ms for
+  // 8 x 4096^2 on the FFMA update; 20.4 vs 20.9 ms on the tensor-core
+  // look-ahead), except 2 for the tensor-core look-ahead below n = 4096 (2.55
+  // vs 3.24 ms at 8 x 1024^2, 6.24 vs 7.34 ms at 8 x 2048^2), else 2; at most
+  // half the batch.
   int groups = (int)g_groups.load();
-  if (groups == 0) groups = n >= 1024 ? 4 : 2;
+  if (groups == 0)
+    groups = (tma_route && p.lookahead && n < 4096) ? 2 : (n >= 1024 ? 4 : 2);
   if (groups > batch / 2) groups = (int)(batch / 2);
   if (batch < 4) groups = 1;
   p.groups = groups < 1 ? 1 : groups;
-  // Two-level blocking (opt-in: measured on B200 it is slower at every size,
-  // 5.58 vs 5.22 ms at 640 x 512^2, 35.0 vs 29.6 ms at 8 x 4096^2) needs a
-  // 64 x 64 factor per matrix, the look-ahead a second 32 x 32 one; two-level
-  // takes precedence.
-  p.two_level = ws.T64 != nullptr && g_two_level.load() == 1;
-  const int64_t la_mode = g_lookahead.load();
-  p.lookahead = !p.two_level && ws.T2 != nullptr &&
-                (la_mode == 1 || (la_mode == 2 && n >= kLookaheadMinN));
   return p;
 }
 
@@ -459,7 +510,8 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
   if (groups <= 1) {
     const TmaRoute r0 = route_of(0);
     return blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, ws.T, ws.T2, batch, n, s,
-                                ss->sp[0], ss->evP[0], ss->evB[0], ss->joinP[0],
+                                g_panel_priority.load() ? ss->sp[0] : ss->spl[0], ss->evP[0],
+                                ss->evB[0], ss->joinP[0],
                                 tma ? &r0 : nullptr);
   }
   // Split the batch into groups that run the same kernel sequence on separate
@@ -482,7 +534,8 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     else if (la)
       rc = blocked_qr_lookahead(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn,
                                 tau + b0 * n, ws.T + b0 * tper, ws.T2 + b0 * tper, b1 - b0, n,
-                                gs, ss->sp[g], ss->evP[g], ss->evB[g], ss->joinP[g],
+                                gs, g_panel_priority.load() ? ss->sp[g] : ss->spl[g],
+                                ss->evP[g], ss->evB[g], ss->joinP[g],
                                 tma ? &rg : nullptr);
     else
       rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
@@ -647,6 +700,21 @@ int qrb_set_config(const char* key, int64_t value) {
     if (rc != QRB_OK) return rc;
     return cudaDeviceSynchronize() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
   }
+  if (std::strcmp(key, "tma_ctas") == 0) {
+    if (value < 0 || value > 4096) return QRB_ERR_INVALID_ARG;
+    g_tma_ctas.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "narrow_update") == 0) {
+    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    g_narrow.store(value);
+    return QRB_OK;
+  }
+  if (std::strcmp(key, "panel_priority") == 0) {
+    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    g_panel_priority.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "larfb_kind") == 0) {
     if (value < -1 || value > 3) return QRB_ERR_INVALID_ARG;
     g_larfb_kind.store(value);
@@ -673,7 +741,7 @@ int qrb_set_config(const char* key, int64_t value) {
     return QRB_OK;
   }
   if (std::strcmp(key, "two_level") == 0) {
-    if (value < 0 || value > 1) return QRB_ERR_INVALID_ARG;
+    if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
     g_two_level.store(value);
     return QRB_OK;
   }
@@ -722,6 +790,9 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "larfb_kind") == 0) { *value = g_larfb_kind.load(); return QRB_OK; }
   if (std::strcmp(key, "wait_limit") == 0) { *value = g_wait_limit.load(); return QRB_OK; }
   if (std::strcmp(key, "test_skip_mma") == 0) { *value = g_skip_mma.load(); return QRB_OK; }
+  if (std::strcmp(key, "tma_ctas") == 0) { *value = g_tma_ctas.load(); return QRB_OK; }
+  if (std::strcmp(key, "narrow_update") == 0) { *value = g_narrow.load(); return QRB_OK; }
+  if (std::strcmp(key, "panel_priority") == 0) { *value = g_panel_priority.load(); return QRB_OK; }
   if (std::strcmp(key, "device_error") == 0) {
     int v = 0;
     const int rc = qrb::device_error_flag(&v, false);

@@ -140,6 +140,19 @@ int launch_larfb_tc(const float* V, int64_t sVb, int64_t ldv, const float* T,
                     int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
                     int64_t batch, int r, int c, cudaStream_t stream);
 
+// Narrow in-place update C <- C - V T^T V^T C of the cw <= 32 columns next to
+// a panel (the next panel's columns): r rows, 32 reflectors read from V's
+// strictly lower part (unit diagonal implied), T 32 x 32 with row stride t_ld;
+// the rows of each matrix split across a thread-block cluster. Needs 16-byte
+// aligned rows and matrices and cw % 4 == 0 (larfb_narrow_supported).
+bool larfb_narrow_supported(const float* V, int64_t sVb, int64_t ldv, const float* C, int64_t sCb,
+                            int64_t ldc, int k, int cw);
+int launch_larfb_narrow(const float* V, int64_t sVb, int64_t ldv, const float* T, int64_t sTb,
+                        int t_ld, float* C, int64_t sCb, int64_t ldc, int64_t batch, int r,
+                        int cw, cudaStream_t stream);
+// Cluster size, rows per cluster rank and rows per staged chunk for r rows.
+void larfb_narrow_shape(int r, int* cs, int* rs, int* rch);
+
 // Two-level blocking (64 reflectors = two panels). larfb64: C_dst <- C_src -
 // V T^T V^T C_src for r x c blocks (r >= 64) with 64 reflectors read from V's
 // strictly lower part and T 64 x 64 per matrix (row stride 64); operands must
@@ -161,6 +174,9 @@ long long device_wait_limit();
 // qrb_set_config("test_skip_mma"): the TMA-fed update issues no pass-1 MMAs,
 // so its bounded waits run out (tests of the timeout path only).
 bool test_skip_mma();
+// qrb_set_config("tma_ctas"): most CTAs of one TMA-fed update launch (0 = one
+// per SM).
+int tma_cta_cap();
 // One probe kernel that waits on an mbarrier nobody arrives at for `limit`
 // cycles and then sets the device error flag.
 int launch_wait_probe(long long limit, cudaStream_t stream);

@@ -603,7 +603,10 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
   const int64_t ntc = (col_end - col0 + TCOLS - 1) / TCOLS;
   const int64_t tiles = ntc * count;
   if (tiles > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
-  const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);  // persistent: <= one CTA per SM
+  int most = sms[dev];  // persistent: at most one CTA per SM
+  const int cap = tma_cta_cap();
+  if (cap > 0 && cap < most) most = cap;
+  const int grid = (int)(tiles < most ? tiles : most);
   k_larfb_tma<KR><<<grid, NTH, Lay<KR>::SMEM_BYTES, stream>>>(
       maps.c1, maps.c2, maps.v1, maps.v2, T, sTb, (int)m0, (int)tiles, (int)ntc, j0, col0,
       col_end, n, vw_hi, vw_lo, err_ptr[dev], device_wait_limit(), test_skip_mma() ? 1 : 0);

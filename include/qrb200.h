@@ -290,6 +290,15 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 bounded waits run out, it abandons the call, sets
  *                 "device_error" and frees its resources (test only; results
  *                 of such calls are wrong).
+ *   "tma_ctas"    most CTAs of one TMA-fed update launch, 1..4096 (0, the
+ *                 default: one per SM).
+ *   "narrow_update" 0: the tensor-core route updates the next panel's 32
+ *                 columns with the TMA-fed kernel as well, instead of the
+ *                 narrow kernel that splits their rows across a cluster
+ *                 (1, the default).
+ *   "panel_priority" 0: the look-ahead stream (panels and the next panel's
+ *                 update) runs at the default stream priority instead of the
+ *                 highest (1, the default).
  *   "device_error" read: 1 if a kernel's bounded device-side wait timed out
  *                 since the last reset (synchronous); set to 0 to reset.
  *   "groups"      1..4: batches of 4 or more matrices with n > 32 are split
@@ -301,16 +310,25 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *   "host_direct" 0..3 (default 3): how qrb_geqrf_f32_host reaches mapped
  *                 page-locked host buffers for n <= 32 (see there).
  *   "direct_blocks" grid of the mode-1 kernel in blocks of 4 warps (0 = 148).
- *   "lookahead"   blocked route: 0 = off, 1 = on, 2 (default) = from n = 4096;
- *                 needs the full qrb_workspace_bytes. Panel j + 1 and the
- *                 update of its columns run on a second stream while the rest
- *                 of step j's update runs; results are unchanged.
- *   "two_level"   blocked route: 0 (default) = off, 1 = on; needs the full
- *                 qrb_workspace_bytes. Two 32-column panels are combined into
- *                 one 64-reflector block (T 64 x 64) for the trailing update;
- *                 takes precedence over "lookahead". Same results to FP32
- *                 rounding; slower than the default on B200 at every measured
- *                 size, kept as an option.
+ *   "lookahead"   blocked route: 0 = off, 1 = on, 2 (default) = automatic
+ *                 (below); needs the full qrb_workspace_bytes. Panel j + 1
+ *                 and the update of its columns run on a second stream (at the
+ *                 highest priority) while the rest of step j's update runs.
+ *                 With the FFMA update the results are unchanged; with the
+ *                 tensor-core update the next panel's 32 columns are updated
+ *                 by an FFMA kernel instead, the same results to FP32
+ *                 rounding.
+ *   "two_level"   blocked route: 0 = off, 1 = on, 2 (default) = automatic;
+ *                 needs the full qrb_workspace_bytes. Two 32-column panels
+ *                 are combined into one 64-reflector block (T 64 x 64) for the
+ *                 trailing update; takes precedence over "lookahead". Same
+ *                 results to FP32 rounding.
+ *                 Automatic (measured on B200): with the tensor-core update,
+ *                 two-level where batch * n^2 > 2^27 (the update's traffic
+ *                 dominates), else the look-ahead from n = 1024 (in 2 batch
+ *                 groups; the panels' latency chain dominates), else neither;
+ *                 with the FFMA update, the look-ahead from n = 4096 and no
+ *                 two-level blocking.
  *   "panel_rpt"   rows per thread of the panel kernel: 0 (default) = 1 up to
  *                 128 rows, else 4; 1 or 2 force that many (CTAs of up to 512
  *                 or 256 threads; 4 where more than 8 CTAs would be needed).

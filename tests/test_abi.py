@@ -206,6 +206,19 @@ def test_config_keys():
         _lib.set_config("test_skip_mma", 2)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("wait_probe", 10)
+    assert _lib.get_config("tma_ctas") == 0
+    _lib.set_config("tma_ctas", 96)
+    assert _lib.get_config("tma_ctas") == 96
+    _lib.set_config("tma_ctas", 0)
+    for key in ("narrow_update", "panel_priority"):
+        assert _lib.get_config(key) == 1
+        _lib.set_config(key, 0)
+        assert _lib.get_config(key) == 0
+        _lib.set_config(key, 1)
+        with pytest.raises(_lib.QRBError):
+            _lib.set_config(key, 2)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("tma_ctas", -1)
     assert _lib.get_config("host_direct") in (0, 1, 2, 3)
     _lib.set_config("host_direct", 0)
     assert _lib.get_config("host_direct") == 0
@@ -232,12 +245,12 @@ def test_config_keys():
     _lib.set_config("lookahead", 2)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("lookahead", 3)
-    assert _lib.get_config("two_level") == 0
-    _lib.set_config("two_level", 1)
-    assert _lib.get_config("two_level") == 1
-    _lib.set_config("two_level", 0)
+    assert _lib.get_config("two_level") == 2  # automatic
+    for v in (0, 1, 2):
+        _lib.set_config("two_level", v)
+        assert _lib.get_config("two_level") == v
     with pytest.raises(_lib.QRBError):
-        _lib.set_config("two_level", 2)
+        _lib.set_config("two_level", 3)
     assert _lib.get_config("panel_rpt") == 0
     for v in (1, 2, 4, 0):
         _lib.set_config("panel_rpt", v)
@@ -293,10 +306,20 @@ def test_route_is_a_function_of_batch_n_and_workspace():
     ws = L.qrb_workspace_bytes(8, 4096)
     assert L.qrb_route(8, 4096, 0) == 0  # the blocked route needs workspace
     code = L.qrb_route(8, 4096, ws)
-    assert code & 0xF == 3 and (code >> 12) & 0xF == 4
+    assert code & 0xF == 3 and code & (1 << 8)  # blocked, with the look-ahead
     # the tensor-core update needs the split-reflector part of the workspace
-    # (and, on a machine without a CUDA driver, the TMA encoder: FFMA then)
-    assert (code >> 4) & 0xF in (0, 3)
+    # (and, on a machine without a CUDA driver, the TMA encoder: FFMA then);
+    kind = (code >> 4) & 0xF
+    assert kind in (0, 3)
+    assert (code >> 12) & 0xF == 4
+    la2 = L.qrb_route(8, 2048, L.qrb_workspace_bytes(8, 2048))
+    assert la2 & (1 << 8) if kind == 3 else not la2 & (1 << 8)
+    assert (la2 >> 12) & 0xF == (2 if kind == 3 else 4)
+    big = L.qrb_route(64, 4096, L.qrb_workspace_bytes(64, 4096))
+    if kind == 3:  # batch * n^2 > 2^27: two-level blocking, no look-ahead
+        assert big & (1 << 9) and not big & (1 << 8)
+    else:
+        assert big & (1 << 8) and not big & (1 << 9)
     assert (L.qrb_route(8, 4096, 4 * 8 * 32 * 32 * 4) >> 4) & 0xF == 0
     assert (L.qrb_route(8, 130, L.qrb_workspace_bytes(8, 130)) >> 4) & 0xF == 0
     assert L.qrb_route(8, 4096, ws) == code  # no hidden state between queries

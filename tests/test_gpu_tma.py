@@ -92,21 +92,28 @@ def test_tma_route_matches_lapack_on_config_3_shape():
     assert checker.check(A, H.cpu(), tau.cpu()).passed
 
 
-def test_tma_lookahead_and_groups_leave_bits_unchanged():
+def test_tma_groups_leave_bits_unchanged_and_lookahead_agrees():
+    # the batch groups change no bits, with or without the look-ahead; the
+    # look-ahead updates the next panel's columns with the narrow FFMA kernel
+    # instead of the tensor-core one, so it agrees within the parity bar
     A = torch.randn(8, 512, 512, generator=torch.Generator().manual_seed(3)).to(DEV)
-    outs = []
+    outs = {}
     old = _hooks(lookahead=0, groups=1)
     try:
-        for la, g in ((0, 1), (1, 1), (0, 4), (1, 4), (1, 2)):
+        for la, g in ((0, 1), (1, 1), (0, 4), (1, 4), (1, 2), (0, 2)):
             _lib.set_config("lookahead", la)
             _lib.set_config("groups", g)
             assert "tcgen05_tma" in api.route(8, 512)
-            outs.append(api.geqrf(A))
+            outs[la, g] = api.geqrf(A)
         torch.cuda.synchronize()
     finally:
         _restore(old)
-    for H, tau in outs[1:]:
-        assert torch.equal(H, outs[0][0]) and torch.equal(tau, outs[0][1])
+    for (la, g), (H, tau) in outs.items():
+        H0, t0 = outs[la, 1]
+        assert torch.equal(H, H0) and torch.equal(tau, t0), (la, g)
+    par = checker.parity(outs[1, 1][0].cpu(), outs[1, 1][1].cpu(), outs[0, 1][0].cpu(),
+                         outs[0, 1][1].cpu())
+    assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 1e-3, par
 
 
 def test_tma_route_in_place_and_strided_inputs():
@@ -234,4 +241,47 @@ def test_two_level_tensor_core_route(b, n, groups):
     H64, t64 = torch.geqrf(A.double())
     par = checker.parity(H.cpu(), tau.cpu(), H64.float(), t64.float())
     assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 5e-4, par
+    assert _lib.get_config("device_error") == 0
+
+
+def test_narrow_update_agrees_with_the_tma_kernel():
+    # the next panel's 32 columns by the narrow cluster kernel (default) or by
+    # the TMA-fed kernel: both within 1e-4 of each other and of FP64 LAPACK
+    b, n = 4, 768
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(21)).to(DEV)
+    old = _hooks(narrow_update=1, lookahead=1)
+    try:
+        Hn, tn = api.geqrf(A)
+        _lib.set_config("narrow_update", 0)
+        Ht, tt = api.geqrf(A)
+        torch.cuda.synchronize()
+    finally:
+        _restore(old)
+    H64, t64 = torch.geqrf(A.cpu().double())
+    for H, tau in ((Hn, tn), (Ht, tt)):
+        par = checker.parity(H.cpu(), tau.cpu(), H64.float(), t64.float())
+        assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 5e-4, par
+    par = checker.parity(Hn.cpu(), tn.cpu(), Ht.cpu(), tt.cpu())
+    assert par.h_rel < RTOL and par.col_rel < RTOL, par
+    assert _lib.get_config("device_error") == 0
+
+
+def test_tall_panels_stage_the_narrow_update_in_chunks():
+    # n = 4160: up to 4128 rows for the narrow update, 544 per cluster rank,
+    # staged in two chunks (512 rows at most per chunk)
+    n = 4160
+    A = torch.randn(1, n, n, generator=torch.Generator().manual_seed(5)).to(DEV)
+    assert "tcgen05_tma" in api.route(1, n)
+    old = _hooks(lookahead=1)
+    try:
+        H, tau = api.geqrf(A)
+        _lib.set_config("larfb_kind", 0)
+        Hf, tf = api.geqrf(A)
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_config("larfb_kind", -1)
+        _restore(old)
+    assert checker.check(A, H, tau).passed
+    par = checker.parity(H.cpu(), tau.cpu(), Hf.cpu(), tf.cpu())
+    assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 1e-3, par
     assert _lib.get_config("device_error") == 0
