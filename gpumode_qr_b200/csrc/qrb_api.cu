@@ -90,8 +90,11 @@ struct TmaRoute {
     return Vs + ((int64_t)(2 * buf) * batch_total + m0) * n * qrb::kPanelW;
   }
   int64_t plane(int n) const { return batch_total * n * qrb::kPanelW; }
-  // two-level blocks: hi plane [batch][n][64] at this group's first matrix
-  float* vsplit64(int n) const { return Vs + m0 * n * 2 * qrb::kPanelW; }
+  // two-level blocks: hi plane [batch][n][64] of V-buffer `buf` at this
+  // group's first matrix (the remainder one plane further on)
+  float* vsplit64(int buf, int n) const {
+    return Vs + ((int64_t)(2 * buf) * batch_total + m0) * n * 2 * qrb::kPanelW;
+  }
   int64_t plane64(int n) const { return batch_total * n * 2 * qrb::kPanelW; }
 };
 
@@ -246,7 +249,7 @@ int blocked_qr2(const float* A, int64_t strideA_b, int64_t strideA_row, float* H
     // tensor-core route: both panels write their split reflectors into one
     // 64-wide plane when a 64-reflector update follows
     const bool big = tr != nullptr && r > K2;
-    float* vs = big ? tr->vsplit64(n) : nullptr;
+    float* vs = big ? tr->vsplit64(0, n) : nullptr;
     const int64_t vpl = tr != nullptr ? tr->plane64(n) : 0;
     int rc = qrb::launch_panel(Sp, sb, ld, Hp, nn, n, tau + j0, n, T1, tsb, K2, nullptr, batch,
                                r, w1, s, vs, (int64_t)n * K2, vpl, j0, K2, big);
@@ -283,6 +286,80 @@ int blocked_qr2(const float* A, int64_t strideA_b, int64_t strideA_row, float* H
     if (rc != QRB_OK) return rc;
   }
   return QRB_OK;
+}
+
+// Two-level blocking with the look-ahead, tensor-core route only (H holds A,
+// tr non-null). Per 64-column block j0 (T64 alternating between two buffers,
+// the split reflectors between V-buffers 0 and 1):
+//   sp  panel 1                     columns j0 .. j0+31 (T1)
+//       narrow update, panel 1      columns j0+32 .. j0+95 (panel 2's and the
+//                                   next block's first panel's)
+//       panel 2                     rows and columns from j0+32 (T2)
+//       narrow update, panel 2      columns j0+64 .. j0+95
+//   sb  t64, then the 64-reflector update of the columns from j0+96.
+// The sp chain reaches the next block's first panel without waiting for the
+// wide update; the next block's first narrow update waits for it (it touches
+// the columns from j0+96). Both streams end joined into sb.
+int blocked_qr2_lookahead(float* H, float* tau, float* T64a, float* T64b, int64_t batch, int n,
+                          cudaStream_t sb, cudaStream_t sp, cudaEvent_t evP, cudaEvent_t evB,
+                          cudaEvent_t joinP, const TmaRoute& tr) {
+  const int64_t nn = (int64_t)n * n;
+  constexpr int W = qrb::kPanelW;
+  constexpr int K2 = 2 * W;
+  constexpr int64_t tsb = (int64_t)K2 * K2;
+  const int64_t vpl = tr.plane64(n);
+  // the reflectors at Vp (r rows) applied to the cw columns at C: the narrow
+  // kernel, or FFMA where its operands do not allow it
+  auto narrow = [&](float* Vp, const float* T, int r, float* C, int cw, cudaStream_t st) {
+    if (cw <= 0) return (int)QRB_OK;
+    if (g_narrow.load() != 0 && qrb::larfb_narrow_supported(Vp, nn, n, C, nn, n, W, cw))
+      return qrb::launch_larfb_narrow(Vp, nn, n, T, tsb, K2, C, nn, n, batch, r, cw, st);
+    return larfb_any(Vp, nn, n, T, tsb, K2, C, nn, n, C, nn, n, batch, r, W, cw, st);
+  };
+  if (cudaEventRecord(evB, sb) != cudaSuccess || cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess)
+    return QRB_ERR_LAUNCH;
+  int rc = QRB_OK;
+  for (int j0 = 0, blk = 0; j0 < n && rc == QRB_OK; j0 += K2, ++blk) {
+    const int buf = blk & 1;
+    float* T64 = buf ? T64b : T64a;
+    float* T1 = T64;
+    float* T2 = T64 + W * K2 + W;
+    const int r = n - j0;
+    const int w1 = r < W ? r : W;
+    const bool wide = r > K2 + W;  // a 64-reflector update follows
+    float* Hp = H + (int64_t)j0 * n + j0;
+    float* vs = wide ? tr.vsplit64(buf, n) : nullptr;
+    rc = qrb::launch_panel(Hp, nn, n, Hp, nn, n, tau + j0, n, T1, tsb, K2, nullptr, batch, r, w1,
+                           sp, vs, (int64_t)n * K2, vpl, j0, K2, wide);
+    if (rc != QRB_OK || r <= W) break;
+    // the columns from j0+32 were last written by the previous block's wide update
+    if (cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+    const int c1 = r - W < K2 ? r - W : K2;
+    rc = narrow(Hp, T1, r, Hp + W, c1, sp);
+    if (rc != QRB_OK) break;
+    const int w2 = r - W < W ? r - W : W;
+    float* Hq = Hp + (int64_t)W * n + W;
+    rc = qrb::launch_panel(Hq, nn, n, Hq, nn, n, tau + j0 + W, n, T2, tsb, K2, nullptr, batch,
+                           r - W, w2, sp, wide ? vs + W : nullptr, (int64_t)n * K2, vpl, j0 + W,
+                           K2, false);
+    if (rc != QRB_OK) break;
+    if (cudaEventRecord(evP, sp) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+    const int c = r - K2;
+    if (c <= 0) break;
+    rc = narrow(Hq, T2, r - W, Hq + W, c < W ? c : W, sp);
+    if (rc != QRB_OK) break;
+    if (!wide) continue;  // the next block is the last, at most 32 columns
+    if (cudaStreamWaitEvent(sb, evP, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+    rc = qrb::launch_t64(Hp, nn, n, T64, tsb, batch, r, sb);
+    if (rc == QRB_OK)
+      rc = qrb::launch_larfb_tma(*tr.maps, T64, tsb, tr.m0, batch, j0, j0 + K2 + W, n, n, buf,
+                                 sb);
+    if (rc != QRB_OK) break;
+    if (cudaEventRecord(evB, sb) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+  }
+  if (cudaEventRecord(joinP, sp) != cudaSuccess || cudaStreamWaitEvent(sb, joinP, 0) != cudaSuccess)
+    if (rc == QRB_OK) rc = QRB_ERR_LAUNCH;
+  return rc;
 }
 
 // Internal streams for batch groups, created once per device and kept for the
@@ -357,7 +434,7 @@ int tma_cta_cap() { return (int)g_tma_ctas.load(); }
 
 size_t vsplit_bytes(int64_t batch, int n) {
   if (batch <= 0 || n < kTmaMinN || n % 4 != 0) return 0;
-  return 4 * (size_t)batch * n * kPanelW * sizeof(float);
+  return 8 * (size_t)batch * n * kPanelW * sizeof(float);
 }
 
 size_t min_workspace_bytes(int64_t batch) {
@@ -372,8 +449,9 @@ FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch, int n
   f.T = base;
   if (bytes >= 2 * unit) f.T2 = base + unit / sizeof(float);
   if (bytes >= 4 * unit) f.T64 = base;
+  if (bytes >= 8 * unit) f.T64b = base + 4 * unit / sizeof(float);
   const size_t vb = vsplit_bytes(batch, n);
-  if (vb != 0 && bytes >= 4 * unit + vb) f.Vs = base + 4 * unit / sizeof(float);
+  if (vb != 0 && bytes >= 8 * unit + vb) f.Vs = base + 8 * unit / sizeof(float);
   return f;
 }
 
@@ -410,31 +488,33 @@ Plan make_plan(int64_t batch, int n, const FactorScratch& ws) {
   else
     p.larfb = (kind == kLarfbTma && !tma_ok) ? kLarfbFfma : (int)kind;
   // Automatic blocking for the tensor-core update, from a sweep on B200 over
-  // n = 256 .. 4096 and batch 8 .. 640: where batch * n^2 > 2^27 the update's
-  // HBM traffic dominates and two-level blocking (each trailing column read
-  // once per 64 reflectors) wins (85.8 vs 126 ms at 64 x 4096^2, 21.2 vs
-  // 25.0 ms at 640 x 1024^2); below that, from n = 1024, the panels' latency
-  // chain dominates and the look-ahead in two batch groups wins (2.55 vs
-  // 3.22 ms at 8 x 1024^2, 21.1 vs 25.3 ms at 8 x 4096^2); smaller n takes
-  // neither (the look-ahead's extra launches cost more than they hide). The
-  // FFMA update keeps its own rule: the look-ahead from n = 4096, two-level
-  // blocking only on request.
+  // n = 256 .. 4096 and batch 8 .. 640. From n = 1024 two-level blocking
+  // (each trailing column read once per 64 reflectors) wins everywhere; with
+  // the look-ahead as well while batch * n <= 2^16, where the panels' latency
+  // chain sets the time (18.1 vs 20.4 ms one-level with the look-ahead and
+  // 23.5 ms two-level alone at 8 x 4096^2; 27.2 vs 29.5 ms at 16 x 4096^2;
+  // 10.0 vs 10.8 ms at 32 x 2048^2; 3.45 vs 3.61 ms at 64 x 1024^2), without
+  // it above, where the update's traffic does (47.1 vs 48.4 ms at
+  // 32 x 4096^2, 6.64 vs 6.93 ms at 160 x 1024^2). Below n = 1024 the plain
+  // loop is as fast or faster (4.63 ms two-level, 4.63 plain at 640 x 512^2;
+  // 0.40 vs 0.42 ms with the look-ahead at 32 x 256^2). The FFMA update keeps
+  // its own rule: the look-ahead from n = 4096, two-level only on request.
   const bool tma_route = p.larfb == kLarfbTma;
-  const bool heavy = (double)batch * n * n > (double)(int64_t(1) << 27);
+  const bool tl_auto = tma_route && n >= 1024;
+  const bool la_auto = tma_route ? tl_auto && (double)batch * n <= 65536.0 : n >= kLookaheadMinN;
   const int64_t tl_mode = g_two_level.load();
   const int64_t la_mode = g_lookahead.load();
-  const bool tl_auto = tma_route && heavy;
   p.two_level = ws.T64 != nullptr && (tl_mode == 1 || (tl_mode == 2 && tl_auto));
-  const bool la_auto = tma_route ? (!heavy && n >= 1024) : n >= kLookaheadMinN;
-  p.lookahead = !p.two_level && ws.T2 != nullptr && (la_mode == 1 || (la_mode == 2 && la_auto));
+  const bool la_want = la_mode == 1 || (la_mode == 2 && la_auto);
+  // two-level blocking combines with the look-ahead on the tensor-core route
+  // (second 64 x 64 factor and double-buffered split reflectors)
+  p.lookahead = la_want && (p.two_level ? tma_route && ws.T64b != nullptr : ws.T2 != nullptr);
   // Groups: automatic 4 from n = 1024 (measured on B200: 30.6 vs 32.8 ms for
-  // 8 x 4096^2 on the FFMA update; 20.4 vs 20.9 ms on the tensor-core
-  // look-ahead), except 2 for the tensor-core look-ahead below n = 4096 (2.55
-  // vs 3.24 ms at 8 x 1024^2, 6.24 vs 7.34 ms at 8 x 2048^2), else 2; at most
-  // half the batch.
+  // 8 x 4096^2 on the FFMA update; 18.1 vs 18.5 ms and 3.45 vs 3.61 ms at
+  // 8 x 4096^2 and 64 x 1024^2 on the tensor-core two-level look-ahead),
+  // else 2; at most half the batch.
   int groups = (int)g_groups.load();
-  if (groups == 0)
-    groups = (tma_route && p.lookahead && n < 4096) ? 2 : (n >= 1024 ? 4 : 2);
+  if (groups == 0) groups = n >= 1024 ? 4 : 2;
   if (groups > batch / 2) groups = (int)(batch / 2);
   if (batch < 4) groups = 1;
   p.groups = groups < 1 ? 1 : groups;
@@ -509,6 +589,10 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
   std::lock_guard<std::mutex> lock(ss->mu);
   if (groups <= 1) {
     const TmaRoute r0 = route_of(0);
+    cudaStream_t sp = g_panel_priority.load() ? ss->sp[0] : ss->spl[0];
+    if (tl)  // with la: two-level blocking with the look-ahead
+      return blocked_qr2_lookahead(H, tau, ws.T64, ws.T64b, batch, n, s, sp, ss->evP[0],
+                                   ss->evB[0], ss->joinP[0], r0);
     return blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, ws.T, ws.T2, batch, n, s,
                                 g_panel_priority.load() ? ss->sp[0] : ss->spl[0], ss->evP[0],
                                 ss->evB[0], ss->joinP[0],
@@ -528,7 +612,12 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     cudaStream_t gs = ss->s[g];
     if (cudaStreamWaitEvent(gs, ss->fork, 0) != cudaSuccess) return QRB_ERR_LAUNCH;
     const TmaRoute rg = route_of(b0);
-    if (tl)
+    if (tl && la)
+      rc = blocked_qr2_lookahead(H + b0 * nn, tau + b0 * n, ws.T64 + b0 * 4 * tper,
+                                 ws.T64b + b0 * 4 * tper, b1 - b0, n, gs,
+                                 g_panel_priority.load() ? ss->sp[g] : ss->spl[g], ss->evP[g],
+                                 ss->evB[g], ss->joinP[g], rg);
+    else if (tl)
       rc = blocked_qr2(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
                        ws.T64 + b0 * 4 * tper, b1 - b0, n, gs, tma ? &rg : nullptr);
     else if (la)
@@ -572,11 +661,12 @@ int32_t qrb_fused_max_n(void) { return qrb::kFusedMidMaxN; }
 
 size_t qrb_workspace_bytes(int64_t batch, int32_t n) {
   if (batch <= 0 || n <= qrb::kFusedMaxN) return 0;
-  // Four 32 x 32 units per matrix: one compact-WY factor T is the minimum, a
-  // second enables the panel look-ahead, all four (one 64 x 64 factor) the
-  // two-level blocking; then the split reflectors of the tensor-core update
-  // (two V buffers x hi / lo, n x 32 each) where that update applies.
-  return 4 * (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float) +
+  // Eight 32 x 32 units per matrix: one compact-WY factor T is the minimum, a
+  // second enables the panel look-ahead, four (one 64 x 64 factor) the
+  // two-level blocking, all eight (two 64 x 64 factors) two-level blocking
+  // with the look-ahead; then the split reflectors of the tensor-core update
+  // (two V buffers x hi / lo, n x 64 each) where that update applies.
+  return 8 * (size_t)batch * qrb::kPanelW * qrb::kPanelW * sizeof(float) +
          qrb::vsplit_bytes(batch, n);
 }
 

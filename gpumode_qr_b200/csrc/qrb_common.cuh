@@ -140,11 +140,11 @@ int launch_larfb_tc(const float* V, int64_t sVb, int64_t ldv, const float* T,
                     int64_t ldcs, float* Cdst, int64_t sCdb, int64_t ldcd,
                     int64_t batch, int r, int c, cudaStream_t stream);
 
-// Narrow in-place update C <- C - V T^T V^T C of the cw <= 32 columns next to
-// a panel (the next panel's columns): r rows, 32 reflectors read from V's
+// Narrow in-place update C <- C - V T^T V^T C of the cw <= 64 columns next to
+// a panel (the next panels' columns): r rows, 32 reflectors read from V's
 // strictly lower part (unit diagonal implied), T 32 x 32 with row stride t_ld;
-// the rows of each matrix split across a thread-block cluster. Needs 16-byte
-// aligned rows and matrices and cw % 4 == 0 (larfb_narrow_supported).
+// one cluster per matrix and 32-column block, splitting the rows. Needs
+// 16-byte aligned rows and matrices and cw % 4 == 0 (larfb_narrow_supported).
 bool larfb_narrow_supported(const float* V, int64_t sVb, int64_t ldv, const float* C, int64_t sCb,
                             int64_t ldc, int k, int cw);
 int launch_larfb_narrow(const float* V, int64_t sVb, int64_t ldv, const float* T, int64_t sTb,
@@ -189,14 +189,17 @@ int device_error_ptr(int** p);
 // The blocked route's factor scratch, carved from the caller's workspace of
 // `bytes` for `batch` matrices: T one 32 x 32 factor per matrix (required),
 // T2 a second one for the panel look-ahead, T64 one 64 x 64 factor per matrix
-// for two-level blocking (each nullptr when the workspace is too small).
-// Vs: the split reflectors of the tensor-core update, [4][batch][n][32]
-// (planes 2 * buf + 0 / 1 = hi / lo of V-buffer buf), when the workspace
-// holds them.
+// for two-level blocking (overlapping T and T2), T64b a second 64 x 64 one
+// for two-level blocking with the look-ahead (each nullptr when the workspace
+// is too small). Vs: the split reflectors of the tensor-core update, when the
+// workspace holds them: for 32-reflector blocks [4][batch][n][32] (planes
+// 2 * buf + 0 / 1 = hi / lo of V-buffer buf), for 64-reflector blocks the
+// same memory as [4][batch][n][64].
 struct FactorScratch {
   float* T = nullptr;
   float* T2 = nullptr;
   float* T64 = nullptr;
+  float* T64b = nullptr;
   float* Vs = nullptr;
 };
 FactorScratch factor_scratch(void* workspace, size_t bytes, int64_t batch, int n);

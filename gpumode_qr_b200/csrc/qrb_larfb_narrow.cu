@@ -1,6 +1,6 @@
-// Narrow trailing update: C <- C - V T^T (V^T C) for the (at most) 32 columns
+// Narrow trailing update: C <- C - V T^T (V^T C) for the (at most) 64 columns
 // next to a panel, in place, FP32 FFMA, with the rows of each matrix split
-// across a thread-block cluster.
+// across a thread-block cluster (one cluster per matrix and 32-column block).
 //
 // This is the update the look-ahead puts on the critical path: the next panel
 // waits for its own 32 columns, which are a tall r x 32 block (r up to 8192).
@@ -121,7 +121,8 @@ k_larfb_narrow(const float* __restrict__ V, int64_t sVb, int64_t ldv, const floa
   const uint32_t rank = cs > 1 ? cluster_rank() : 0;
   const int64_t m = blockIdx.x / cs;
   const float* Vm = V + m * sVb;
-  float* Cm = C + m * sCb;
+  float* Cm = C + m * sCb + K * blockIdx.y;  // this CTA's block of 32 columns
+  cw = min(K, cw - K * (int)blockIdx.y);
   const float* Tm = T + m * sTb;
   for (int e = tid; e < K * K; e += NT) Ts[(e >> 5) * (K + 1) + (e & 31)] = Tm[(e >> 5) * t_ld + (e & 31)];
 
@@ -232,7 +233,7 @@ void larfb_narrow_shape(int r, int* cs, int* rs, int* rch) {
 
 bool larfb_narrow_supported(const float* V, int64_t sVb, int64_t ldv, const float* C, int64_t sCb,
                             int64_t ldc, int k, int cw) {
-  return k == K && cw >= 1 && cw <= K && cw % 4 == 0 && ldv % 4 == 0 && sVb % 4 == 0 &&
+  return k == K && cw >= 1 && cw <= 2 * K && cw % 4 == 0 && ldv % 4 == 0 && sVb % 4 == 0 &&
          ldc % 4 == 0 && sCb % 4 == 0 && aligned16(V) && aligned16(C);
 }
 
@@ -255,7 +256,7 @@ int launch_larfb_narrow(const float* V, int64_t sVb, int64_t ldv, const float* T
     attr_set[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(batch * cs), 1, 1);
+  cfg.gridDim = dim3((unsigned)(batch * cs), (unsigned)((cw + K - 1) / K), 1);
   cfg.blockDim = dim3(NT, 1, 1);
   cfg.dynamicSmemBytes = L.bytes();
   cfg.stream = stream;

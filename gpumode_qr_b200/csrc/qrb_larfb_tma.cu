@@ -565,9 +565,9 @@ int make_larfb_maps(LarfbMaps* maps, const float* H, const float* Vs, int64_t ba
   const uint64_t nn = (uint64_t)n, k = (uint64_t)kr;
   const uint64_t cdims[3] = {nn, nn, (uint64_t)batch};
   const uint64_t cstr[2] = {nn * 4, nn * nn * 4};
-  // the split reflectors: 4 planes of [batch][n][32] (two V buffers x hi / lo)
-  // for 32-reflector blocks, 2 planes of [batch][n][64] (hi / lo) for 64
-  const uint64_t vdims[4] = {k, nn, (uint64_t)batch, kr == 32 ? 4u : 2u};
+  // the split reflectors: 4 planes (two V buffers x hi / lo) of
+  // [batch][n][kr]
+  const uint64_t vdims[4] = {k, nn, (uint64_t)batch, 4u};
   const uint64_t vstr[3] = {k * 4, nn * k * 4, (uint64_t)batch * nn * k * 4};
   // pass-1 boxes are MN-major operands (32-byte-atom swizzle); pass-2 V boxes
   // are K-major operands and the C boxes take the staged reduce-add (plain
@@ -620,14 +620,16 @@ int launch_larfb_tma(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t
                      cudaStream_t stream) {
   if (count <= 0 || col_end <= col0) return QRB_OK;
   const int kr = maps.kr;
-  if (j0 < 0 || j0 + kr > n || col0 % 4 != 0 || m0 < 0 || m0 + count > 0x7fffffffLL)
+  if (j0 < 0 || j0 + kr > n || col0 % 4 != 0 || m0 < 0 || m0 + count > 0x7fffffffLL ||
+      vbuf < 0 || vbuf > 1)
     return QRB_ERR_UNSUPPORTED;
   if (col_end != n && (col_end - col0) % 32 != 0) return QRB_ERR_UNSUPPORTED;
   if (kr == 32)
     return launch_tma_t<32>(maps, T, sTb, m0, count, j0, col0, col_end, n, 2 * vbuf, 2 * vbuf + 1,
                             stream);
-  if (kr == 64 && vbuf == 0)
-    return launch_tma_t<64>(maps, T, sTb, m0, count, j0, col0, col_end, n, 0, 1, stream);
+  if (kr == 64)
+    return launch_tma_t<64>(maps, T, sTb, m0, count, j0, col0, col_end, n, 2 * vbuf,
+                            2 * vbuf + 1, stream);
   return QRB_ERR_UNSUPPORTED;
 }
 

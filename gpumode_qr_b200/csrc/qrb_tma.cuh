@@ -155,9 +155,9 @@ bool encode_f32_sw128(CUtensorMap* map, const void* base, int rank, const uint64
 
 // The tensor-core trailing update (qrb_larfb_tma.cu). Tensor maps over the
 // whole batch of one qrb_geqrf_f32 call: H [batch][n][n] (C boxes for pass-1
-// loads and pass-2 reduce-adds) and the panels' split reflectors: for blocks
-// of kr = 32 reflectors Vs [4][batch][n][32] (plane 2 * buf + 0 = TF32 high
-// part, + 1 = remainder), for kr = 64 (two panels) Vs [2][batch][n][64].
+// loads and pass-2 reduce-adds) and the panels' split reflectors,
+// Vs [4][batch][n][kr] for blocks of kr = 32 or 64 (two panels) reflectors
+// (plane 2 * buf + 0 = TF32 high part of V-buffer buf, + 1 = remainder).
 struct LarfbMaps {
   CUtensorMap c1, c2, v1, v2;
   int kr = 32;
@@ -168,7 +168,7 @@ int make_larfb_maps(LarfbMaps* maps, const float* H, const float* Vs, int64_t ba
 // C <- C - V T^T V^T C for the columns [col0, col_end) of rows [j0, n) of
 // matrices m0 .. m0 + count - 1 of the maps (T: kr x kr per matrix, stride
 // sTb, pointing at matrix m0's factor), with the reflectors of V-buffer vbuf
-// (0 for kr = 64). col_end is n or col0 + a multiple of 32.
+// (0 or 1). col_end is n or col0 + a multiple of 32.
 int launch_larfb_tma(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
                      int64_t count, int j0, int col0, int col_end, int n, int vbuf,
                      cudaStream_t stream);

@@ -61,12 +61,13 @@ QRB_API const char* qrb_status_string(int status);
 QRB_API int32_t qrb_max_n(void);
 
 /* Bytes of device workspace to give qrb_geqrf_f32 for (batch, n): 0 for
- * n <= 32; otherwise four 32 x 32 units (16 KiB) per matrix, plus, for
+ * n <= 32; otherwise eight 32 x 32 units (32 KiB) per matrix, plus, for
  * n >= 129 with n % 4 == 0, the split reflectors of the tensor-core trailing
- * update (two buffers of n x 32 high parts and n x 32 remainders, 512 * n
- * bytes per matrix). One 32 x 32 unit per matrix is the minimum accepted;
- * two enable the panel look-ahead ("lookahead" below), four two-level
- * blocking ("two_level"), the whole amount the tensor-core update. */
+ * update (four buffers of n x 32 high parts and n x 32 remainders,
+ * 1024 * n bytes per matrix). One 32 x 32 unit per matrix is the minimum
+ * accepted; two enable the panel look-ahead ("lookahead" below), four
+ * two-level blocking ("two_level"), the whole amount the tensor-core update
+ * (and with it two-level blocking with the look-ahead). */
 QRB_API size_t qrb_workspace_bytes(int64_t batch, int32_t n);
 
 /*
@@ -324,11 +325,12 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 trailing update; takes precedence over "lookahead". Same
  *                 results to FP32 rounding.
  *                 Automatic (measured on B200): with the tensor-core update,
- *                 two-level where batch * n^2 > 2^27 (the update's traffic
- *                 dominates), else the look-ahead from n = 1024 (in 2 batch
- *                 groups; the panels' latency chain dominates), else neither;
- *                 with the FFMA update, the look-ahead from n = 4096 and no
- *                 two-level blocking.
+ *                 from n = 1024 two-level blocking, with the look-ahead as
+ *                 well while batch * n <= 65536 (the panels' latency chain
+ *                 sets the time there, the update's traffic above), below
+ *                 n = 1024 neither; with the FFMA update, the look-ahead from
+ *                 n = 4096 and no two-level blocking. Two-level blocking with
+ *                 the look-ahead needs the tensor-core update.
  *   "panel_rpt"   rows per thread of the panel kernel: 0 (default) = 1 up to
  *                 128 rows, else 4; 1 or 2 force that many (CTAs of up to 512
  *                 or 256 threads; 4 where more than 8 CTAs would be needed).

@@ -58,20 +58,21 @@ def test_status_strings_and_constants():
 def test_workspace_bytes():
     L = _lib.lib()
     assert L.qrb_workspace_bytes(4096, 32) == 0
-    assert L.qrb_workspace_bytes(8, 64) == 4 * 8 * 32 * 32 * 4
+    unit = 8 * 32 * 32 * 4  # one 32 x 32 factor per matrix
+    assert L.qrb_workspace_bytes(8, 64) == 8 * unit
     assert L.qrb_workspace_bytes(0, 512) == 0
-    # from n = 129 with n % 4 == 0: plus two buffers of split reflectors
-    # (hi and lo, n x 32 each) for the tensor-core update
-    assert L.qrb_workspace_bytes(8, 128) == 4 * 8 * 32 * 32 * 4
-    assert L.qrb_workspace_bytes(8, 130) == 4 * 8 * 32 * 32 * 4
-    assert L.qrb_workspace_bytes(8, 4096) == 4 * 8 * 32 * 32 * 4 + 4 * 8 * 4096 * 32 * 4
+    # from n = 129 with n % 4 == 0: plus four buffers of split reflectors
+    # (two V buffers x hi and lo, n x 64 each) for the tensor-core update
+    assert L.qrb_workspace_bytes(8, 128) == 8 * unit
+    assert L.qrb_workspace_bytes(8, 130) == 8 * unit
+    assert L.qrb_workspace_bytes(8, 4096) == 8 * unit + 4 * 8 * 4096 * 64 * 4
 
 
 def test_host_entry_workspace_and_validation_without_gpu():
     L = _lib.lib()
     mats, taus = 8 * 64 * 64 * 4, 8 * 64 * 4
     up = lambda x: (x + 255) // 256 * 256
-    assert L.qrb_host_workspace_bytes(8, 64) == up(mats) + up(taus) + 4 * 8 * 32 * 32 * 4
+    assert L.qrb_host_workspace_bytes(8, 64) == up(mats) + up(taus) + 8 * 8 * 32 * 32 * 4
     assert L.qrb_host_workspace_bytes(4096, 32) == up(4096 * 32 * 32 * 4) + up(4096 * 32 * 4)
     assert L.qrb_host_workspace_bytes(0, 64) == 0
     assert L.qrb_host_workspace_bytes(4, 8193) == 0
@@ -110,7 +111,7 @@ def test_gram_validation_without_gpu():
     assert L.qrb_gram_f32(FAKE, 0, 80, FAKE, 1, 8193, 80, None) == 2
     # gram + geqrf: null tau, short / missing / misaligned workspace
     assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, None, 2, 64, 80, ws, need, None) == 1
-    assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, FAKE, 2, 64, 80, ws, need // 4 - 1,
+    assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, FAKE, 2, 64, 80, ws, need // 8 - 1,
                                 None) == 3
     assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, FAKE, 2, 64, 80, None, need, None) == 3
     assert L.qrb_gram_geqrf_f32(FAKE, 64 * 80, 80, FAKE, FAKE, 2, 64, 80,
@@ -308,17 +309,18 @@ def test_route_is_a_function_of_batch_n_and_workspace():
     code = L.qrb_route(8, 4096, ws)
     assert code & 0xF == 3 and code & (1 << 8)  # blocked, with the look-ahead
     # the tensor-core update needs the split-reflector part of the workspace
-    # (and, on a machine without a CUDA driver, the TMA encoder: FFMA then);
+    # (and, on a machine without a CUDA driver, the TMA encoder: FFMA then)
     kind = (code >> 4) & 0xF
     assert kind in (0, 3)
     assert (code >> 12) & 0xF == 4
-    la2 = L.qrb_route(8, 2048, L.qrb_workspace_bytes(8, 2048))
-    assert la2 & (1 << 8) if kind == 3 else not la2 & (1 << 8)
-    assert (la2 >> 12) & 0xF == (2 if kind == 3 else 4)
     big = L.qrb_route(64, 4096, L.qrb_workspace_bytes(64, 4096))
-    if kind == 3:  # batch * n^2 > 2^27: two-level blocking, no look-ahead
+    small = L.qrb_route(640, 512, L.qrb_workspace_bytes(640, 512))
+    assert not small & (3 << 8)
+    if kind == 3:  # two-level from n = 1024, with the look-ahead up to batch * n = 2^16
+        assert code & (1 << 9)
         assert big & (1 << 9) and not big & (1 << 8)
-    else:
+    else:  # FFMA: the look-ahead from n = 4096, no two-level blocking
+        assert not code & (1 << 9)
         assert big & (1 << 8) and not big & (1 << 9)
     assert (L.qrb_route(8, 4096, 4 * 8 * 32 * 32 * 4) >> 4) & 0xF == 0
     assert (L.qrb_route(8, 130, L.qrb_workspace_bytes(8, 130)) >> 4) & 0xF == 0

@@ -229,14 +229,14 @@ def test_two_level_tensor_core_route(b, n, groups):
     # factors and their cross block), the 64-reflector update on the tensor
     # cores: FP64 gates, and within 1e-4 of FP64 LAPACK like the one-level route
     A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(17 * n + b))
-    old = _hooks(two_level=1, groups=groups)
+    old = _hooks(two_level=1, lookahead=0, groups=groups)
     try:
         route = api.route(b, n)
         H, tau = api.geqrf(A.to(DEV))
         torch.cuda.synchronize()
     finally:
         _restore(old)
-    assert "tcgen05_tma" in route and "two_level" in route, route
+    assert "tcgen05_tma" in route and "two_level" in route and "lookahead" not in route, route
     assert checker.check(A, H.cpu(), tau.cpu()).passed
     H64, t64 = torch.geqrf(A.double())
     par = checker.parity(H.cpu(), tau.cpu(), H64.float(), t64.float())
@@ -284,4 +284,31 @@ def test_tall_panels_stage_the_narrow_update_in_chunks():
     assert checker.check(A, H, tau).passed
     par = checker.parity(H.cpu(), tau.cpu(), Hf.cpu(), tf.cpu())
     assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 1e-3, par
+    assert _lib.get_config("device_error") == 0
+
+
+@pytest.mark.parametrize("b,n,groups", [(3, 160, 1), (2, 196, 1), (4, 300, 2), (3, 512, 1),
+                                        (8, 640, 4), (2, 1028, 1), (2, 2048, 2)])
+def test_two_level_lookahead_route(b, n, groups):
+    # two-level blocking with the look-ahead: per 64 columns panel 1, the
+    # narrow update of the next 64 columns, panel 2, the narrow update of the
+    # next 32; t64 and the 64-reflector update of the rest on the other
+    # stream. FP64 gates, within 1e-4 of FP64 LAPACK, and the batch groups
+    # leave the bits unchanged
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(29 * n + b))
+    old = _hooks(two_level=1, lookahead=1, groups=groups)
+    try:
+        route = api.route(b, n)
+        H, tau = api.geqrf(A.to(DEV))
+        _lib.set_config("groups", 1)
+        H1, t1 = api.geqrf(A.to(DEV))
+        torch.cuda.synchronize()
+    finally:
+        _restore(old)
+    assert "two_level" in route and "lookahead" in route and "tcgen05_tma" in route, route
+    assert torch.equal(H, H1) and torch.equal(tau, t1)
+    assert checker.check(A, H.cpu(), tau.cpu()).passed
+    H64, t64 = torch.geqrf(A.double())
+    par = checker.parity(H.cpu(), tau.cpu(), H64.float(), t64.float())
+    assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 5e-4, par
     assert _lib.get_config("device_error") == 0
