@@ -9,20 +9,23 @@
 //     slot[m] = sum_{i>j} x_i * a_im,   x = column j
 // which yields, at once, sigma = slot[j] (the norm below the diagonal), the
 // trailing dot products d_k = a_jk + scale * slot[k] (k > j), and the Gram
-// column G[m][j] (m < j) used by the T recurrence. The reduction is a warp
-// reduce-scatter (31 shuffles), a cross-warp sum in shared memory, and for
-// clusters a cross-CTA sum over distributed shared memory. Every warp forms
-// the reflector coefficients itself from the summed slots, so a step costs one
-// block barrier (plus one cluster barrier for clusters); the partial-sum
+// column G[m][j] = v_m(j) + scale * slot[m] (m < j) used by the T recurrence.
+// The reduction is a warp reduce-scatter (31 shuffles), a cross-warp sum in
+// shared memory, and for clusters a push of each CTA's sums into every rank's
+// shared memory (st.async, completing on the receiver's mbarrier; the waits
+// are bounded and a timeout sets the device error flag). Every warp forms the
+// reflector coefficients itself from the summed slots, so a step costs one
+// block barrier (plus one mbarrier wait for clusters); the partial-sum
 // buffers alternate by step parity so no second barrier is needed.
 //
-// The column loop is a runtime loop with a compact body (the register array is
-// indexed only by compile-time constants; the current column is picked with a
-// select tree), which keeps the kernel inside the instruction cache. Reflector
-// scaling is deferred: below the diagonal a finished column keeps its unscaled
-// values x_m during the loop and is multiplied by scale_m = 1/(alpha_m-beta_m)
-// only when the panel is written back; the Gram entries are scaled to match:
-//     G[m][j] = scale_m * (x_m(j) + scale_j * sum_{i>j} x_j(i) x_m(i)).
+// The column loop is a runtime loop with a compact body: the register array
+// is indexed only by compile-time constants, and the current column is always
+// register 0 because every step rotates the columns down by one (the update
+// of column j + q + 1 writes register q) and puts the finished column j, in
+// its final form (reflector v = x / (alpha - beta) below the diagonal, beta
+// on it, R above it), into register 31. After the 32 steps (a panel narrower
+// than 32 runs its zero padding columns as tau = 0 steps) every column is
+// back in its own register.
 //
 // Semantics follow the reference panel kernel (src/qrbench/triton_kernels.py
 // :839-871 reflectors and packing, :873-884 unit-lower V, :886-909 forward
@@ -31,6 +34,7 @@
 
 #include "qrb_common.cuh"
 #include "qrb_tc.cuh"
+#include "qrb_tma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -57,18 +61,19 @@ __device__ __forceinline__ void reduce_scatter32(float (&v)[W], int lane) {
   }
 }
 
-// v[j] for a runtime j in [0, 32): a five-level select tree (31 selects).
-__device__ __forceinline__ float pick32(const float (&v)[W], int j) {
-  float t16[16], t8[8], t4[4], t2[2];
-#pragma unroll
-  for (int q = 0; q < 16; ++q) t16[q] = (j & 16) ? v[q + 16] : v[q];
-#pragma unroll
-  for (int q = 0; q < 8; ++q) t8[q] = (j & 8) ? t16[q + 8] : t16[q];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) t4[q] = (j & 4) ? t8[q + 4] : t8[q];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) t2[q] = (j & 2) ? t4[q + 2] : t4[q];
-  return (j & 1) ? t2[1] : t2[0];
+// Shared-memory address of the same variable in cluster rank q.
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t a, uint32_t q) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(q));
+  return r;
+}
+// Store v into a peer's shared memory; the store completes 4 bytes of
+// transactions on the peer's mbarrier at bar.
+__device__ __forceinline__ void push_f32(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+                   addr),
+               "r"(__float_as_uint(v)), "r"(bar)
+               : "memory");
 }
 
 template <int RPT>
@@ -78,12 +83,17 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
         float* __restrict__ tau_out, int64_t tau_sb, float* __restrict__ T_out,
         int64_t T_sb, int t_ld, float* __restrict__ V_out, float* __restrict__ Vsplit,
         int64_t vs_mat, int64_t vs_plane, int vs_row0, int vs_ld, int vs_zero, int r, int w,
-        int cs, int vec_src, int vec_dst) {
+        int cs, int vec_src, int vec_dst, int* __restrict__ err, long long wait_limit) {
   __shared__ float red[2][kMaxThreads / 32][W];  // [parity][warp][slot]
-  __shared__ float xch[2][2][W];                 // [parity][0 = CTA slot sums, 1 = row j]
-  __shared__ __align__(16) float fbuf[kMaxThreads / 32][W];  // per-warp tau_j * d_k
+  __shared__ float rowj[2][W];                   // [parity] row j of the panel (rotated)
+  __shared__ __align__(16) float fbuf[kMaxThreads / 32][W];  // per-warp tau_j * d, shifted
   __shared__ float Gs[W][W + 1];                 // Gram V^T V, strictly upper part
-  __shared__ float taus[W], scales[W], betas[W];
+  __shared__ float taus[W];
+  // cluster exchange: [parity][source rank][slot] CTA slot sums, row j from
+  // rank 0, one mbarrier per parity
+  __shared__ float inbox[2][kMaxCluster][W];
+  __shared__ float rowbox[2][W];
+  __shared__ __align__(8) uint64_t xbar[2];
 
   const int nt = blockDim.x;
   const int tid = threadIdx.x;
@@ -96,10 +106,11 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
   const int row0 = rank * nt * RPT;
 
   for (int e = tid; e < W * (W + 1); e += nt) (&Gs[0][0])[e] = 0.f;
-  if (tid < W) {
-    taus[tid] = 0.f;
-    scales[tid] = 0.f;
-    betas[tid] = 0.f;
+  if (tid < W) taus[tid] = 0.f;
+  if (cs > 1 && tid == 0) {
+    tma::mbar_init(tma::smem_addr(&xbar[0]), 1);
+    tma::mbar_init(tma::smem_addr(&xbar[1]), 1);
+    tma::mbar_fence_init();
   }
 
   float a[RPT][W];
@@ -124,27 +135,42 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
       for (int c = 0; c < W; ++c) a[p][c] = (i < r && c < w) ? __ldg(rowp + c) : 0.f;
     }
   }
-  __syncthreads();
+  if (cs > 1)
+    cg::this_cluster().sync();  // the peers' mbarriers are initialised
+  else
+    __syncthreads();
 
+  const uint32_t in_mine = tma::smem_addr(&inbox[0][rank][lane]);
+  const uint32_t row_mine = tma::smem_addr(&rowbox[0][lane]);
+  const uint32_t bar_mine = tma::smem_addr(&xbar[0]);
+  constexpr uint32_t kParIn = kMaxCluster * W * 4, kParRow = W * 4, kParBar = 8;
+  bool dead = false;  // a bounded wait of this thread ran out
+
+  // Column j is always register 0: each step rotates the columns down by one
+  // and puts the finished column, in its final form (reflector below the
+  // diagonal, beta on it, R above), into register 31; after 32 steps every
+  // column is back in its own register. Padding columns (w < 32) are zero and
+  // take tau = 0 steps.
 #pragma unroll 1
-  for (int j = 0; j < w; ++j) {  // uniform across the cluster
+  for (int j = 0; j < W; ++j) {  // uniform across the cluster
     const int par = j & 1;
 
-    // Phase A: slot partials over this thread's rows below j.
+    // Phase A: slot partials over this thread's rows below j (slot q =
+    // rotated column q: trailing columns j + q for q < 32 - j, finished
+    // columns q + j - 32 above).
     float x[RPT];
     float sl[W];
 #pragma unroll
     for (int q = 0; q < W; ++q) sl[q] = 0.f;
 #pragma unroll
     for (int p = 0; p < RPT; ++p) {
-      const float xj = pick32(a[p], j);
-      x[p] = xj;
-      const float xm = rowi[p] > j ? xj : 0.f;
+      x[p] = a[p][0];
+      const float xm = rowi[p] > j ? x[p] : 0.f;
 #pragma unroll
       for (int q = 0; q < W; ++q) sl[q] = fmaf(xm, a[p][q], sl[q]);
       if (rowi[p] == j) {
 #pragma unroll
-        for (int q = 0; q < W; ++q) xch[par][1][q] = a[p][q];
+        for (int q = 0; q < W; ++q) rowj[par][q] = a[p][q];
       }
     }
     reduce_scatter32(sl, lane);
@@ -153,67 +179,81 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
 
     float tot = 0.f, rowv;
     if (cs > 1) {
+      // warp 0 pushes this CTA's sums (and rank 0 row j) to every rank; every
+      // rank waits for all of them on its own mbarrier
+      const uint32_t bar = bar_mine + par * kParBar;
       if (warp == 0) {
-        for (int w2 = 0; w2 < nwarps; ++w2) tot += red[par][w2][lane];
-        xch[par][0][lane] = tot;
+        float ct = 0.f;
+        for (int w2 = 0; w2 < nwarps; ++w2) ct += red[par][w2][lane];
+        const float rv = rowj[par][lane];
+        for (int q = 0; q < cs; ++q) {
+          const uint32_t rb = mapa_rank(bar, (uint32_t)q);
+          push_f32(mapa_rank(in_mine + par * kParIn, (uint32_t)q), ct, rb);
+          if (rank == 0) push_f32(mapa_rank(row_mine + par * kParRow, (uint32_t)q), rv, rb);
+        }
+        if (lane == 0) tma::mbar_expect_tx(bar, (uint32_t)((cs + 1) * W * 4));
       }
-      cg::cluster_group cl = cg::this_cluster();
-      cl.sync();
-      tot = 0.f;
-      for (int q = 0; q < cs; ++q) tot += cl.map_shared_rank(&xch[par][0][0], q)[lane];
-      rowv = cl.map_shared_rank(&xch[par][1][0], 0)[lane];
+      if (!dead && !tma::mbar_wait_bounded(bar, (uint32_t)((j >> 1) & 1), wait_limit)) {
+        dead = true;
+        atomicExch(err, 1);
+      }
+      for (int q = 0; q < cs; ++q) tot += inbox[par][q][lane];
+      rowv = rowbox[par][lane];
     } else {
       for (int w2 = 0; w2 < nwarps; ++w2) tot += red[par][w2][lane];
-      rowv = xch[par][1][lane];
+      rowv = rowj[par][lane];
     }
 
-    // Every warp forms the reflector from the summed slots (lane = column).
-    const float sigma = __shfl_sync(kFull, tot, j);
-    const float alpha = __shfl_sync(kFull, rowv, j);
+    // Every warp forms the reflector from the summed slots (lane = rotated
+    // column): lane 0 is column j.
+    const float sigma = __shfl_sync(kFull, tot, 0);
+    const float alpha = __shfl_sync(kFull, rowv, 0);
     const Reflector h = make_reflector(alpha, sigma);
-    const float d = fmaf(h.scale, tot, rowv);
-    fbuf[warp][lane] = lane > j ? h.tau * d : 0.f;
+    const float d = fmaf(h.scale, tot, rowv);  // v_j^T (rotated column lane)
+    const int live = W - j;                    // lanes 1 .. live - 1: trailing columns
+    fbuf[warp][(lane + W - 1) & (W - 1)] = (lane >= 1 && lane < live) ? h.tau * d : 0.f;
     if (warp == 0) {
-      if (lane < j) Gs[lane][j] = scales[lane] * d;
-      if (lane == 0) {
-        taus[j] = h.tau;
-        scales[j] = h.scale;
-        betas[j] = h.beta;
-      }
+      if (lane >= live) Gs[lane - live][j] = d;  // finished column lane - live: v^T v_j
+      if (lane == 0) taus[j] = h.tau;
     }
     __syncwarp();
 
-    // Phase B: apply H_j to this thread's rows of the trailing columns
-    // (f_k = 0 for k <= j leaves the finished columns untouched).
-    float vrow[RPT];
+    // Phase B: apply H_j to this thread's rows of the trailing columns while
+    // rotating: register q takes rotated column q + 1 (f = 0 for finished
+    // columns), register 31 the finished column j.
+    float vrow[RPT], fin[RPT];
 #pragma unroll
-    for (int p = 0; p < RPT; ++p)
-      vrow[p] = rowi[p] > j ? h.scale * x[p] : (rowi[p] == j ? 1.f : 0.f);
+    for (int p = 0; p < RPT; ++p) {
+      const bool below = rowi[p] > j;
+      vrow[p] = below ? h.scale * x[p] : (rowi[p] == j ? 1.f : 0.f);
+      fin[p] = below ? vrow[p] : (rowi[p] == j ? h.beta : x[p]);
+    }
 #pragma unroll
     for (int k4 = 0; k4 < W / 4; ++k4) {
       const float4 f4 = reinterpret_cast<const float4*>(fbuf[warp])[k4];
+      const float fk[4] = {f4.x, f4.y, f4.z, f4.w};
 #pragma unroll
-      for (int p = 0; p < RPT; ++p) {
-        a[p][4 * k4 + 0] = fmaf(-f4.x, vrow[p], a[p][4 * k4 + 0]);
-        a[p][4 * k4 + 1] = fmaf(-f4.y, vrow[p], a[p][4 * k4 + 1]);
-        a[p][4 * k4 + 2] = fmaf(-f4.z, vrow[p], a[p][4 * k4 + 2]);
-        a[p][4 * k4 + 3] = fmaf(-f4.w, vrow[p], a[p][4 * k4 + 3]);
+      for (int e = 0; e < 4; ++e) {
+        const int q = 4 * k4 + e;
+        if (q < W - 1) {
+#pragma unroll
+          for (int p = 0; p < RPT; ++p) a[p][q] = fmaf(-fk[e], vrow[p], a[p][q + 1]);
+        }
       }
     }
+#pragma unroll
+    for (int p = 0; p < RPT; ++p) a[p][W - 1] = fin[p];
     __syncwarp();  // fbuf is rewritten next step
   }
-  __syncthreads();  // scales / betas / Gs from warp 0 visible to all
+  __syncthreads();  // taus / Gs from warp 0 visible to all
 
-  // Write the factored panel rows back: R above the diagonal, beta on it,
-  // v = scale * x below it.
+  // Write the factored panel rows back (R above the diagonal, beta on it, v
+  // below it: the registers hold the final values).
   float* __restrict__ D = dst + m * sb_dst;
 #pragma unroll
   for (int p = 0; p < RPT; ++p) {
     const int i = rowi[p];
     if (i >= r) continue;
-#pragma unroll
-    for (int c = 0; c < W; ++c)
-      a[p][c] = i > c ? scales[c] * a[p][c] : (i == c ? betas[c] : a[p][c]);
     const float (&o)[W] = a[p];
     float* rowp = D + (int64_t)i * ld_dst;
     if (vec_dst) {
@@ -283,7 +323,7 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
       }
     }
   }
-  if (cs > 1) cg::this_cluster().sync();  // peers may still read our xch
+  if (cs > 1) cg::this_cluster().sync();  // every push into this CTA has landed
 }
 
 template <int RPT>
@@ -309,10 +349,14 @@ int launch_panel_rpt(const float* src, int64_t sb_src, int64_t ld_src,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = cs > 1 ? 1 : 0;
+  static int* err_ptr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;
+  if (err_ptr[dev] == nullptr && device_error_ptr(&err_ptr[dev]) != QRB_OK) return QRB_ERR_DEVICE;
   const cudaError_t e = cudaLaunchKernelEx(
       &cfg, k_panel<RPT>, src, sb_src, ld_src, dst, sb_dst, ld_dst, tau_out,
       tau_sb, T_out, T_sb, t_ld, V_out, Vsplit, vs_mat, vs_plane, vs_row0, vs_ld, vs_zero, r, w,
-      cs, (int)vec_src, (int)vec_dst);
+      cs, (int)vec_src, (int)vec_dst, err_ptr[dev], device_wait_limit());
   note_launches(1);
   return e == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
 }

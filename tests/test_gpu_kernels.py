@@ -261,8 +261,11 @@ def test_fused_cta_kernel_mid_n(n, b):
         torch.cuda.synchronize()
     finally:
         _lib.set_config("mid_fused", old)
+    # both routes against FP64 at the parity bar; with each other (two FP32
+    # algorithms, every matrix of the batch) H within 1e-4, tau within 2e-4
+    assert checker.parity(Hb[:k].cpu(), tb[:k].cpu(), Ho, to).ok(RTOL), n
     assert _rel(H, Hb.cpu().numpy()) < RTOL
-    assert (tau - tb).abs().max() < RTOL
+    assert (tau - tb).abs().max() < 2 * RTOL
 
 
 def test_fused_cta_kernel_in_place_and_strided():
