@@ -19,6 +19,7 @@ std::atomic<int64_t> g_groups{0};  // 0 = automatic
 std::atomic<int64_t> g_host_direct{3};
 std::atomic<int64_t> g_direct_blocks{0};
 std::atomic<int64_t> g_host_ramp{0};
+std::atomic<int64_t> g_host_groups{8};  // pieces of the host pipeline's blocked route
 std::atomic<int64_t> g_fused_cpl{0};
 std::atomic<int64_t> g_mid_fused{1};
 std::atomic<int64_t> g_lookahead{2};  // 0 off, 1 on, 2 from kLookaheadMinN
@@ -364,7 +365,7 @@ int blocked_qr2_lookahead(float* H, float* tau, float* T64a, float* T64b, int64_
 
 // Internal streams for batch groups, created once per device and kept for the
 // life of the process (streams and events, no device memory).
-constexpr int kMaxGroups = 4;
+constexpr int kMaxGroups = 8;
 struct SideStreams {
   std::mutex mu;
   cudaStream_t s[kMaxGroups] = {};
@@ -418,6 +419,7 @@ namespace qrb {
 bool take_injected_failure_any() { return take_injected_failure(); }
 int host_direct_mode() { return (int)g_host_direct.load(); }
 bool host_ramp() { return g_host_ramp.load() != 0; }
+int host_groups() { return (int)g_host_groups.load(); }
 int fused_cpl() { return (int)g_fused_cpl.load(); }
 bool mid_fused_enabled() { return g_mid_fused.load() != 0; }
 bool mid_fused_always() { return g_mid_fused.load() == 2; }
@@ -533,14 +535,20 @@ int route_code(const Plan& p) {
 // split into batch groups on internal streams, with the panel look-ahead or
 // two-level blocking where selected and the workspace holds their factors).
 int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float* H, float* tau,
-                  const FactorScratch& ws, int64_t batch, int n, cudaStream_t s) {
+                  const FactorScratch& ws, int64_t batch, int n, cudaStream_t s,
+                  GroupHooks* hooks) {
   const Plan plan = make_plan(batch, n, ws);
   if (plan.route == kRouteFusedWarp)
     return launch_fused_small(A, strideA_b, strideA_row, H, tau, batch, n, s);
   if (plan.route == kRouteFusedCta)
     return launch_fused_mid(A, strideA_b, strideA_row, H, tau, batch, n, s);
   if (plan.route != kRouteBlocked) return QRB_ERR_WORKSPACE;
-  const int groups = plan.groups;
+  if (hooks != nullptr && A != H) return QRB_ERR_INVALID_ARG;
+  int groups = plan.groups;
+  if (hooks != nullptr && hooks->min_groups > groups) {  // finer pieces (the bits do not change)
+    const int64_t g = hooks->min_groups < batch ? hooks->min_groups : batch;
+    groups = (int)(g < kMaxGroups ? g : kMaxGroups);
+  }
   const bool tl = plan.two_level;
   const bool la = plan.lookahead;
   // Tensor-core route: H must hold A before the first update adds into it in
@@ -577,27 +585,33 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     r.m0 = m0;
     return r;
   };
-  if (groups <= 1 && !la) {
+  if (groups <= 1) {
+    int rc = hooks != nullptr ? hooks->before(0, batch, s) : QRB_OK;
+    if (rc != QRB_OK) return rc;
     const TmaRoute r0 = route_of(0);
-    if (tl)
-      return blocked_qr2(A, strideA_b, strideA_row, H, tau, ws.T64, batch, n, s,
-                         tma ? &r0 : nullptr);
-    return blocked_qr(A, strideA_b, strideA_row, H, tau, ws.T, batch, n, s, tma ? &r0 : nullptr);
+    if (!la) {
+      rc = tl ? blocked_qr2(A, strideA_b, strideA_row, H, tau, ws.T64, batch, n, s,
+                            tma ? &r0 : nullptr)
+              : blocked_qr(A, strideA_b, strideA_row, H, tau, ws.T, batch, n, s,
+                           tma ? &r0 : nullptr);
+    } else {
+      SideStreams* ss = side_streams();
+      if (ss == nullptr) return QRB_ERR_DEVICE;
+      std::lock_guard<std::mutex> lock(ss->mu);
+      cudaStream_t sp = g_panel_priority.load() ? ss->sp[0] : ss->spl[0];
+      rc = tl  // with la: two-level blocking with the look-ahead
+               ? blocked_qr2_lookahead(H, tau, ws.T64, ws.T64b, batch, n, s, sp, ss->evP[0],
+                                       ss->evB[0], ss->joinP[0], r0)
+               : blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, ws.T, ws.T2, batch, n,
+                                      s, sp, ss->evP[0], ss->evB[0], ss->joinP[0],
+                                      tma ? &r0 : nullptr);
+    }
+    if (rc == QRB_OK && hooks != nullptr) rc = hooks->after(0, batch, s);
+    return rc;
   }
   SideStreams* ss = side_streams();
   if (ss == nullptr) return QRB_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(ss->mu);
-  if (groups <= 1) {
-    const TmaRoute r0 = route_of(0);
-    cudaStream_t sp = g_panel_priority.load() ? ss->sp[0] : ss->spl[0];
-    if (tl)  // with la: two-level blocking with the look-ahead
-      return blocked_qr2_lookahead(H, tau, ws.T64, ws.T64b, batch, n, s, sp, ss->evP[0],
-                                   ss->evB[0], ss->joinP[0], r0);
-    return blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, ws.T, ws.T2, batch, n, s,
-                                g_panel_priority.load() ? ss->sp[0] : ss->spl[0], ss->evP[0],
-                                ss->evB[0], ss->joinP[0],
-                                tma ? &r0 : nullptr);
-  }
   // Split the batch into groups that run the same kernel sequence on separate
   // internal streams, forked from and joined back into the caller's stream, so
   // that one group's (latency-bound) panel kernels overlap another group's
@@ -611,6 +625,7 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     if (b1 <= b0) continue;
     cudaStream_t gs = ss->s[g];
     if (cudaStreamWaitEvent(gs, ss->fork, 0) != cudaSuccess) return QRB_ERR_LAUNCH;
+    if (hooks != nullptr && (rc = hooks->before(b0, b1, gs)) != QRB_OK) break;
     const TmaRoute rg = route_of(b0);
     if (tl && la)
       rc = blocked_qr2_lookahead(H + b0 * nn, tau + b0 * n, ws.T64 + b0 * 4 * tper,
@@ -629,6 +644,7 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
     else
       rc = blocked_qr(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
                       ws.T + b0 * tper, b1 - b0, n, gs, tma ? &rg : nullptr);
+    if (rc == QRB_OK && hooks != nullptr) rc = hooks->after(b0, b1, gs);
     if (cudaEventRecord(ss->join[g], gs) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
     if (cudaStreamWaitEvent(s, ss->join[g], 0) != cudaSuccess && rc == QRB_OK) rc = QRB_ERR_LAUNCH;
   }
@@ -707,7 +723,7 @@ int qrb_panel_qr_f32(const float* P, int64_t strideP_b, int64_t strideP_row,
   if (batch == 0 || r == 0 || w == 0) return QRB_OK;
   if (!P || !H || !tau || !T) return QRB_ERR_INVALID_ARG;
   if (w > qrb::kPanelW || r < w) return QRB_ERR_UNSUPPORTED;
-  if (qrb::panel_cluster_size(r) > qrb::kMaxCluster) return QRB_ERR_UNSUPPORTED;
+  if (qrb::panel_cluster_size(r, batch) > qrb::kMaxCluster) return QRB_ERR_UNSUPPORTED;
   if (bad_matrix_strides(strideP_b, strideP_row, r, w, batch)) return QRB_ERR_INVALID_ARG;
   if (take_injected_failure()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -855,6 +871,11 @@ int qrb_set_config(const char* key, int64_t value) {
     g_fused_cpl.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "host_groups") == 0) {
+    if (value < 0 || value > kMaxGroups) return QRB_ERR_INVALID_ARG;
+    g_host_groups.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "host_ramp") == 0) {
     if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
     g_host_ramp.store(value);
@@ -893,6 +914,7 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "groups") == 0) { *value = g_groups.load(); return QRB_OK; }
   if (std::strcmp(key, "host_direct") == 0) { *value = g_host_direct.load(); return QRB_OK; }
   if (std::strcmp(key, "host_ramp") == 0) { *value = g_host_ramp.load(); return QRB_OK; }
+  if (std::strcmp(key, "host_groups") == 0) { *value = g_host_groups.load(); return QRB_OK; }
   if (std::strcmp(key, "fused_cpl") == 0) { *value = g_fused_cpl.load(); return QRB_OK; }
   if (std::strcmp(key, "mid_fused") == 0) { *value = g_mid_fused.load(); return QRB_OK; }
   if (std::strcmp(key, "lookahead") == 0) { *value = g_lookahead.load(); return QRB_OK; }

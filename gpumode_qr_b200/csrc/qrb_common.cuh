@@ -122,9 +122,10 @@ int launch_larfb(const float* V, int64_t sVb, int64_t ldv, const float* T,
                  int64_t batch, int r, int k, int c, bool tc_pass2,
                  cudaStream_t stream);
 
-int panel_cluster_size(int r);
+int panel_cluster_size(int r, int64_t batch);
 // qrb_set_config("panel_rpt"): rows per thread of the panel kernel, 1, 2 or 4
-// (0 = automatic: 1 up to 128 rows, else 4).
+// (0 = automatic: 1 up to 128 rows, else 2 where the batch's panels still fit
+// on the SMs at once, else 4).
 int panel_rpt();
 // qrb_set_config("gram_tile"): S tile of the Gram kernel, 64 or 128 (0 =
 // automatic: 128 above n = 64).
@@ -227,8 +228,23 @@ int route_code(const Plan& p);
 
 // Whole factorization of already validated arguments, enqueued on `stream`
 // (no fault injection, no sync check), the blocked route's factors in ws.
+// Per-group hooks of the blocked route: before(b0, b1, gs) is called before
+// the first kernel of batch group [b0, b1) is enqueued on its stream gs,
+// after(b0, b1, gs) after its last (the whole batch is one group on the
+// caller's stream when the route has no groups). The host-memory entry point
+// uses them to stream each group's copies against the other groups' work.
+struct GroupHooks {
+  int min_groups = 0;  // at least this many groups (capped at the batch and the stream sets)
+  virtual int before(int64_t b0, int64_t b1, cudaStream_t gs) = 0;
+  virtual int after(int64_t b0, int64_t b1, cudaStream_t gs) = 0;
+ protected:
+  ~GroupHooks() = default;
+};
+// hooks (blocked route only) require A == H: the factorization reads nothing
+// a group's hook has not made ready.
 int geqrf_enqueue(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau,
-                  const FactorScratch& ws, int64_t batch, int n, cudaStream_t stream);
+                  const FactorScratch& ws, int64_t batch, int n, cudaStream_t stream,
+                  GroupHooks* hooks = nullptr);
 
 // The public entry points' shared epilogue pieces: consume one injected
 // failure (fail_next), and apply the sync_check mode to a call's status.
@@ -244,6 +260,9 @@ int host_direct_mode();
 // qrb_set_config("host_ramp"): 1 = chunk sizes rise and fall (1, 2, .., 2, 1)
 // so that the pipeline fills and drains on small pieces; 0 = equal chunks.
 bool host_ramp();
+// qrb_set_config("host_groups"): qrb_geqrf_f32_host on the blocked route runs
+// at least this many batch groups (1..8; 0 = the route's own; default 8).
+int host_groups();
 // qrb_set_config("direct_blocks"): grid of the direct kernel (0 = automatic).
 int64_t host_direct_blocks();
 
@@ -252,7 +271,8 @@ int64_t host_direct_blocks();
 int fused_cpl();
 
 // Path taken by the last qrb_geqrf_f32_host call (the host_direct mode that
-// ran: 0..3), -1 none yet (qrb_get_config("host_path")).
+// ran: 0..3, or 4 for the blocked route's groups as pieces), -1 none yet
+// (qrb_get_config("host_path")).
 int64_t host_last_path();
 
 // Count of kernel launches enqueued by this library (all devices, all calls);

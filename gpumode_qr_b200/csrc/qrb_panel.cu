@@ -363,15 +363,38 @@ int launch_panel_rpt(const float* src, int64_t sb_src, int64_t ld_src,
 
 }  // namespace
 
-// Rows per thread: 1 up to 128 rows (one CTA of up to 128 threads), else 4:
-// one CTA of up to 256 threads up to 1024 rows, beyond that a cluster of cs
-// CTAs of 256 threads (cs a power of two, <= 8 for the launch to be accepted).
-// qrb_set_config("panel_rpt") = 1 (CTAs of up to 512 threads) or 2 (up to 256)
-// selects that many rows per thread instead (4 where that would need more than
-// 8 CTAs).
-static void panel_shape(int r, int* rpt, int* cs, int* nt) {
+// Rows per thread: 1 up to 128 rows (one CTA of up to 512 threads); above,
+// 2 when the batch's panels then still fit on the SMs at once (clusters of
+// 256-thread CTAs, 512 rows each: the column steps' latency chain is then
+// shorter), else 4 (256-thread CTAs of 1024 rows: fewer CTAs when there are
+// more than the SMs hold). Beyond 1 CTA, a cluster of cs CTAs (cs a power of
+// two, <= 8 for the launch to be accepted). Measured on B200: 16.0 vs
+// 16.7 ms with 2 rows per thread at 8 x 4096^2, 4.56 vs 4.41 ms at
+// 640 x 512^2 (320 matrices per panel launch). qrb_set_config("panel_rpt") = 1
+// (CTAs of up to 512 threads), 2 or 4 forces that many rows per thread (4
+// where that would need more than 8 CTAs).
+static void panel_shape(int r, int64_t batch, int* rpt, int* cs, int* nt) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+      sms = v;
+    else
+      sms = 148;
+  }
   const int pref = panel_rpt();
-  int R = pref > 0 ? pref : (r > 128 ? 4 : 1);
+  int R = pref;
+  if (R == 0) {
+    if (r <= 128) {
+      R = 1;
+    } else {
+      const int per2 = kPanelCtaThreads * 2;
+      int c2 = 1;
+      while (c2 * per2 < r) c2 <<= 1;
+      R = (c2 <= kMaxCluster && batch * c2 <= sms) ? 2 : 4;
+    }
+  }
   int c = 1;
   for (;;) {
     const int per_cta_max = (R >= 2 ? kPanelCtaThreads : kMaxThreads) * R;
@@ -389,9 +412,9 @@ static void panel_shape(int r, int* rpt, int* cs, int* nt) {
   *nt = threads;
 }
 
-int panel_cluster_size(int r) {
+int panel_cluster_size(int r, int64_t batch) {
   int rpt, cs, nt;
-  panel_shape(r, &rpt, &cs, &nt);
+  panel_shape(r, batch, &rpt, &cs, &nt);
   return cs;
 }
 
@@ -405,7 +428,7 @@ int launch_panel(const float* src, int64_t sb_src, int64_t ld_src, float* dst,
                             vs_ld % 4 != 0 || vs_ld < (vs_zero ? 2 * W : W)))
     return QRB_ERR_UNSUPPORTED;
   int rpt, cs, nt;
-  panel_shape(r, &rpt, &cs, &nt);
+  panel_shape(r, batch, &rpt, &cs, &nt);
   if (cs > kMaxCluster) return QRB_ERR_UNSUPPORTED;
   if (batch * cs > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
   if (rpt == 1)

@@ -145,7 +145,11 @@ QRB_API int qrb_geqrf_f32_noalloc(const float* A, int64_t strideA_b,
  *   workspace device memory of qrb_host_workspace_bytes(batch, n) bytes,
  *             256-byte aligned (staging for A/H and tau, plus the T scratch).
  *   chunks    pipeline depth: the batch is cut into this many pieces
- *             (1..64; 0 = 6 for n <= 64, else 4; capped at batch).
+ *             (1..64, capped at batch; 0 = automatic: 6 pieces for n <= 64,
+ *             4 up to n = 128, and above, where qrb_geqrf_f32 runs its
+ *             blocked route, that route's batch groups: one factorization
+ *             over the whole batch whose groups each start when their own
+ *             matrices have landed and are copied out when done).
  * The pieces run on three internal streams of the current device (copy in,
  * factor, copy out), forked from and joined back into `stream`: synchronise
  * `stream` before reading H_host / tau_host. Page-locked host buffers
@@ -302,7 +306,7 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 highest (1, the default).
  *   "device_error" read: 1 if a kernel's bounded device-side wait timed out
  *                 since the last reset (synchronous); set to 0 to reset.
- *   "groups"      1..4: batches of 4 or more matrices with n > 32 are split
+ *   "groups"      1..8: batches of 4 or more matrices with n > 32 are split
  *                 into this many groups (at most batch / 2) run on internal
  *                 streams (forked from and joined back into the caller's
  *                 stream) so that panel and trailing-update kernels of
@@ -332,8 +336,10 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 n = 4096 and no two-level blocking. Two-level blocking with
  *                 the look-ahead needs the tensor-core update.
  *   "panel_rpt"   rows per thread of the panel kernel: 0 (default) = 1 up to
- *                 128 rows, else 4; 1 or 2 force that many (CTAs of up to 512
- *                 or 256 threads; 4 where more than 8 CTAs would be needed).
+ *                 128 rows, else 2 where the batch's panels (clusters of
+ *                 256-thread CTAs) all fit on the SMs at once, else 4; 1, 2
+ *                 or 4 force that many (CTAs of up to 512 or 256 threads; 4
+ *                 where more than 8 CTAs would be needed).
  *   "mid_fused"   1 (default): 32 < n <= 64 and 96 < n <= 128, and
  *                 64 < n <= 96 up to 592 matrices, are factored by one CTA per
  *                 matrix in one launch;
@@ -341,10 +347,16 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 route above n = 32.
  *   "fused_cpl"   n <= 32 kernel: 2 or 4 matrices per warp, 0 (default) = 4 up
  *                 to 4736 matrices, else 2. Results are identical either way.
+ *   "host_groups" qrb_geqrf_f32_host on the blocked route without the
+ *                 look-ahead (automatic depth) runs at least this many batch
+ *                 groups, at most one per matrix (1..8; 0 = the route's own
+ *                 count; default 8): finer pieces start sooner after their
+ *                 copies; the bits do not change.
  *   "host_ramp"   1: qrb_geqrf_f32_host cuts the batch into pieces of relative
  *                 size 1, 2, .., 2, 1 instead of equal pieces (default 0).
- *   "host_path"   read: the host_direct mode the last qrb_geqrf_f32_host call
- *                 ran (0..3; -1 before the first call).
+ *   "host_path"   read: the path the last qrb_geqrf_f32_host call ran: the
+ *                 host_direct mode 0..3, or 4 = the blocked route's batch
+ *                 groups as pieces (-1 before the first call).
  *   "launches"    number of kernel launches this library has enqueued since
  *                 load or since the last qrb_set_config("launches", 0).
  * Returns QRB_ERR_INVALID_ARG for an unknown key or value.

@@ -207,6 +207,12 @@ def test_config_keys():
         _lib.set_config("test_skip_mma", 2)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("wait_probe", 10)
+    assert _lib.get_config("host_groups") == 8
+    _lib.set_config("host_groups", 0)
+    assert _lib.get_config("host_groups") == 0
+    _lib.set_config("host_groups", 8)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("host_groups", 9)
     assert _lib.get_config("tma_ctas") == 0
     _lib.set_config("tma_ctas", 96)
     assert _lib.get_config("tma_ctas") == 96
@@ -239,7 +245,7 @@ def test_config_keys():
     assert _lib.get_config("groups") == 3
     _lib.set_config("groups", 0)
     with pytest.raises(_lib.QRBError):
-        _lib.set_config("groups", 5)
+        _lib.set_config("groups", 9)
     assert _lib.get_config("lookahead") == 2
     _lib.set_config("lookahead", 1)
     assert _lib.get_config("lookahead") == 1
@@ -284,7 +290,7 @@ def test_config_keys():
     _lib.set_config("direct_blocks", 0)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("direct_blocks", -1)
-    assert _lib.get_config("host_path") in (-1, 0, 1, 2, 3)
+    assert _lib.get_config("host_path") in (-1, 0, 1, 2, 3, 4)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("host_path", 1)  # read-only
     with pytest.raises(_lib.QRBError):

@@ -219,16 +219,26 @@ def test_error_paths_raise():
 
 
 @pytest.mark.parametrize("b,n,chunks", [(10, 48, 3), (4096, 32, 0), (7, 100, 64), (5, 33, 1),
-                                         (600, 64, 0), (3, 256, 2)])
+                                         (600, 64, 0), (3, 256, 2), (8, 512, 0), (3, 1024, 0),
+                                         (8, 1024, 0), (6, 130, 0), (5, 2048, 0)])
 def test_host_buffer_api_matches_device_api(b, n, chunks):
+    # the blocked route with the automatic depth streams its batch groups
+    # (host path 4): each group's copy gates only that group's kernels
     A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(b * 1000 + n))
     Ah = A.pin_memory()
-    Hh = torch.empty_like(Ah).pin_memory()
-    th = torch.empty(b, n).pin_memory()
-    api.geqrf_host(Ah, Hh, th, device=DEV, chunks=chunks)
-    torch.cuda.synchronize()
     H, tau = _gpu_qr(A)
-    assert torch.equal(Hh, H) and torch.equal(th, tau)
+    for host_groups in ((8, 0, 3) if n > 128 and chunks == 0 else (8,)):
+        _lib.set_config("host_groups", host_groups)
+        try:
+            Hh = torch.empty_like(Ah).pin_memory()
+            th = torch.empty(b, n).pin_memory()
+            api.geqrf_host(Ah, Hh, th, device=DEV, chunks=chunks)
+            torch.cuda.synchronize()
+        finally:
+            _lib.set_config("host_groups", 8)
+        if n > 128 and chunks == 0:
+            assert _lib.get_config("host_path") == 4
+        assert torch.equal(Hh, H) and torch.equal(th, tau), host_groups
 
 
 @pytest.mark.parametrize("b,n", [(4096, 32), (9, 17), (1, 1), (3, 32)])
