@@ -23,7 +23,9 @@
 //              T = [[T1, X], [0, T2]] (LARFT of the combined block; the
 //              reference's forward recurrence gives the same matrix,
 //              src/qrbench/triton_kernels.py:886-909). The Gram block V1^T V2
-//              is split by rows over a cluster of up to 8 CTAs.
+//              is split by rows over a cluster of up to 8 CTAs (about 256
+//              rows each), staged in 128-row chunks by double-buffered
+//              cp.async.
 // V is read through its strictly lower part: the diagonal is 1, everything
 // above it 0 (so V points into a packed H; panel 2's first 32 rows, which hold
 // R entries, read as 0).
@@ -278,13 +280,15 @@ k_larfb64(const float* __restrict__ V, int64_t sVb, int64_t ldv, const float* __
 // the lower-left block. The Gram block G = V1^T V2 is split over a cluster of
 // cs CTAs by rows (each CTA a contiguous slice of rows_per rows); rank 0 sums
 // the slices through distributed shared memory and forms X.
+constexpr int T64_CH = 128;  // rows per staged chunk of k_t64
+constexpr size_t T64_SMEM = 2 * (size_t)T64_CH * K * sizeof(float);  // double buffer
+
 __global__ void __launch_bounds__(NT)
 k_t64(const float* __restrict__ V, int64_t sVb, int64_t ldv, float* __restrict__ T,
       int64_t sTb, int r, int cs, int rows_per) {
   constexpr int W = 32;
   constexpr int NG = NT / W;  // 8 row groups
-  constexpr int RCH = 32;
-  __shared__ __align__(16) float Vs[RCH][K];
+  extern __shared__ __align__(16) float vbuf[];  // [2][T64_CH][K]
   __shared__ float red[NG / 2][W][W + 1];
   __shared__ float Gs[W][W + 1];
   __shared__ float t1[W][W + 1], t2[W][W + 1], y[W][W + 1];
@@ -307,36 +311,56 @@ k_t64(const float* __restrict__ V, int64_t sVb, int64_t ldv, float* __restrict__
   int lo = rank * rows_per;
   const int hi = min(r, lo + rows_per);
   if (lo < W) lo = W;
+  const int nchunk = hi > lo ? (hi - lo + T64_CH - 1) / T64_CH : 0;
+  // stage chunk c (rows lo + c * T64_CH ..) into buffer c & 1: 16-byte cp.async,
+  // all of a chunk's requests in flight, the next chunk loading while this
+  // one is multiplied
+  auto stage = [&](int c) {
+    float* dst = vbuf + (size_t)(c & 1) * T64_CH * K;
+    const int i0 = lo + c * T64_CH;
+    const int nr = min(T64_CH, hi - i0);
+    for (int e = tid; e < nr * (K / 4); e += NT) {
+      const int row = e >> 4, c4 = (e & 15) << 2;
+      cp_async16(dst + row * K + c4, Vm + (int64_t)(i0 + row) * ldv + c4, true);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
   float acc[W];
 #pragma unroll
   for (int b = 0; b < W; ++b) acc[b] = 0.f;
-  for (int i0 = lo; i0 < hi; i0 += RCH) {
-    __syncthreads();
-#pragma unroll
-    for (int e = 0; e < (RCH * K) / (4 * NT); ++e) {
-      const int idx = tid + e * NT;
-      const int row = idx >> 4, c4 = (idx & 15) << 2;
-      const int i = i0 + row;
-      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (i < hi) t = __ldg(reinterpret_cast<const float4*>(Vm + (int64_t)i * ldv + c4));
-      Vs[row][c4 + 0] = vmask(t.x, i, c4 + 0);
-      Vs[row][c4 + 1] = vmask(t.y, i, c4 + 1);
-      Vs[row][c4 + 2] = vmask(t.z, i, c4 + 2);
-      Vs[row][c4 + 3] = vmask(t.w, i, c4 + 3);
+  if (nchunk > 0) stage(0);
+  for (int c = 0; c < nchunk; ++c) {
+    if (c + 1 < nchunk) {
+      stage(c + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-#pragma unroll
-    for (int row = g; row < RCH; row += NG) {
-      const float xa = Vs[row][a];
+    float* Vs = vbuf + (size_t)(c & 1) * T64_CH * K;
+    const int i0 = lo + c * T64_CH;
+    const int nr = min(T64_CH, hi - i0);
+    if (i0 < K) {  // panel 2's diagonal block: unit diagonal, zero above it
+      for (int e = tid; e < nr * W; e += NT) {
+        const int row = e >> 5, b = e & (W - 1);
+        const int i = i0 + row;
+        if (i < K) Vs[row * K + W + b] = vmask(Vs[row * K + W + b], i, W + b);
+      }
+      __syncthreads();
+    }
+#pragma unroll 4
+    for (int row = g; row < nr; row += NG) {
+      const float xa = Vs[row * K + a];
 #pragma unroll
       for (int b4 = 0; b4 < W / 4; ++b4) {
-        const float4 xb = *reinterpret_cast<const float4*>(&Vs[row][W + 4 * b4]);
+        const float4 xb = *reinterpret_cast<const float4*>(&Vs[row * K + W + 4 * b4]);
         acc[4 * b4 + 0] = fmaf(xa, xb.x, acc[4 * b4 + 0]);
         acc[4 * b4 + 1] = fmaf(xa, xb.y, acc[4 * b4 + 1]);
         acc[4 * b4 + 2] = fmaf(xa, xb.z, acc[4 * b4 + 2]);
         acc[4 * b4 + 3] = fmaf(xa, xb.w, acc[4 * b4 + 3]);
       }
     }
+    __syncthreads();  // the buffer is restaged two chunks on
   }
   // tree-sum the 8 row groups: 4..7 -> 0..3, 2..3 -> 0..1, 1 -> 0
 #pragma unroll
@@ -431,12 +455,26 @@ int launch_larfb64(const float* V, int64_t sVb, int64_t ldv, const float* T, int
 int launch_t64(const float* V, int64_t sVb, int64_t ldv, float* T64, int64_t sT64b,
                int64_t batch, int r, cudaStream_t stream) {
   if (r <= K) return QRB_ERR_UNSUPPORTED;
-  const int cs = r <= 1024 ? 1 : r <= 2048 ? 2 : r <= 4096 ? 4 : 8;
+  if (ldv % 4 != 0 || sVb % 4 != 0 || (reinterpret_cast<uintptr_t>(V) & 15) != 0)
+    return QRB_ERR_UNSUPPORTED;
+  // about 256 rows per cluster rank (up to 8 ranks)
+  int cs = (r + 255) / 256;
+  if (cs > kMaxCluster) cs = kMaxCluster;
   if (batch * cs > 0x7fffffffLL) return QRB_ERR_UNSUPPORTED;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(k_t64, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)T64_SMEM) != cudaSuccess)
+      return QRB_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
   const int rows_per = ((r + cs - 1) / cs + 31) / 32 * 32;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(batch * cs), 1, 1);
   cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = T64_SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
