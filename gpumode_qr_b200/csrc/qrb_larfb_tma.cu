@@ -333,15 +333,17 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
           tc::fence_after();
           const uint32_t st = base + (uint32_t)s * L::ST1;
           const uint32_t d1 = tmem + (uint32_t)KR * (uint32_t)(ch % NP1);
+          // the k-step's operands are 1024 bytes further on: add to the
+          // descriptors' address field (units of 16 bytes; no carry)
+          const uint64_t ah0 = sdesc_mn32(st, BOX1), al0 = sdesc_mn32(st + L::S1_CL, BOX1);
+          const uint64_t bh0 = sdesc_mn32(st + L::S1_VH, BOX1);
+          const uint64_t bl0 = sdesc_mn32(st + L::S1_VL, BOX1);
 #pragma unroll
           for (int ks = 0; ks < R1 / 8; ++ks) {
-            const uint64_t ah = sdesc_mn32(st + ks * 1024, BOX1);
-            const uint64_t al = sdesc_mn32(st + L::S1_CL + ks * 1024, BOX1);
-            const uint64_t bh = sdesc_mn32(st + L::S1_VH + ks * 1024, BOX1);
-            const uint64_t bl = sdesc_mn32(st + L::S1_VL + ks * 1024, BOX1);
-            tc::mma_tf32(d1, ah, bh, L::IDESC1, (ch >= NP1 || ks != 0) ? 1u : 0u);
-            tc::mma_tf32(d1, ah, bl, L::IDESC1, 1u);
-            tc::mma_tf32(d1, al, bh, L::IDESC1, 1u);
+            const uint64_t dk = (uint64_t)(ks * (1024 >> 4));
+            tc::mma_tf32(d1, ah0 + dk, bh0 + dk, L::IDESC1, (ch >= NP1 || ks != 0) ? 1u : 0u);
+            tc::mma_tf32(d1, ah0 + dk, bl0 + dk, L::IDESC1, 1u);
+            tc::mma_tf32(d1, al0 + dk, bh0 + dk, L::IDESC1, 1u);
           }
           tc::mma_commit(BAR(B_EMPTY1 + s));
         }
@@ -361,16 +363,17 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
           tc::fence_after();
           const uint32_t va = base + (uint32_t)v * L::V2ST;
           const uint32_t d = tmem + TM_D2 + 128u * (uint32_t)ab;
+          const uint64_t ah0 = sdesc_kmajor(va), al0 = sdesc_kmajor(va + NA * BOX2);
+          const uint64_t bh0 = sdesc_kmajor(base + L::OFF_BH);
+          const uint64_t bl0 = sdesc_kmajor(base + L::OFF_BL);
 #pragma unroll
           for (int ks = 0; ks < KR / 8; ++ks) {
             const uint32_t ka = (uint32_t)(ks >> 2), ko = 32u * (uint32_t)(ks & 3);
-            const uint64_t ah = sdesc_kmajor(va + ka * BOX2 + ko);
-            const uint64_t al = sdesc_kmajor(va + (NA + ka) * BOX2 + ko);
-            const uint64_t bh = sdesc_kmajor(base + L::OFF_BH + ka * TCOLS * 128 + ko);
-            const uint64_t bl = sdesc_kmajor(base + L::OFF_BL + ka * TCOLS * 128 + ko);
-            tc::mma_tf32(d, ah, bh, IDESC2, ks != 0 ? 1u : 0u);
-            tc::mma_tf32(d, ah, bl, IDESC2, 1u);
-            tc::mma_tf32(d, al, bh, IDESC2, 1u);
+            const uint64_t da = (uint64_t)((ka * BOX2 + ko) >> 4);
+            const uint64_t db = (uint64_t)((ka * TCOLS * 128 + ko) >> 4);
+            tc::mma_tf32(d, ah0 + da, bh0 + db, IDESC2, ks != 0 ? 1u : 0u);
+            tc::mma_tf32(d, ah0 + da, bl0 + db, IDESC2, 1u);
+            tc::mma_tf32(d, al0 + da, bh0 + db, IDESC2, 1u);
           }
           tc::mma_commit(BAR(B_V2EMPTY + v));
           tc::mma_commit(BAR(B_ACCFULL + ab));
@@ -393,9 +396,11 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
       const int ml = t / ntc, m = m0 + ml;
       const int tc0 = col0 + (t % ntc) * TCOLS;
       const int nbox = min(4, (col_end - tc0 + 31) / 32);
-      const float* Tm = T + (int64_t)ml * sTb;
-      for (int e = wt; e < KR * KR; e += 32 * NWORK)
-        Ts[(e / KR) * L::T_LD + (e % KR)] = __ldg(Tm + e);
+      if (it == 0) {  // later tiles' T is prefetched during the previous tile's pass 2
+        const float* Tm = T + (int64_t)ml * sTb;
+        for (int e = wt; e < KR * KR; e += 32 * NWORK)
+          Ts[(e / KR) * L::T_LD + (e % KR)] = __ldg(Tm + e);
+      }
       workers_sync_or(false);  // T in shared memory for the W' step below
 
       // ---- pass 1: split each chunk's C boxes into hi (in place) and lo ----
@@ -477,6 +482,17 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         if (lane == 0) tma::mbar_arrive(BAR(B_B2READY));
       }
 
+      // the next tile's T, into registers now and into Ts once every worker
+      // is past this tile's W' step (the first pass-2 barrier below)
+      constexpr int TPT = KR * KR / (32 * NWORK);
+      float tnext[TPT];
+      const int tn = t + (int)gridDim.x;
+      if (tn < ntiles) {
+        const float* Tn = T + (int64_t)(tn / ntc) * sTb;
+#pragma unroll
+        for (int k = 0; k < TPT; ++k) tnext[k] = __ldg(Tn + wt + k * 32 * NWORK);
+      }
+
       // ---- pass 2 epilogues: C += -(V W') by TMA reduce-add ----
       for (int p = 0; p < nch2; ++p, ++g2) {
         const int ab = g2 & 1, ua = g2 >> 1;
@@ -498,6 +514,13 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         }
         if (issuer) tma::bulk_wait_read_all();  // the previous reduce has read the staging tile
         if (workers_sync_or(sk || *s_abort != 0)) continue;
+        if (p == 0 && tn < ntiles) {
+#pragma unroll
+          for (int k = 0; k < TPT; ++k) {
+            const int e = wt + k * 32 * NWORK;
+            Ts[(e / KR) * L::T_LD + (e % KR)] = tnext[k];
+          }
+        }
 #pragma unroll
         for (int uu = 0; uu < 8; ++uu) {
           *reinterpret_cast<float4*>(sm + L::OFF_STG + (2 * h) * BOX2 + sw128(row, uu)) =
