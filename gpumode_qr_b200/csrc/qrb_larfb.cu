@@ -75,7 +75,8 @@ struct __align__(1024) SmemTc {
   unsigned char B[2][B2T_BYTES];            // [hi, lo]
   float Ws[K * WS_LD];
   float Ts[K * T_LD];
-  uint64_t bar[2];
+  uint64_t bar[3];                          // [0,1] accumulators, [2] drain after an abort
+  int abort;
   uint32_t tmem;
 };
 
@@ -131,6 +132,7 @@ __device__ __forceinline__ void pass2_tc(SmemTc& sm, const float* __restrict__ V
   const uint32_t tmem = sm.tmem;
   uint32_t ph[2] = {0u, 0u};
   const uint32_t bar0 = tc::smem_u32(&sm.bar[0]);
+  volatile int* abort = &sm.abort;
   const int nch = (r + R2T - 1) / R2T;
 
   // The previous chunk's C rows are loaded before waiting for its MMAs, and
@@ -146,8 +148,9 @@ __device__ __forceinline__ void pass2_tc(SmemTc& sm, const float* __restrict__ V
     for (int j4 = 0; j4 < 8; ++j4)
       cv[j4] = (row_ok && c0 + 32 * h + 4 * j4 < c) ? *reinterpret_cast<const float4*>(src + 4 * j4)
                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-    tc::mbar_wait(bar0 + 8 * s, ph[s], err);
+    tc::mbar_wait(bar0 + 8 * s, ph[s], err, abort);
     ph[s] ^= 1u;
+    if (__any_sync(tc::kFullMask, *abort != 0)) return;  // no TMEM reads, no stores
     tc::fence_after();
     float d[32];
     tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + s * TC + 32 * h, d);
@@ -202,7 +205,7 @@ __device__ __forceinline__ void pass2_tc(SmemTc& sm, const float* __restrict__ V
     tc::fence_async_smem();
     tc::fence_before();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 && *abort == 0) {
       tc::fence_after();
       const uint32_t a_hi = tc::smem_u32(sm.u.A[s][0]), a_lo = tc::smem_u32(sm.u.A[s][1]);
       const uint32_t b_hi = tc::smem_u32(sm.B[0]), b_lo = tc::smem_u32(sm.B[1]);
@@ -223,6 +226,8 @@ __device__ __forceinline__ void pass2_tc(SmemTc& sm, const float* __restrict__ V
     if (ch >= 1) epilogue(ch - 1);
   }
   epilogue(nch - 1);
+  __syncthreads();
+  if (tid == 0 && *abort != 0) tc::drain_mmas(bar0 + 8 * 2);
   __syncthreads();
   tc::fence_after();
   if (warp == 0)
@@ -265,11 +270,12 @@ k_larfb(const float* __restrict__ V, int64_t sVb, int64_t ldv,
       asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-      for (int b = 0; b < 2; ++b)
+      for (int b = 0; b < 3; ++b)
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc::smem_u32(&sm.bar[b])),
                      "r"(1)
                      : "memory");
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      sm.abort = 0;
     }
   }
 

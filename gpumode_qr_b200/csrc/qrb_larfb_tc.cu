@@ -81,7 +81,9 @@ k_larfb_tc(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   float* __restrict__ Dm = Cdst + m * sCdb;
 
   float* Ts = reinterpret_cast<float*>(smem + OFF_T);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // [0,1] G1, [2,3] G2
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // [0,1] G1, [2,3] G2, [4] drain
+  __shared__ int s_abort_word;
+  volatile int* s_abort = &s_abort_word;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 64);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = smem_u32(bars);
@@ -95,9 +97,10 @@ k_larfb_tc(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   }
   if (tid == 0) {
 #pragma unroll
-    for (int b = 0; b < 4; ++b)
+    for (int b = 0; b < 5; ++b)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar0 + 8 * b), "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    *s_abort = 0;
   }
   for (int e = tid; e < KR * KR; e += NT) {
     const int q = e / KR, k = e % KR;
@@ -114,7 +117,7 @@ k_larfb_tc(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   for (int ch = 0; ch < nch1; ++ch) {
     const int s = ch & 1;
     if (ch >= 2) {  // the MMAs of chunk ch-2 have finished reading buffer s
-      mbar_wait(bar0 + 8 * s, ph[s], err);
+      mbar_wait(bar0 + 8 * s, ph[s], err, s_abort);
       ph[s] ^= 1u;
     }
     unsigned char* st = smem + s * G1_STAGE;
@@ -159,7 +162,7 @@ k_larfb_tc(const float* __restrict__ V, int64_t sVb, int64_t ldv,
     }
     fence_async_smem();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 && *s_abort == 0) {
       fence_after();
       const uint32_t a_hi = sbase + s * G1_STAGE, a_lo = a_hi + G1_A;
       const uint32_t b_hi = a_hi + 2 * G1_A, b_lo = b_hi + G1_B;
@@ -180,13 +183,13 @@ k_larfb_tc(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   // Drain the last (up to two) commits: G1 is complete.
   for (int ch = (nch1 >= 2 ? nch1 - 2 : 0); ch < nch1; ++ch) {
     const int s = ch & 1;
-    mbar_wait(bar0 + 8 * s, ph[s], err);
+    mbar_wait(bar0 + 8 * s, ph[s], err, s_abort);
     ph[s] ^= 1u;
   }
   fence_after();
 
   // ---------------- mid: W' = T^T W, written as G2's A operand ----------------
-  if (warp < 4) {
+  if (warp < 4 && !__any_sync(kFullMask, *s_abort != 0)) {
     float w[32];
     tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + TM_D1, w);
     const int parts = nch1 < kG1Parts ? nch1 : kG1Parts;
@@ -223,8 +226,9 @@ k_larfb_tc(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   const int nch2 = (r + R2 - 1) / R2;
   auto epilogue = [&](int cp) {
     const int s = cp & 1;
-    mbar_wait(bar0 + 8 * (2 + s), ph[2 + s], err);
+    mbar_wait(bar0 + 8 * (2 + s), ph[2 + s], err, s_abort);
     ph[2 + s] ^= 1u;
+    if (__any_sync(kFullMask, *s_abort != 0)) return;  // no TMEM reads, no stores
     fence_after();
     const int q = warp & 3, h = warp >> 2;
     const int col = c0 + 32 * q + lane;
@@ -268,7 +272,7 @@ k_larfb_tc(const float* __restrict__ V, int64_t sVb, int64_t ldv,
     }
     fence_async_smem();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 && *s_abort == 0) {
       fence_after();
       const uint32_t a_hi = sbase + OFF_A2, a_lo = a_hi + A2_BYTES;
       const uint32_t b_hi = sbase + s * G2_STAGE, b_lo = b_hi + G2_B;
@@ -289,6 +293,8 @@ k_larfb_tc(const float* __restrict__ V, int64_t sVb, int64_t ldv,
   }
   epilogue(nch2 - 1);
 
+  __syncthreads();
+  if (tid == 0 && *s_abort != 0) drain_mmas(bar0 + 8 * 4);
   __syncthreads();
   fence_after();
   if (warp == 0)

@@ -61,8 +61,13 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                : "memory");
 }
 
-// Bounded wait on an mbarrier phase; on timeout records the error and gives up.
-__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t phase, int* err) {
+// Bounded wait on an mbarrier phase. Returns at once when *abort (a flag in
+// shared memory) is set; on timeout records the device error and sets *abort,
+// after which the block issues no further MMAs, reads no TMEM and writes no
+// results, drains its issued MMAs (drain_mmas) and frees its TMEM.
+__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t phase, int* err,
+                                          volatile int* abort) {
+  if (*abort != 0) return;
   const long long t0 = clock64();
   while (true) {
     uint32_t done;
@@ -74,7 +79,9 @@ __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t phase, int* err
         : "r"(bar), "r"(phase)
         : "memory");
     if (done) return;
+    if (*abort != 0) return;
     if (clock64() - t0 > kWaitCycles) {
+      *abort = 1;
       atomicExch(err, 1);
       return;
     }
@@ -86,6 +93,24 @@ __device__ __forceinline__ void fence_before() {
 }
 __device__ __forceinline__ void fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// After an abort: commit every tcgen05 operation this thread issued to a
+// fresh mbarrier (count 1, never used before) and wait for it, bounded, so
+// that no MMA still writes TMEM when it is freed.
+__device__ __forceinline__ void drain_mmas(uint32_t fresh_bar) {
+  mma_commit(fresh_bar);
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(fresh_bar), "r"(0u)
+        : "memory");
+    if (done || clock64() - t0 > kWaitCycles) return;
+  }
 }
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
