@@ -178,29 +178,40 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
     __syncthreads();
 
     float tot = 0.f, rowv;
+    // Sums in a fixed order (warp 0 first, rank 0 first), unrolled to the
+    // largest count with a predicate so that the loads issue together.
+    auto warp_sum = [&]() {
+      float t = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kMaxThreads / 32; ++w2)
+        if (w2 < nwarps) t += red[par][w2][lane];
+      return t;
+    };
     if (cs > 1) {
-      // warp 0 pushes this CTA's sums (and rank 0 row j) to every rank; every
+      // this CTA's sums (and rank 0's row j) go to every rank, the pushes
+      // spread over the warps (warp w serves ranks w, w + nwarps, ...); every
       // rank waits for all of them on its own mbarrier
       const uint32_t bar = bar_mine + par * kParBar;
-      if (warp == 0) {
-        float ct = 0.f;
-        for (int w2 = 0; w2 < nwarps; ++w2) ct += red[par][w2][lane];
+      if (warp < cs) {
+        const float ct = warp_sum();
         const float rv = rowj[par][lane];
-        for (int q = 0; q < cs; ++q) {
+        for (int q = warp; q < cs; q += nwarps) {
           const uint32_t rb = mapa_rank(bar, (uint32_t)q);
           push_f32(mapa_rank(in_mine + par * kParIn, (uint32_t)q), ct, rb);
           if (rank == 0) push_f32(mapa_rank(row_mine + par * kParRow, (uint32_t)q), rv, rb);
         }
-        if (lane == 0) tma::mbar_expect_tx(bar, (uint32_t)((cs + 1) * W * 4));
       }
+      if (tid == 0) tma::mbar_expect_tx(bar, (uint32_t)((cs + 1) * W * 4));
       if (!dead && !tma::mbar_wait_bounded(bar, (uint32_t)((j >> 1) & 1), wait_limit)) {
         dead = true;
         atomicExch(err, 1);
       }
-      for (int q = 0; q < cs; ++q) tot += inbox[par][q][lane];
+#pragma unroll
+      for (int q = 0; q < kMaxCluster; ++q)
+        if (q < cs) tot += inbox[par][q][lane];
       rowv = rowbox[par][lane];
     } else {
-      for (int w2 = 0; w2 < nwarps; ++w2) tot += red[par][w2][lane];
+      tot = warp_sum();
       rowv = rowj[par][lane];
     }
 
