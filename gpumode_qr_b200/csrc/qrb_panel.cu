@@ -89,6 +89,7 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
   __shared__ __align__(16) float fbuf[kMaxThreads / 32][W];  // per-warp tau_j * d, shifted
   __shared__ float Gs[W][W + 1];                 // Gram V^T V, strictly upper part
   __shared__ float taus[W];
+  __shared__ float Tsm[W][W + 1], Ysm[W][W + 1];  // T and the products of its block steps
   // cluster exchange: [parity][source rank][slot] CTA slot sums, row j from
   // rank 0, one mbarrier per parity
   __shared__ float inbox[2][kMaxCluster][W];
@@ -311,26 +312,50 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
 
   if (rank == 0) {
     if (tid < w) tau_out[m * tau_sb + tid] = taus[tid];
-    if (warp == 0 && T_out != nullptr) {
-      // Forward LARFT: lane `row` computes row `row` of T.
-      const int row = lane;
-      float trow[W];
-#pragma unroll
-      for (int i = 0; i < W; ++i) {
-        float t = 0.f;
-#pragma unroll
-        for (int q = 0; q < i; ++q) t = fmaf(trow[q], Gs[q][i], t);
-        trow[i] = row < i ? -taus[i] * t : (row == i ? taus[i] : 0.f);
+    if (T_out != nullptr) {
+      // T by blocks: T of the first 2b columns from the two T of b columns,
+      //   T12 = -T11 (V1^T V2) T22   (V1^T V2 from the Gram, strictly upper),
+      // for b = 1, 2, 4, 8, 16, every entry of a level in parallel. The same
+      // matrix as the forward column recurrence (src/qrbench/triton_kernels.py
+      // :886-909), summed in another order.
+      for (int e = tid; e < W * W; e += nt) {
+        const int i = e / W, k = e % W;
+        Tsm[i][k] = i == k ? taus[i] : 0.f;
       }
-      if (row < w) {
-        float* Tm = T_out + m * T_sb + (int64_t)row * t_ld;
+      __syncthreads();
 #pragma unroll
-        for (int i = 0; i < W; ++i)
-          if (i < t_ld && (t_ld == W || i < w)) Tm[i] = (i < w) ? trow[i] : 0.f;
-      } else if (t_ld == W) {
-        float* Tm = T_out + m * T_sb + (int64_t)row * t_ld;
+      for (int lb = 0; lb < 5; ++lb) {  // block size b = 2^lb (a constant once unrolled)
+        const int b = 1 << lb, cnt = (W / 2) * b;  // (W / 2b) pairs x b^2 entries
+        for (int e = tid; e < cnt; e += nt) {  // Y = G12 T22
+          const int a0 = (e >> (2 * lb)) * 2 * b, b0 = a0 + b;
+          const int i = (e >> lb) & (b - 1), k = e & (b - 1);
+          float y = 0.f;
 #pragma unroll
-        for (int i = 0; i < W; ++i) Tm[i] = 0.f;
+          for (int q = 0; q < b; ++q)
+            if (q <= k) y = fmaf(Gs[a0 + i][b0 + q], Tsm[b0 + q][b0 + k], y);
+          Ysm[a0 + i][b0 + k] = y;
+        }
+        __syncthreads();
+        for (int e = tid; e < cnt; e += nt) {  // T12 = -T11 Y
+          const int a0 = (e >> (2 * lb)) * 2 * b, b0 = a0 + b;
+          const int i = (e >> lb) & (b - 1), k = e & (b - 1);
+          float t = 0.f;
+#pragma unroll
+          for (int q = 0; q < b; ++q)
+            if (q >= i) t = fmaf(Tsm[a0 + i][a0 + q], Ysm[a0 + q][b0 + k], t);
+          Tsm[a0 + i][b0 + k] = -t;
+        }
+        __syncthreads();
+      }
+      for (int e = tid; e < W * W; e += nt) {
+        const int row = e / W, i = e % W;
+        if (i >= t_ld) continue;
+        float* Tm = T_out + m * T_sb + (int64_t)row * t_ld;
+        if (row < w) {
+          if (t_ld == W || i < w) Tm[i] = (i < w) ? Tsm[row][i] : 0.f;
+        } else if (t_ld == W) {
+          Tm[i] = 0.f;
+        }
       }
     }
   }
