@@ -108,10 +108,15 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
 
   for (int e = tid; e < W * (W + 1); e += nt) (&Gs[0][0])[e] = 0.f;
   if (tid < W) taus[tid] = 0.f;
-  if (cs > 1 && tid == 0) {
-    tma::mbar_init(tma::smem_addr(&xbar[0]), 1);
-    tma::mbar_init(tma::smem_addr(&xbar[1]), 1);
-    tma::mbar_fence_init();
+  if (cs > 1) {
+    if (tid == 0) {
+      tma::mbar_init(tma::smem_addr(&xbar[0]), 1);
+      tma::mbar_init(tma::smem_addr(&xbar[1]), 1);
+      tma::mbar_fence_init();
+    }
+    // the peers may push into this CTA once every rank has arrived here (the
+    // wait is after the panel load, which it overlaps)
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   }
 
   float a[RPT][W];
@@ -137,9 +142,8 @@ k_panel(const float* __restrict__ src, int64_t sb_src, int64_t ld_src,
     }
   }
   if (cs > 1)
-    cg::this_cluster().sync();  // the peers' mbarriers are initialised
-  else
-    __syncthreads();
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // peers initialised
+  __syncthreads();
 
   const uint32_t in_mine = tma::smem_addr(&inbox[0][rank][lane]);
   const uint32_t row_mine = tma::smem_addr(&rowbox[0][lane]);
