@@ -97,7 +97,8 @@ constexpr uint32_t BOX2 = R2 * 128;   // one {32 x 128} box, 16 KiB
 constexpr int B_FULL1 = 0, B_SPLIT1 = B_FULL1 + S1, B_EMPTY1 = B_SPLIT1 + S1,
               B_D1FULL = B_EMPTY1 + S1, B_B2READY = B_D1FULL + 1, B_V2FULL = B_B2READY + 1,
               B_V2EMPTY = B_V2FULL + 2, B_ACCFULL = B_V2EMPTY + 2, B_ACCEMPTY = B_ACCFULL + 2,
-              B_TILEDONE = B_ACCEMPTY + 2, B_FIN = B_TILEDONE + 1, NBAR = B_FIN + 1;
+              B_TILEDONE = B_ACCEMPTY + 2, B_FIN = B_TILEDONE + 1, B_XFULL = B_FIN + 1,
+              B_XREAD = B_XFULL + 1, NBAR = B_XREAD + 1;
 constexpr uint32_t TM_COLS = 512;
 constexpr uint32_t TM_D2 = 256;   // two pass-2 accumulators of 128 columns at 256 and 384
 
@@ -134,6 +135,10 @@ struct Lay {
   static constexpr int NP1 = 256 / KR;
   static constexpr uint32_t IDESC1 = tc::idesc(TCOLS, KR, /*a_mn=*/true, /*b_mn=*/true);
   static_assert(OFF_BL + B2B <= REGION, "pass-2 buffers must fit the pass-1 region");
+  // row-split tiles: this CTA's partial W (TCOLS x KR) sits in the staging
+  // boxes between the end of pass 1 and the first pass-2 epilogue
+  static constexpr uint32_t OFF_X = OFF_STG;
+  static_assert(TCOLS * KR * 4 <= 4 * BOX2, "partial W must fit the staging boxes");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 constexpr uint32_t IDESC2 = tc::idesc(R2, TCOLS, /*a_mn=*/false, /*b_mn=*/false);
@@ -203,14 +208,76 @@ __device__ __forceinline__ bool workers_sync_or(bool v) {
   return r != 0;
 }
 
+// ---- the two CTAs of a row-split cluster ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared-memory address of the same byte in cluster rank q.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t a, uint32_t q) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(q));
+  return r;
+}
+__device__ __forceinline__ float4 ld_peer4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+// Arrive on an mbarrier of a peer CTA, releasing this thread's earlier
+// shared-memory accesses at cluster scope.
+__device__ __forceinline__ void mbar_arrive_peer(uint32_t peer_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(peer_bar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait (acquire at cluster scope) for a phase the peer CTA completes;
+// as tma::mbar_wait_or_abort for the abort flag.
+__device__ __forceinline__ bool mbar_wait_cluster_or_abort(uint32_t bar, uint32_t parity,
+                                                           long long limit,
+                                                           volatile int* abort) {
+  if (mbar_try_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_cluster(bar, parity)) {
+    if (*abort != 0) return false;
+    if (clock64() - t0 > limit) {
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
 // vw_hi / vw_lo: plane coordinates of the V hi / lo boxes in the V map.
-template <int KR>
+// CS = 1: one CTA per tile. CS = 2: a cluster of two CTAs per tile, rank q
+// taking rows [q * rsplit, (q + 1) * rsplit) of the trailing block (rsplit a
+// multiple of 128): each forms the partial W^T of its rows, the two swap
+// partials through distributed shared memory and add them (the same sum on
+// both: a + b = b + a in FP32), and each applies the update to its own rows.
+template <int KR, int CS>
 __global__ void __launch_bounds__(NTH, 1)
 k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUtensorMap mC2,
             const __grid_constant__ CUtensorMap mV1, const __grid_constant__ CUtensorMap mV2,
             const float* __restrict__ T, int64_t sTb, int m0, int ntiles, int ntc, int j0,
-            int col0, int col_end, int n, int vw_hi, int vw_lo, int* __restrict__ err,
-            long long wait_limit, int skip_mma) {
+            int col0, int col_end, int n, int vw_hi, int vw_lo, int rsplit,
+            int* __restrict__ err, long long wait_limit, int skip_mma) {
   using L = Lay<KR>;
   constexpr int NA = L::NA, NV2 = L::NV2, NP1 = L::NP1;
   extern __shared__ unsigned char smem_raw[];
@@ -224,9 +291,14 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
   auto BAR = [&](int i) { return bar0 + 8u * (uint32_t)i; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // this CTA's rows of the trailing block: [y0, y0 + rq)
+  const uint32_t rank = CS > 1 ? cluster_rank() : 0u, peer = rank ^ 1u;
   const int r = n - j0;
-  const int nch1 = (r + R1 - 1) / R1;
-  const int nch2 = (r + R2 - 1) / R2;
+  const int y0 = j0 + (int)rank * rsplit;
+  const int rq = CS > 1 ? min(r - (int)rank * rsplit, rsplit) : r;
+  const int nch1 = (rq + R1 - 1) / R1;
+  const int nch2 = (rq + R2 - 1) / R2;
+  const int tfirst = (int)blockIdx.x / CS, tstep = (int)gridDim.x / CS;
 
   if (tid == 0) {
     const uint32_t counts[NBAR] = {1, 1, 1, 1,                          // full1
@@ -236,7 +308,8 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
                                    NWORK,                               // b2ready
                                    1, 1, 1, 1, 1, 1,                    // v2full, v2empty, accfull
                                    NWORK, NWORK,                        // accempty
-                                   1, 1};                               // tiledone, fin
+                                   1, 1,                                // tiledone, fin
+                                   32 * NWORK, 32 * NWORK};             // xfull, xread
     for (int i = 0; i < NBAR; ++i) tma::mbar_init(BAR(i), counts[i]);
     tma::mbar_fence_init();
     *s_abort = 0;
@@ -255,6 +328,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
+  if (CS > 1) cluster_sync_all();  // the peer's mbarriers are initialised
   const uint32_t tmem = *s_tmem;
 
   if (warp == 0) {
@@ -262,7 +336,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
     if (lane == 0) {
       int g1 = 0, g2 = 0, it = 0;
       int last1[S1] = {-1, -1, -1, -1}, last2[2] = {-1, -1};  // use index of the last load issued
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      for (int t = tfirst; t < ntiles; t += tstep, ++it) {
         const int m = m0 + t / ntc;
         const int tc0 = col0 + (t % ntc) * TCOLS;
         const int nbox = min(4, (col_end - tc0 + 31) / 32);
@@ -278,7 +352,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
                                        s_abort))
             continue;
           const uint32_t st = base + (uint32_t)s * L::ST1, fb = BAR(B_FULL1 + s);
-          const int y = j0 + ch * R1;
+          const int y = y0 + ch * R1;
           tma::mbar_expect_tx(fb, tx1);
           for (int bq = 0; bq < nbox; ++bq)
             tma::load_3d(st + bq * BOX1, &mC1, fb, tc0 + 32 * bq, y, m);
@@ -300,7 +374,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
                                        s_abort))
             continue;
           const uint32_t st = base + (uint32_t)v * L::V2ST, fb = BAR(B_V2FULL + v);
-          const int y = j0 + p * R2;
+          const int y = y0 + p * R2;
           tma::mbar_expect_tx(fb, L::V2ST);
 #pragma unroll
           for (int a = 0; a < NA; ++a) {
@@ -324,7 +398,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
     // ================= MMA issuer =================
     if (lane == 0) {
       int g1 = 0, g2 = 0, it = 0;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      for (int t = tfirst; t < ntiles; t += tstep, ++it) {
         for (int ch = 0; ch < nch1; ++ch, ++g1) {
           const int s = g1 % S1, u = g1 / S1;
           if (*s_abort != 0 || skip_mma) continue;
@@ -392,7 +466,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
     const int row = 32 * q + lane;         // TMEM lane = tile column (pass 1) / chunk row (pass 2)
     const bool issuer = wt == 0;
     int g1 = 0, g2 = 0, it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+    for (int t = tfirst; t < ntiles; t += tstep, ++it) {
       const int ml = t / ntc, m = m0 + ml;
       const int tc0 = col0 + (t % ntc) * TCOLS;
       const int nbox = min(4, (col_end - tc0 + 31) / 32);
@@ -429,9 +503,10 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
       bool skip = *s_abort != 0 ||
                   !tma::mbar_wait_or_abort(BAR(B_D1FULL), (uint32_t)(it & 1), wait_limit, s_abort);
       skip = __any_sync(tc::kFullMask, skip);  // tcgen05.ld below is warp-collective
+      float w[KR];
       if (!skip) {
         tc::fence_after();
-        float w[KR], wp[32];
+        float wp[32];
         const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
 #pragma unroll
         for (int a = 0; a < NA; ++a) tmem_ld32_nowait(tl + 32u * a, w + 32 * a);
@@ -446,6 +521,48 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
             for (int b = 0; b < 32; ++b) w[32 * a + b] += wp[b];
           }
         }
+        constexpr int HALF = KR / 2;
+        if (CS > 1) {
+          // partial W of this CTA's rows -> X (16-byte unit (k / 4) * TCOLS +
+          // column; half h writes reflectors [h * HALF, (h + 1) * HALF)), then
+          // add the peer's (half 0 needs reflectors < HALF only)
+          const uint32_t xl = base + L::OFF_X;
+#pragma unroll
+          for (int k4 = 0; k4 < KR / 4; ++k4)
+            if ((k4 < HALF / 4) == (h == 0))
+              *reinterpret_cast<float4*>(sm + L::OFF_X + ((uint32_t)k4 * TCOLS + row) * 16u) =
+                  make_float4(w[4 * k4], w[4 * k4 + 1], w[4 * k4 + 2], w[4 * k4 + 3]);
+          mbar_arrive_peer(peer_addr(BAR(B_XFULL), peer));
+          bool ok = mbar_wait_cluster_or_abort(BAR(B_XFULL), (uint32_t)(it & 1), wait_limit,
+                                               s_abort);
+          ok = __all_sync(tc::kFullMask, ok);
+          if (ok) {
+            const uint32_t xp = peer_addr(xl, peer) + (uint32_t)row * 16u;
+            // 8 loads in flight at a time (registers)
+#pragma unroll
+            for (int g = 0; g < KR / 32; ++g) {
+              float4 pv[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (h == 1 || 8 * g + i < HALF / 4)
+                  pv[i] = ld_peer4(xp + (uint32_t)(8 * g + i) * TCOLS * 16u);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (h == 1 || 8 * g + i < HALF / 4) {
+                  const int k = 4 * (8 * g + i);
+                  w[k] += pv[i].x;
+                  w[k + 1] += pv[i].y;
+                  w[k + 2] += pv[i].z;
+                  w[k + 3] += pv[i].w;
+                }
+            }
+            // the peer may overwrite its X once all 256 workers are past here
+            mbar_arrive_peer(peer_addr(BAR(B_XREAD), peer));
+          }
+          skip = !ok;
+        }
+      }
+      if (!skip) {
         constexpr int HALF = KR / 2;
         float o[HALF];
         if (h == 0) {  // W'[a] for a < KR/2: T[b][a] = 0 for b > a
@@ -486,7 +603,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
       // is past this tile's W' step (the first pass-2 barrier below)
       constexpr int TPT = KR * KR / (32 * NWORK);
       float tnext[TPT];
-      const int tn = t + (int)gridDim.x;
+      const int tn = t + tstep;
       if (tn < ntiles) {
         const float* Tn = T + (int64_t)(tn / ntc) * sTb;
 #pragma unroll
@@ -513,6 +630,9 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
           if (lane == 0) tma::mbar_arrive(BAR(B_ACCEMPTY + ab));
         }
         if (issuer) tma::bulk_wait_read_all();  // the previous reduce has read the staging tile
+        // row-split tiles: the staging boxes hold X until the peer has read it
+        if (CS > 1 && p == 0 && issuer && *s_abort == 0)
+          mbar_wait_cluster_or_abort(BAR(B_XREAD), (uint32_t)(it & 1), wait_limit, s_abort);
         if (workers_sync_or(sk || *s_abort != 0)) continue;
         if (p == 0 && tn < ntiles) {
 #pragma unroll
@@ -532,7 +652,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         workers_sync_or(false);
         if (issuer) {
           for (int bq = 0; bq < nbox; ++bq)
-            tma::reduce_add_3d(&mC2, base + L::OFF_STG + bq * BOX2, tc0 + 32 * bq, j0 + R2 * p,
+            tma::reduce_add_3d(&mC2, base + L::OFF_STG + bq * BOX2, tc0 + 32 * bq, y0 + R2 * p,
                                m);
           tma::bulk_commit();
         }
@@ -549,6 +669,9 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
+  // the peer reads this CTA's shared memory and arrives on its mbarriers
+  // until it is past its last exchange (every wait before here is bounded)
+  if (CS > 1) cluster_sync_all();
   if (tid == 0 && *s_abort != 0) atomicExch(err, 1);
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_COLS)
@@ -604,6 +727,10 @@ int make_larfb_maps(LarfbMaps* maps, const float* H, const float* Vs, int64_t ba
 }
 
 namespace {
+// Row split of a tile across a 2-CTA cluster: rank 0 takes the first rsplit
+// rows of the trailing block (a multiple of the pass-2 chunk), rank 1 the rest.
+int split_rows_of(int r) { return (((r + 1) / 2 + R2 - 1) / R2) * R2; }
+
 template <int KR>
 int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0, int64_t count,
                  int j0, int col0, int col_end, int n, int vw_hi, int vw_lo,
@@ -611,16 +738,36 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
   static bool attr_set[64] = {};
   static int* err_ptr[64] = {};
   static int sms[64] = {};
+  static int max_pairs[64] = {};  // co-resident 2-CTA clusters
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(k_larfb_tma<KR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(k_larfb_tma<KR, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)Lay<KR>::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(k_larfb_tma<KR, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Lay<KR>::SMEM_BYTES) != cudaSuccess)
       return QRB_ERR_LAUNCH;
     if (device_error_ptr(&err_ptr[dev]) != QRB_OK) return QRB_ERR_DEVICE;
     if (cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         sms[dev] <= 0)
       return QRB_ERR_DEVICE;
+    cudaLaunchConfig_t qc = {};
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 2;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    qc.gridDim = dim3(2 * (unsigned)sms[dev]);
+    qc.blockDim = dim3(NTH);
+    qc.dynamicSmemBytes = Lay<KR>::SMEM_BYTES;
+    qc.attrs = qa;
+    qc.numAttrs = 1;
+    int pairs = 0;
+    if (cudaOccupancyMaxActiveClusters(&pairs, k_larfb_tma<KR, 2>, &qc) != cudaSuccess) {
+      (void)cudaGetLastError();
+      pairs = 0;  // no row split on this device
+    }
+    max_pairs[dev] = pairs;
     attr_set[dev] = true;
   }
   const int64_t ntc = (col_end - col0 + TCOLS - 1) / TCOLS;
@@ -629,10 +776,39 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
   int most = sms[dev];  // persistent: at most one CTA per SM
   const int cap = tma_cta_cap();
   if (cap > 0 && cap < most) most = cap;
-  const int grid = (int)(tiles < most ? tiles : most);
-  k_larfb_tma<KR><<<grid, NTH, Lay<KR>::SMEM_BYTES, stream>>>(
-      maps.c1, maps.c2, maps.v1, maps.v2, T, sTb, (int)m0, (int)tiles, (int)ntc, j0, col0,
-      col_end, n, vw_hi, vw_lo, err_ptr[dev], device_wait_limit(), test_skip_mma() ? 1 : 0);
+  const int r = n - j0;
+  const int split_min = tma_split_rows();
+  // a pure function of the trailing block's height (and the hooks), never of
+  // the batch, so that results do not depend on how a batch is grouped
+  const bool split = split_min > 0 && r >= split_min && r > R2 && max_pairs[dev] > 0;
+  if (!split) {
+    const int grid = (int)(tiles < most ? tiles : most);
+    k_larfb_tma<KR, 1><<<grid, NTH, Lay<KR>::SMEM_BYTES, stream>>>(
+        maps.c1, maps.c2, maps.v1, maps.v2, T, sTb, (int)m0, (int)tiles, (int)ntc, j0, col0,
+        col_end, n, vw_hi, vw_lo, r, err_ptr[dev], device_wait_limit(),
+        test_skip_mma() ? 1 : 0);
+  } else {
+    int pairs = most / 2 > 0 ? most / 2 : 1;
+    if (pairs > max_pairs[dev]) pairs = max_pairs[dev];
+    if (tiles < pairs) pairs = (int)tiles;
+    cudaLaunchConfig_t lc = {};
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeClusterDimension;
+    la[0].val.clusterDim.x = 2;
+    la[0].val.clusterDim.y = 1;
+    la[0].val.clusterDim.z = 1;
+    lc.gridDim = dim3(2 * (unsigned)pairs);
+    lc.blockDim = dim3(NTH);
+    lc.dynamicSmemBytes = Lay<KR>::SMEM_BYTES;
+    lc.stream = stream;
+    lc.attrs = la;
+    lc.numAttrs = 1;
+    if (cudaLaunchKernelEx(&lc, k_larfb_tma<KR, 2>, maps.c1, maps.c2, maps.v1, maps.v2, T, sTb,
+                           (int)m0, (int)tiles, (int)ntc, j0, col0, col_end, n, vw_hi, vw_lo,
+                           split_rows_of(r), err_ptr[dev], device_wait_limit(),
+                           test_skip_mma() ? 1 : 0) != cudaSuccess)
+      return QRB_ERR_LAUNCH;
+  }
   note_launches(1);
   return cudaGetLastError() == cudaSuccess ? QRB_OK : QRB_ERR_LAUNCH;
 }

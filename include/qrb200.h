@@ -297,6 +297,12 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 of such calls are wrong).
  *   "tma_ctas"    most CTAs of one TMA-fed update launch, 1..4096 (0, the
  *                 default: one per SM).
+ *   "tma_split_rows" 0..2^20: the TMA-fed update splits each tile's rows
+ *                 across a cluster of two CTAs (each forms the partial
+ *                 V^T C of its rows; the two add the partials through
+ *                 distributed shared memory) when the trailing block has at
+ *                 least this many rows (default 1024; 0 = never). Results
+ *                 depend on this value, never on the batch or its grouping.
  *   "narrow_update" 0: the tensor-core route updates the next panel's 32
  *                 columns with the TMA-fed kernel as well, instead of the
  *                 narrow kernel that splits their rows across a cluster

@@ -213,6 +213,12 @@ def test_config_keys():
     _lib.set_config("host_groups", 8)
     with pytest.raises(_lib.QRBError):
         _lib.set_config("host_groups", 9)
+    assert _lib.get_config("tma_split_rows") == 1024
+    _lib.set_config("tma_split_rows", 0)
+    assert _lib.get_config("tma_split_rows") == 0
+    _lib.set_config("tma_split_rows", 1024)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("tma_split_rows", -1)
     assert _lib.get_config("tma_ctas") == 0
     _lib.set_config("tma_ctas", 96)
     assert _lib.get_config("tma_ctas") == 96
