@@ -29,7 +29,8 @@ std::atomic<int64_t> g_gram_tile{0};
 std::atomic<int64_t> g_wait_limit{2000000000LL};  // clock cycles, about 1 s
 std::atomic<int64_t> g_skip_mma{0};
 std::atomic<int64_t> g_tma_ctas{0};        // 0 = one per SM
-std::atomic<int64_t> g_tma_split{1024};    // row-split TMA tiles from this height (0 = never)
+std::atomic<int64_t> g_tma_split{1024};    // two row halves from this height (0 = never)
+std::atomic<int64_t> g_tma_pair{0};        // halves on: 0 auto, 1 one CTA, 2 a CTA pair per tile
 std::atomic<int64_t> g_narrow{1};          // narrow cluster kernel for the next panel's columns
 std::atomic<int64_t> g_panel_priority{1};  // look-ahead stream at the highest priority
 
@@ -435,6 +436,7 @@ long long device_wait_limit() { return (long long)g_wait_limit.load(); }
 bool test_skip_mma() { return g_skip_mma.load() != 0; }
 int tma_cta_cap() { return (int)g_tma_ctas.load(); }
 int tma_split_rows() { return (int)g_tma_split.load(); }
+int tma_pair_mode() { return (int)g_tma_pair.load(); }
 
 size_t vsplit_bytes(int64_t batch, int n) {
   if (batch <= 0 || n < kTmaMinN || n % 4 != 0) return 0;
@@ -818,6 +820,11 @@ int qrb_set_config(const char* key, int64_t value) {
     g_tma_split.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "tma_pair") == 0) {
+    if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
+    g_tma_pair.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "narrow_update") == 0) {
     if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
     g_narrow.store(value);
@@ -911,6 +918,7 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "tma_ctas") == 0) { *value = g_tma_ctas.load(); return QRB_OK; }
   if (std::strcmp(key, "narrow_update") == 0) { *value = g_narrow.load(); return QRB_OK; }
   if (std::strcmp(key, "tma_split_rows") == 0) { *value = g_tma_split.load(); return QRB_OK; }
+  if (std::strcmp(key, "tma_pair") == 0) { *value = g_tma_pair.load(); return QRB_OK; }
   if (std::strcmp(key, "panel_priority") == 0) { *value = g_panel_priority.load(); return QRB_OK; }
   if (std::strcmp(key, "device_error") == 0) {
     int v = 0;

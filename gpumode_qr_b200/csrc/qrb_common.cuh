@@ -178,10 +178,12 @@ bool test_skip_mma();
 // qrb_set_config("tma_ctas"): most CTAs of one TMA-fed update launch (0 = one
 // per SM).
 int tma_cta_cap();
-// qrb_set_config("tma_split_rows"): the TMA-fed update splits the rows of each
-// tile across a 2-CTA cluster when the trailing block has at least this many
-// rows (0 = never).
+// qrb_set_config("tma_split_rows"): the TMA-fed update sums V^T C in two row
+// halves when the trailing block has at least this many rows (0 = never).
 int tma_split_rows();
+// qrb_set_config("tma_pair"): with two halves, 0 = a 2-CTA cluster per tile
+// when 2 x tiles <= SMs, 1 = one CTA per tile, 2 = always a pair.
+int tma_pair_mode();
 // One probe kernel that waits on an mbarrier nobody arrives at for `limit`
 // cycles and then sets the device error flag.
 int launch_wait_probe(long long limit, cudaStream_t stream);

@@ -183,6 +183,20 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float* v) {
 #pragma unroll
   for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(r[q]);
 }
+// 16 consecutive TMEM columns of this warp's lane quarter (no wait).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int q = 0; q < 16; ++q) v[q] = __uint_as_float(r[q]);
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -298,6 +312,15 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
   const int rq = CS > 1 ? min(r - (int)rank * rsplit, rsplit) : r;
   const int nch1 = (rq + R1 - 1) / R1;
   const int nch2 = (rq + R2 - 1) / R2;
+  // Pass-1 partial accumulators. Without halves (rsplit >= r, one CTA): chunk
+  // ch into partial ch % NP1. With halves (rsplit < r): rows [0, rsplit) and
+  // [rsplit, r) each into NP1 / 2 interleaved partials and the two half sums
+  // added last -- one CTA keeps both halves (partials NP1 / 2 and up for the
+  // second), a 2-CTA cluster one half per CTA: the same FP32 operations in
+  // the same order either way, so the bits do not depend on the CTA count.
+  constexpr int NPH = NP1 / 2;
+  const bool halves = CS > 1 || rsplit < r;
+  const int c1 = CS > 1 ? nch1 : (halves ? rsplit / R1 : nch1);  // chunks of the first half
   const int tfirst = (int)blockIdx.x / CS, tstep = (int)gridDim.x / CS;
 
   if (tid == 0) {
@@ -406,7 +429,19 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
             continue;
           tc::fence_after();
           const uint32_t st = base + (uint32_t)s * L::ST1;
-          const uint32_t d1 = tmem + (uint32_t)KR * (uint32_t)(ch % NP1);
+          int slot;
+          bool first;
+          if (!halves) {
+            slot = ch % NP1;
+            first = ch < NP1;
+          } else if (ch < c1) {
+            slot = ch % NPH;
+            first = ch < NPH;
+          } else {
+            slot = NPH + (ch - c1) % NPH;
+            first = ch - c1 < NPH;
+          }
+          const uint32_t d1 = tmem + (uint32_t)KR * (uint32_t)slot;
           // the k-step's operands are 1024 bytes further on: add to the
           // descriptors' address field (units of 16 bytes; no carry)
           const uint64_t ah0 = sdesc_mn32(st, BOX1), al0 = sdesc_mn32(st + L::S1_CL, BOX1);
@@ -415,7 +450,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
 #pragma unroll
           for (int ks = 0; ks < R1 / 8; ++ks) {
             const uint64_t dk = (uint64_t)(ks * (1024 >> 4));
-            tc::mma_tf32(d1, ah0 + dk, bh0 + dk, L::IDESC1, (ch >= NP1 || ks != 0) ? 1u : 0u);
+            tc::mma_tf32(d1, ah0 + dk, bh0 + dk, L::IDESC1, (!first || ks != 0) ? 1u : 0u);
             tc::mma_tf32(d1, ah0 + dk, bl0 + dk, L::IDESC1, 1u);
             tc::mma_tf32(d1, al0 + dk, bh0 + dk, L::IDESC1, 1u);
           }
@@ -511,7 +546,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
 #pragma unroll
         for (int a = 0; a < NA; ++a) tmem_ld32_nowait(tl + 32u * a, w + 32 * a);
         tmem_wait_ld();
-        const int np = nch1 < NP1 ? nch1 : NP1;
+        const int np = halves ? min(c1, NPH) : min(nch1, NP1);
         for (int pp = 1; pp < np; ++pp) {
 #pragma unroll
           for (int a = 0; a < NA; ++a) {
@@ -519,6 +554,23 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
             tmem_wait_ld();
 #pragma unroll
             for (int b = 0; b < 32; ++b) w[32 * a + b] += wp[b];
+          }
+        }
+        if (CS == 1 && halves) {  // the second half's sum (16 columns at a time), added
+          const int np2 = min(nch1 - c1, NPH);
+#pragma unroll
+          for (int a = 0; a < KR / 16; ++a) {
+            float ws2[16];
+            tmem_ld16_nowait(tl + (uint32_t)(KR * NPH + 16 * a), ws2);
+            tmem_wait_ld();
+            for (int pp = 1; pp < np2; ++pp) {
+              tmem_ld16_nowait(tl + (uint32_t)(KR * (NPH + pp) + 16 * a), wp);
+              tmem_wait_ld();
+#pragma unroll
+              for (int b = 0; b < 16; ++b) ws2[b] += wp[b];
+            }
+#pragma unroll
+            for (int b = 0; b < 16; ++b) w[16 * a + b] += ws2[b];
           }
         }
         constexpr int HALF = KR / 2;
@@ -778,14 +830,21 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
   if (cap > 0 && cap < most) most = cap;
   const int r = n - j0;
   const int split_min = tma_split_rows();
-  // a pure function of the trailing block's height (and the hooks), never of
-  // the batch, so that results do not depend on how a batch is grouped
-  const bool split = split_min > 0 && r >= split_min && r > R2 && max_pairs[dev] > 0;
-  if (!split) {
+  // The arithmetic (two row halves or not) is a pure function of the trailing
+  // block's height and the hooks, never of the batch, so results do not depend
+  // on how a batch is grouped. One CTA or a CTA pair per tile computes the
+  // same bits: a pair when the launch's tiles fit the SMs twice over (the
+  // batch groups and the look-ahead kernels beside it fill the SMs left).
+  const bool halves = split_min > 0 && r >= split_min && r > R2;
+  const int rs = halves ? split_rows_of(r) : r;
+  const int mode = tma_pair_mode();
+  const bool pair = halves && max_pairs[dev] > 0 &&
+                    (mode == 2 || (mode == 0 && 2 * tiles <= sms[dev]));
+  if (!pair) {
     const int grid = (int)(tiles < most ? tiles : most);
     k_larfb_tma<KR, 1><<<grid, NTH, Lay<KR>::SMEM_BYTES, stream>>>(
         maps.c1, maps.c2, maps.v1, maps.v2, T, sTb, (int)m0, (int)tiles, (int)ntc, j0, col0,
-        col_end, n, vw_hi, vw_lo, r, err_ptr[dev], device_wait_limit(),
+        col_end, n, vw_hi, vw_lo, rs, err_ptr[dev], device_wait_limit(),
         test_skip_mma() ? 1 : 0);
   } else {
     int pairs = most / 2 > 0 ? most / 2 : 1;
@@ -805,7 +864,7 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
     lc.numAttrs = 1;
     if (cudaLaunchKernelEx(&lc, k_larfb_tma<KR, 2>, maps.c1, maps.c2, maps.v1, maps.v2, T, sTb,
                            (int)m0, (int)tiles, (int)ntc, j0, col0, col_end, n, vw_hi, vw_lo,
-                           split_rows_of(r), err_ptr[dev], device_wait_limit(),
+                           rs, err_ptr[dev], device_wait_limit(),
                            test_skip_mma() ? 1 : 0) != cudaSuccess)
       return QRB_ERR_LAUNCH;
   }

@@ -297,12 +297,18 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 of such calls are wrong).
  *   "tma_ctas"    most CTAs of one TMA-fed update launch, 1..4096 (0, the
  *                 default: one per SM).
- *   "tma_split_rows" 0..2^20: the TMA-fed update splits each tile's rows
- *                 across a cluster of two CTAs (each forms the partial
- *                 V^T C of its rows; the two add the partials through
- *                 distributed shared memory) when the trailing block has at
- *                 least this many rows (default 1024; 0 = never). Results
- *                 depend on this value, never on the batch or its grouping.
+ *   "tma_split_rows" 0..2^20: the TMA-fed update sums each tile's V^T C in
+ *                 two row halves (each over its own interleaved partial
+ *                 accumulators, the two sums added last) when the trailing
+ *                 block has at least this many rows (default 1024; 0 =
+ *                 never). Results depend on this value, never on the batch,
+ *                 its grouping or "tma_pair".
+ *   "tma_pair"    with two row halves, 0 (default): a cluster of two CTAs per
+ *                 tile (one half each; the partial sums added through
+ *                 distributed shared memory) when the launch's tiles fit the
+ *                 SMs twice over (2 x tiles <= SMs), else one CTA per tile;
+ *                 1: always one CTA; 2: always a pair. The same bits either
+ *                 way.
  *   "narrow_update" 0: the tensor-core route updates the next panel's 32
  *                 columns with the TMA-fed kernel as well, instead of the
  *                 narrow kernel that splits their rows across a cluster

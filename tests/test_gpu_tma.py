@@ -318,15 +318,20 @@ def test_two_level_lookahead_route(b, n, groups):
                                                      (8, 512, 0, 0, 4), (2, 1024, 1, 1, 1),
                                                      (4, 1028, 1, 0, 2), (1, 2048, 1, 1, 1)])
 def test_row_split_tiles(b, n, two_level, la, groups):
-    # every tile of every update over more than 128 rows split across a 2-CTA
-    # cluster (each CTA's rows form a partial V^T C; the two add them through
-    # distributed shared memory): FP64 gates, within 1e-4 of FP64 LAPACK and
-    # of the unsplit update, and the batch groups leave the bits unchanged
+    # every update over more than 128 rows sums V^T C in two row halves: one
+    # CTA per tile keeping both, or a 2-CTA cluster per tile (one half each,
+    # the partials added through distributed shared memory) give the same
+    # bits, as do the batch groups; FP64 gates, within 1e-4 of FP64 LAPACK and
+    # of the update without halves
     A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(31 * n + b)).to(DEV)
-    old = _hooks(tma_split_rows=129, two_level=two_level, lookahead=la, groups=groups)
+    old = _hooks(tma_split_rows=129, tma_pair=2, two_level=two_level, lookahead=la,
+                 groups=groups)
     try:
         assert "tcgen05_tma" in api.route(b, n)
         Hs, ts = api.geqrf(A)
+        _lib.set_config("tma_pair", 1)
+        Hp, tp = api.geqrf(A)
+        _lib.set_config("tma_pair", 0)
         _lib.set_config("groups", 1)
         Hs1, ts1 = api.geqrf(A)
         _lib.set_config("tma_split_rows", 0)
@@ -334,6 +339,7 @@ def test_row_split_tiles(b, n, two_level, la, groups):
         torch.cuda.synchronize()
     finally:
         _restore(old)
+    assert torch.equal(Hs, Hp) and torch.equal(ts, tp)
     assert torch.equal(Hs, Hs1) and torch.equal(ts, ts1)
     assert checker.check(A, Hs, ts).passed
     H64, t64 = torch.geqrf(A.cpu().double())
@@ -350,7 +356,8 @@ def test_row_split_update_abandons_a_call_whose_waits_run_out():
     # flag, meet at the closing cluster barrier and free their TMEM
     A = torch.randn(2, 256, 256, generator=torch.Generator().manual_seed(2)).to(DEV)
     _lib.set_config("device_error", 0)
-    old = _hooks(wait_limit=2_000_000, test_skip_mma=1, sync_check=1, tma_split_rows=129)
+    old = _hooks(wait_limit=2_000_000, test_skip_mma=1, sync_check=1, tma_split_rows=129,
+                 tma_pair=2)
     try:
         with pytest.raises(_lib.QRBError) as exc:
             api.geqrf(A)
@@ -359,7 +366,7 @@ def test_row_split_update_abandons_a_call_whose_waits_run_out():
         _restore(old)
     assert _lib.get_config("device_error") == 1
     _lib.set_config("device_error", 0)
-    old = _hooks(tma_split_rows=129)
+    old = _hooks(tma_split_rows=129, tma_pair=2)
     try:
         H, tau = api.geqrf(A)
         torch.cuda.synchronize()
