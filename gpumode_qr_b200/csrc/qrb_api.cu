@@ -31,6 +31,7 @@ std::atomic<int64_t> g_skip_mma{0};
 std::atomic<int64_t> g_tma_ctas{0};        // 0 = one per SM
 std::atomic<int64_t> g_tma_split{1024};    // two row halves from this height (0 = never)
 std::atomic<int64_t> g_tma_pair{0};        // halves on: 0 auto, 1 one CTA, 2 a CTA pair per tile
+std::atomic<int64_t> g_tma_dual{0};        // 32 reflectors: 0 auto, 1 one CTA per SM, 2 two
 std::atomic<int64_t> g_narrow{1};          // narrow cluster kernel for the next panel's columns
 std::atomic<int64_t> g_panel_priority{1};  // look-ahead stream at the highest priority
 
@@ -437,6 +438,7 @@ bool test_skip_mma() { return g_skip_mma.load() != 0; }
 int tma_cta_cap() { return (int)g_tma_ctas.load(); }
 int tma_split_rows() { return (int)g_tma_split.load(); }
 int tma_pair_mode() { return (int)g_tma_pair.load(); }
+int tma_dual_mode() { return (int)g_tma_dual.load(); }
 
 size_t vsplit_bytes(int64_t batch, int n) {
   if (batch <= 0 || n < kTmaMinN || n % 4 != 0) return 0;
@@ -825,6 +827,11 @@ int qrb_set_config(const char* key, int64_t value) {
     g_tma_pair.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "tma_dual") == 0) {
+    if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
+    g_tma_dual.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "narrow_update") == 0) {
     if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
     g_narrow.store(value);
@@ -919,6 +926,7 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "narrow_update") == 0) { *value = g_narrow.load(); return QRB_OK; }
   if (std::strcmp(key, "tma_split_rows") == 0) { *value = g_tma_split.load(); return QRB_OK; }
   if (std::strcmp(key, "tma_pair") == 0) { *value = g_tma_pair.load(); return QRB_OK; }
+  if (std::strcmp(key, "tma_dual") == 0) { *value = g_tma_dual.load(); return QRB_OK; }
   if (std::strcmp(key, "panel_priority") == 0) { *value = g_panel_priority.load(); return QRB_OK; }
   if (std::strcmp(key, "device_error") == 0) {
     int v = 0;

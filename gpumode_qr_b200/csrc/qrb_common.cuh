@@ -184,6 +184,10 @@ int tma_split_rows();
 // qrb_set_config("tma_pair"): with two halves, 0 = a 2-CTA cluster per tile
 // when 2 x tiles <= SMs, 1 = one CTA per tile, 2 = always a pair.
 int tma_pair_mode();
+// qrb_set_config("tma_dual"): 32-reflector updates without row halves, 0 = two
+// CTAs per SM when the launch has more tiles than SMs, 1 = one CTA per SM,
+// 2 = always two (the same bits either way).
+int tma_dual_mode();
 // One probe kernel that waits on an mbarrier nobody arrives at for `limit`
 // cycles and then sets the device error flag.
 int launch_wait_probe(long long limit, cudaStream_t stream);

@@ -85,61 +85,74 @@ bool encode_f32_sw128(CUtensorMap* map, const void* base, int rank, const uint64
 namespace {
 
 constexpr int TCOLS = 128;    // columns of C per tile
-constexpr int NWORK = 8;      // worker warps
-constexpr int NTH = 32 * (2 + NWORK);
 constexpr int R1 = 32;        // rows per pass-1 chunk
-constexpr int S1 = 4;         // pass-1 ring stages
+constexpr int S1MAX = 4;      // pass-1 ring stages (mbarrier slots)
 constexpr int R2 = 128;       // rows per pass-2 chunk (MMA M)
 constexpr uint32_t BOX1 = R1 * 128;   // one {32 x R1} FP32 box, 4 KiB
 constexpr uint32_t CST = 4 * BOX1;    // C part of a pass-1 stage: 4 boxes = 128 columns
 constexpr uint32_t BOX2 = R2 * 128;   // one {32 x 128} box, 16 KiB
 // mbarriers
-constexpr int B_FULL1 = 0, B_SPLIT1 = B_FULL1 + S1, B_EMPTY1 = B_SPLIT1 + S1,
-              B_D1FULL = B_EMPTY1 + S1, B_B2READY = B_D1FULL + 1, B_V2FULL = B_B2READY + 1,
+constexpr int B_FULL1 = 0, B_SPLIT1 = B_FULL1 + S1MAX, B_EMPTY1 = B_SPLIT1 + S1MAX,
+              B_D1FULL = B_EMPTY1 + S1MAX, B_B2READY = B_D1FULL + 1, B_V2FULL = B_B2READY + 1,
               B_V2EMPTY = B_V2FULL + 2, B_ACCFULL = B_V2EMPTY + 2, B_ACCEMPTY = B_ACCFULL + 2,
               B_TILEDONE = B_ACCEMPTY + 2, B_FIN = B_TILEDONE + 1, B_XFULL = B_FIN + 1,
               B_XREAD = B_XFULL + 1, NBAR = B_XREAD + 1;
-constexpr uint32_t TM_COLS = 512;
-constexpr uint32_t TM_D2 = 256;   // two pass-2 accumulators of 128 columns at 256 and 384
 
 // Layout for a block of KR reflectors (32, or 64 for two-level blocking).
 //   Shared memory (bytes from a 1024-aligned base): a pass-1 stage holds the
 //   C chunk (hi after the split), the V hi and lo boxes (KR / 32 boxes each)
 //   and the C lo buffer. Pass 2 reuses the pass-1 region once every pass-1
-//   MMA of the tile is done: NV2 stages of V (hi and lo), 4 staging boxes for
-//   -V W', and W' hi / lo as the K-major B operand.
-//   TMEM: pass 1 accumulates into NP1 partial accumulators of KR columns
+//   MMA of the tile is done: NV2 stages of V (hi and lo), NSTG staging boxes
+//   for -V W', and W' hi / lo as the K-major B operand.
+//   TMEM: pass 1 accumulates into NP1 = 4 partial accumulators of KR columns
 //   (chunk ch into partial ch % NP1), summed in FP32 afterwards: the tensor
 //   core's accumulation inside an MMA is not rounded to nearest at every add,
 //   so one accumulator over thousands of rows drifts ~5x further from FP64
-//   than FFMA; short chains keep it at FFMA's level.
-template <int KR>
+//   than FFMA; short chains keep it at FFMA's level. Pass 2 accumulates into
+//   NACC accumulators of 128 columns from column TM_D2.
+// DUAL (32 reflectors only): two CTAs per SM, so that one CTA's pass 1 (bound
+//   by issuing MMAs) runs beside the other's pass 2 (bound by the TMA
+//   reduce-adds reading the staging tile): 4 worker warps, 2 pass-1 stages, one
+//   pass-2 V stage and accumulator, 2 staging boxes (the epilogue in two
+//   column halves), 256 TMEM columns. The FP32 operations are those of the
+//   one-CTA-per-SM layout, in the same order: the same bits.
+template <int KR, bool DUAL = false>
 struct Lay {
+  static constexpr int NWORK = DUAL ? 4 : 8;               // worker warps
+  static constexpr int NTH = 32 * (2 + NWORK);
+  static constexpr int S1 = DUAL ? 2 : 4;                  // pass-1 ring stages
   static constexpr int NA = KR / 32;                       // 32-wide atoms of V / of K
   static constexpr uint32_t VB1 = NA * BOX1;
   static constexpr uint32_t ST1 = CST + 2 * VB1 + CST;
   static constexpr uint32_t S1_VH = CST, S1_VL = CST + VB1, S1_CL = CST + 2 * VB1;
-  static constexpr uint32_t REGION = S1 * ST1;
-  static constexpr int NV2 = KR == 32 ? 2 : 1;
+  static constexpr int NV2 = DUAL ? 1 : (KR == 32 ? 2 : 1);
   static constexpr uint32_t V2ST = 2 * NA * BOX2;
   static constexpr uint32_t OFF_STG = NV2 * V2ST;
+  static constexpr int NSTG = DUAL ? 2 : 4;                // staging boxes of 32 columns
   static constexpr uint32_t B2B = NA * TCOLS * 128;
-  static constexpr uint32_t OFF_BH = OFF_STG + 4 * BOX2;
+  static constexpr uint32_t OFF_BH = OFF_STG + NSTG * BOX2;
   static constexpr uint32_t OFF_BL = OFF_BH + B2B;
+  static constexpr uint32_t P1END = S1 * ST1, P2END = OFF_BL + B2B;
+  static constexpr uint32_t REGION = P1END > P2END ? P1END : P2END;
   static constexpr uint32_t OFF_T = REGION;
   static constexpr int T_LD = KR + 1;
   static constexpr uint32_t OFF_BAR = OFF_T + ((KR * T_LD * 4 + 127) / 128) * 128;
   static constexpr uint32_t OFF_TMEMV = OFF_BAR + NBAR * 8;
   static constexpr uint32_t OFF_ABORT = OFF_TMEMV + 4;
   static constexpr size_t SMEM_BYTES = OFF_ABORT + 12 + 1024;  // slack for aligning the base
-  static constexpr int NP1 = 256 / KR;
+  static constexpr int NP1 = 4;
+  static constexpr int NACC = DUAL ? 1 : 2;
+  static constexpr uint32_t TM_COLS = DUAL ? 256 : 512;
+  static constexpr uint32_t TM_D2 = TM_COLS - 128 * NACC;
   static constexpr uint32_t IDESC1 = tc::idesc(TCOLS, KR, /*a_mn=*/true, /*b_mn=*/true);
-  static_assert(OFF_BL + B2B <= REGION, "pass-2 buffers must fit the pass-1 region");
   // row-split tiles: this CTA's partial W (TCOLS x KR) sits in the staging
   // boxes between the end of pass 1 and the first pass-2 epilogue
   static constexpr uint32_t OFF_X = OFF_STG;
-  static_assert(TCOLS * KR * 4 <= 4 * BOX2, "partial W must fit the staging boxes");
-  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(!DUAL || KR == 32, "two CTAs per SM for 32 reflectors only");
+  static_assert(S1 <= S1MAX, "pass-1 stages");
+  static_assert(NP1 * KR <= (int)TM_D2, "pass-1 partials below the pass-2 accumulators");
+  static_assert(TCOLS * KR * 4 <= NSTG * BOX2, "partial W must fit the staging boxes");
+  static_assert(SMEM_BYTES <= (DUAL ? 113 * 1024 : 227 * 1024), "shared memory budget");
 };
 constexpr uint32_t IDESC2 = tc::idesc(R2, TCOLS, /*a_mn=*/false, /*b_mn=*/false);
 
@@ -209,6 +222,7 @@ __device__ __forceinline__ uint32_t sw128(int row, int u) {
 
 // Barrier among the worker warps only (named barrier 1), with an OR of a
 // per-thread flag: every worker gets the same answer.
+template <int NW>
 __device__ __forceinline__ bool workers_sync_or(bool v) {
   uint32_t r;
   asm volatile(
@@ -217,7 +231,7 @@ __device__ __forceinline__ bool workers_sync_or(bool v) {
       "bar.red.or.pred p, 1, %2, q;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(r)
-      : "r"((uint32_t)v), "n"(32 * NWORK)
+      : "r"((uint32_t)v), "n"(32 * NW)
       : "memory");
   return r != 0;
 }
@@ -285,15 +299,16 @@ __device__ __forceinline__ bool mbar_wait_cluster_or_abort(uint32_t bar, uint32_
 // multiple of 128): each forms the partial W^T of its rows, the two swap
 // partials through distributed shared memory and add them (the same sum on
 // both: a + b = b + a in FP32), and each applies the update to its own rows.
-template <int KR, int CS>
-__global__ void __launch_bounds__(NTH, 1)
+template <int KR, int CS, bool DUAL>
+__global__ void __launch_bounds__(Lay<KR, DUAL>::NTH, DUAL ? 2 : 1)
 k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUtensorMap mC2,
             const __grid_constant__ CUtensorMap mV1, const __grid_constant__ CUtensorMap mV2,
             const float* __restrict__ T, int64_t sTb, int m0, int ntiles, int ntc, int j0,
             int col0, int col_end, int n, int vw_hi, int vw_lo, int rsplit,
             int* __restrict__ err, long long wait_limit, int skip_mma) {
-  using L = Lay<KR>;
-  constexpr int NA = L::NA, NV2 = L::NV2, NP1 = L::NP1;
+  using L = Lay<KR, DUAL>;
+  constexpr int NA = L::NA, NV2 = L::NV2, NP1 = L::NP1, S1 = L::S1, NWORK = L::NWORK;
+  static_assert(!(DUAL && CS > 1), "row-split pairs use the one-CTA-per-SM layout");
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = tma::smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -344,7 +359,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      base + L::OFF_TMEMV),
-                 "r"(TM_COLS)
+                 "r"(L::TM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -358,7 +373,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
     // ================= TMA producer =================
     if (lane == 0) {
       int g1 = 0, g2 = 0, it = 0;
-      int last1[S1] = {-1, -1, -1, -1}, last2[2] = {-1, -1};  // use index of the last load issued
+      int last1[S1MAX] = {-1, -1, -1, -1}, last2[2] = {-1, -1};  // use index of the last load issued
       for (int t = tfirst; t < ntiles; t += tstep, ++it) {
         const int m = m0 + t / ntc;
         const int tc0 = col0 + (t % ntc) * TCOLS;
@@ -462,7 +477,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
           tma::mbar_wait_or_abort(BAR(B_B2READY), (uint32_t)(it & 1), wait_limit, s_abort);
         for (int p = 0; p < nch2; ++p, ++g2) {
           const int v = g2 % NV2, u = g2 / NV2;
-          const int ab = g2 & 1, ua = g2 >> 1;  // TMEM accumulator
+          const int ab = g2 % L::NACC, ua = g2 / L::NACC;  // TMEM accumulator
           if (*s_abort != 0) continue;
           if (!tma::mbar_wait_or_abort(BAR(B_V2FULL + v), (uint32_t)(u & 1), wait_limit, s_abort))
             continue;
@@ -471,7 +486,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
             continue;
           tc::fence_after();
           const uint32_t va = base + (uint32_t)v * L::V2ST;
-          const uint32_t d = tmem + TM_D2 + 128u * (uint32_t)ab;
+          const uint32_t d = tmem + L::TM_D2 + 128u * (uint32_t)ab;
           const uint64_t ah0 = sdesc_kmajor(va), al0 = sdesc_kmajor(va + NA * BOX2);
           const uint64_t bh0 = sdesc_kmajor(base + L::OFF_BH);
           const uint64_t bl0 = sdesc_kmajor(base + L::OFF_BL);
@@ -495,9 +510,10 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
     }
   } else {
     // ================= workers =================
-    const int wt = tid - 64;               // 0..255
+    const int wt = tid - 64;               // 0 .. 32 * NWORK - 1
     const int q = warp & 3;                // TMEM lane quarter of this warp
-    const int h = (warp - 2) >> 2;         // half of the reflectors / columns
+    // half of the reflectors / columns (DUAL: each worker takes both)
+    const int h = DUAL ? 0 : (warp - 2) >> 2;
     const int row = 32 * q + lane;         // TMEM lane = tile column (pass 1) / chunk row (pass 2)
     const bool issuer = wt == 0;
     int g1 = 0, g2 = 0, it = 0;
@@ -510,7 +526,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
         for (int e = wt; e < KR * KR; e += 32 * NWORK)
           Ts[(e / KR) * L::T_LD + (e % KR)] = __ldg(Tm + e);
       }
-      workers_sync_or(false);  // T in shared memory for the W' step below
+      workers_sync_or<NWORK>(false);  // T in shared memory for the W' step below
 
       // ---- pass 1: split each chunk's C boxes into hi (in place) and lo ----
       const int units = nbox * (int)(BOX1 / 16);
@@ -616,34 +632,36 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
       }
       if (!skip) {
         constexpr int HALF = KR / 2;
-        float o[HALF];
-        if (h == 0) {  // W'[a] for a < KR/2: T[b][a] = 0 for b > a
+        for (int hh = h; hh < (DUAL ? 2 : h + 1); ++hh) {
+          float o[HALF];
+          if (hh == 0) {  // W'[a] for a < KR/2: T[b][a] = 0 for b > a
 #pragma unroll
-          for (int i = 0; i < HALF; ++i) {
-            float acc = 0.f;
+            for (int i = 0; i < HALF; ++i) {
+              float acc = 0.f;
 #pragma unroll
-            for (int b = 0; b < HALF; ++b) acc = fmaf(Ts[b * L::T_LD + i], w[b], acc);
-            o[i] = acc;
+              for (int b = 0; b < HALF; ++b) acc = fmaf(Ts[b * L::T_LD + i], w[b], acc);
+              o[i] = acc;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < HALF; ++i) {
+              float acc = 0.f;
+#pragma unroll
+              for (int b = 0; b < KR; ++b) acc = fmaf(Ts[b * L::T_LD + HALF + i], w[b], acc);
+              o[i] = acc;
+            }
           }
-        } else {
+          // B operand of pass 2, K-major: row = tile column, K atoms of 32
+          // reflectors (128 bytes) each
 #pragma unroll
-          for (int i = 0; i < HALF; ++i) {
-            float acc = 0.f;
-#pragma unroll
-            for (int b = 0; b < KR; ++b) acc = fmaf(Ts[b * L::T_LD + HALF + i], w[b], acc);
-            o[i] = acc;
+          for (int j = 0; j < HALF / 4; ++j) {
+            const int a0 = hh * HALF + 4 * j;
+            float4 hi, lo;
+            tc::split4(make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]), hi, lo);
+            const uint32_t off = (uint32_t)(a0 >> 5) * TCOLS * 128 + sw128(row, (a0 & 31) >> 2);
+            *reinterpret_cast<float4*>(sm + L::OFF_BH + off) = hi;
+            *reinterpret_cast<float4*>(sm + L::OFF_BL + off) = lo;
           }
-        }
-        // B operand of pass 2, K-major: row = tile column, K atoms of 32
-        // reflectors (128 bytes) each
-#pragma unroll
-        for (int j = 0; j < HALF / 4; ++j) {
-          const int a0 = h * HALF + 4 * j;
-          float4 hi, lo;
-          tc::split4(make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]), hi, lo);
-          const uint32_t off = (uint32_t)(a0 >> 5) * TCOLS * 128 + sw128(row, (a0 & 31) >> 2);
-          *reinterpret_cast<float4*>(sm + L::OFF_BH + off) = hi;
-          *reinterpret_cast<float4*>(sm + L::OFF_BL + off) = lo;
         }
         tma::fence_proxy_async();
         tc::fence_before();
@@ -663,50 +681,63 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
       }
 
       // ---- pass 2 epilogues: C += -(V W') by TMA reduce-add ----
+      // 64-column pieces of each chunk: one per worker half (staging boxes 2h
+      // and 2h + 1, all four reduced together), or with DUAL both, one after
+      // the other through staging boxes 0 and 1
+      constexpr int NPC = DUAL ? 2 : 1;
       for (int p = 0; p < nch2; ++p, ++g2) {
-        const int ab = g2 & 1, ua = g2 >> 1;
+        const int ab = g2 % L::NACC, ua = g2 / L::NACC;
         bool sk = *s_abort != 0 ||
                   !tma::mbar_wait_or_abort(BAR(B_ACCFULL + ab), (uint32_t)(ua & 1), wait_limit,
                                            s_abort);
         sk = __any_sync(tc::kFullMask, sk);
-        float d0[32], d1[32];
-        if (!sk) {
-          tc::fence_after();
-          const uint32_t ta =
-              tmem + ((uint32_t)(32 * q) << 16) + TM_D2 + 128u * (uint32_t)ab + 64u * (uint32_t)h;
-          tmem_ld32_nowait(ta, d0);
-          tmem_ld32_nowait(ta + 32, d1);
-          tmem_wait_ld();
-          tc::fence_before();
-          __syncwarp();
-          if (lane == 0) tma::mbar_arrive(BAR(B_ACCEMPTY + ab));
-        }
-        if (issuer) tma::bulk_wait_read_all();  // the previous reduce has read the staging tile
-        // row-split tiles: the staging boxes hold X until the peer has read it
-        if (CS > 1 && p == 0 && issuer && *s_abort == 0)
-          mbar_wait_cluster_or_abort(BAR(B_XREAD), (uint32_t)(it & 1), wait_limit, s_abort);
-        if (workers_sync_or(sk || *s_abort != 0)) continue;
-        if (p == 0 && tn < ntiles) {
-#pragma unroll
-          for (int k = 0; k < TPT; ++k) {
-            const int e = wt + k * 32 * NWORK;
-            Ts[(e / KR) * L::T_LD + (e % KR)] = tnext[k];
+        for (int pc = 0; pc < NPC; ++pc) {
+          const int piece = DUAL ? pc : h;
+          float d0[32], d1[32];
+          if (!sk) {
+            tc::fence_after();
+            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + L::TM_D2 +
+                                128u * (uint32_t)ab + 64u * (uint32_t)piece;
+            tmem_ld32_nowait(ta, d0);
+            tmem_ld32_nowait(ta + 32, d1);
+            tmem_wait_ld();
+            if (pc == NPC - 1) {
+              tc::fence_before();
+              __syncwarp();
+              if (lane == 0) tma::mbar_arrive(BAR(B_ACCEMPTY + ab));
+            }
           }
-        }
+          if (issuer) tma::bulk_wait_read_all();  // the previous reduce has read the staging tile
+          // row-split tiles: the staging boxes hold X until the peer has read it
+          if (CS > 1 && p == 0 && issuer && *s_abort == 0)
+            mbar_wait_cluster_or_abort(BAR(B_XREAD), (uint32_t)(it & 1), wait_limit, s_abort);
+          if (workers_sync_or<NWORK>(sk || *s_abort != 0)) break;
+          if (p == 0 && pc == 0 && tn < ntiles) {
 #pragma unroll
-        for (int uu = 0; uu < 8; ++uu) {
-          *reinterpret_cast<float4*>(sm + L::OFF_STG + (2 * h) * BOX2 + sw128(row, uu)) =
-              make_float4(-d0[4 * uu], -d0[4 * uu + 1], -d0[4 * uu + 2], -d0[4 * uu + 3]);
-          *reinterpret_cast<float4*>(sm + L::OFF_STG + (2 * h + 1) * BOX2 + sw128(row, uu)) =
-              make_float4(-d1[4 * uu], -d1[4 * uu + 1], -d1[4 * uu + 2], -d1[4 * uu + 3]);
-        }
-        tma::fence_proxy_async();
-        workers_sync_or(false);
-        if (issuer) {
-          for (int bq = 0; bq < nbox; ++bq)
-            tma::reduce_add_3d(&mC2, base + L::OFF_STG + bq * BOX2, tc0 + 32 * bq, y0 + R2 * p,
-                               m);
-          tma::bulk_commit();
+            for (int k = 0; k < TPT; ++k) {
+              const int e = wt + k * 32 * NWORK;
+              Ts[(e / KR) * L::T_LD + (e % KR)] = tnext[k];
+            }
+          }
+          const uint32_t sb = L::OFF_STG + (DUAL ? 0u : 2u * (uint32_t)h) * BOX2;
+#pragma unroll
+          for (int uu = 0; uu < 8; ++uu) {
+            *reinterpret_cast<float4*>(sm + sb + sw128(row, uu)) =
+                make_float4(-d0[4 * uu], -d0[4 * uu + 1], -d0[4 * uu + 2], -d0[4 * uu + 3]);
+            *reinterpret_cast<float4*>(sm + sb + BOX2 + sw128(row, uu)) =
+                make_float4(-d1[4 * uu], -d1[4 * uu + 1], -d1[4 * uu + 2], -d1[4 * uu + 3]);
+          }
+          tma::fence_proxy_async();
+          workers_sync_or<NWORK>(false);
+          if (issuer) {
+            for (int bq = 0; bq < L::NSTG; ++bq) {
+              const int box = (DUAL ? 2 * pc : 0) + bq;
+              if (box < nbox)
+                tma::reduce_add_3d(&mC2, base + L::OFF_STG + bq * BOX2, tc0 + 32 * box,
+                                   y0 + R2 * p, m);
+            }
+            tma::bulk_commit();
+          }
         }
       }
       if (issuer) {  // the tile's buffers are free once the last reduce has read its staging
@@ -726,7 +757,8 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
   if (CS > 1) cluster_sync_all();
   if (tid == 0 && *s_abort != 0) atomicExch(err, 1);
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_COLS)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(L::TM_COLS)
                  : "memory");
 }
 
@@ -794,11 +826,19 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(k_larfb_tma<KR, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(k_larfb_tma<KR, 1, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Lay<KR>::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(k_larfb_tma<KR, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(k_larfb_tma<KR, 2, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Lay<KR>::SMEM_BYTES) != cudaSuccess)
       return QRB_ERR_LAUNCH;
+    if constexpr (KR == 32) {
+      if (cudaFuncSetAttribute(k_larfb_tma<KR, 1, true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)Lay<KR, true>::SMEM_BYTES) != cudaSuccess)
+        return QRB_ERR_LAUNCH;
+    }
     if (device_error_ptr(&err_ptr[dev]) != QRB_OK) return QRB_ERR_DEVICE;
     if (cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         sms[dev] <= 0)
@@ -810,12 +850,12 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
     qa[0].val.clusterDim.y = 1;
     qa[0].val.clusterDim.z = 1;
     qc.gridDim = dim3(2 * (unsigned)sms[dev]);
-    qc.blockDim = dim3(NTH);
+    qc.blockDim = dim3(Lay<KR>::NTH);
     qc.dynamicSmemBytes = Lay<KR>::SMEM_BYTES;
     qc.attrs = qa;
     qc.numAttrs = 1;
     int pairs = 0;
-    if (cudaOccupancyMaxActiveClusters(&pairs, k_larfb_tma<KR, 2>, &qc) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&pairs, k_larfb_tma<KR, 2, false>, &qc) != cudaSuccess) {
       (void)cudaGetLastError();
       pairs = 0;  // no row split on this device
     }
@@ -840,9 +880,24 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
   const int mode = tma_pair_mode();
   const bool pair = halves && max_pairs[dev] > 0 &&
                     (mode == 2 || (mode == 0 && 2 * tiles <= sms[dev]));
-  if (!pair) {
+  // Two CTAs per SM (32 reflectors, no row halves; the same bits as one CTA
+  // per SM) when one CTA per SM would take more than one wave of tiles.
+  const int dmode = tma_dual_mode();
+  const bool dual = KR == 32 && !halves &&
+                    (dmode == 2 || (dmode == 0 && tiles > (int64_t)sms[dev]));
+  if (dual) {
+    if constexpr (KR == 32) {
+      int most2 = 2 * sms[dev];
+      if (cap > 0 && cap < most2) most2 = cap;
+      const int grid = (int)(tiles < most2 ? tiles : most2);
+      k_larfb_tma<KR, 1, true><<<grid, Lay<KR, true>::NTH, Lay<KR, true>::SMEM_BYTES, stream>>>(
+          maps.c1, maps.c2, maps.v1, maps.v2, T, sTb, (int)m0, (int)tiles, (int)ntc, j0, col0,
+          col_end, n, vw_hi, vw_lo, rs, err_ptr[dev], device_wait_limit(),
+          test_skip_mma() ? 1 : 0);
+    }
+  } else if (!pair) {
     const int grid = (int)(tiles < most ? tiles : most);
-    k_larfb_tma<KR, 1><<<grid, NTH, Lay<KR>::SMEM_BYTES, stream>>>(
+    k_larfb_tma<KR, 1, false><<<grid, Lay<KR>::NTH, Lay<KR>::SMEM_BYTES, stream>>>(
         maps.c1, maps.c2, maps.v1, maps.v2, T, sTb, (int)m0, (int)tiles, (int)ntc, j0, col0,
         col_end, n, vw_hi, vw_lo, rs, err_ptr[dev], device_wait_limit(),
         test_skip_mma() ? 1 : 0);
@@ -857,12 +912,12 @@ int launch_tma_t(const LarfbMaps& maps, const float* T, int64_t sTb, int64_t m0,
     la[0].val.clusterDim.y = 1;
     la[0].val.clusterDim.z = 1;
     lc.gridDim = dim3(2 * (unsigned)pairs);
-    lc.blockDim = dim3(NTH);
+    lc.blockDim = dim3(Lay<KR>::NTH);
     lc.dynamicSmemBytes = Lay<KR>::SMEM_BYTES;
     lc.stream = stream;
     lc.attrs = la;
     lc.numAttrs = 1;
-    if (cudaLaunchKernelEx(&lc, k_larfb_tma<KR, 2>, maps.c1, maps.c2, maps.v1, maps.v2, T, sTb,
+    if (cudaLaunchKernelEx(&lc, k_larfb_tma<KR, 2, false>, maps.c1, maps.c2, maps.v1, maps.v2, T, sTb,
                            (int)m0, (int)tiles, (int)ntc, j0, col0, col_end, n, vw_hi, vw_lo,
                            rs, err_ptr[dev], device_wait_limit(),
                            test_skip_mma() ? 1 : 0) != cudaSuccess)

@@ -309,6 +309,12 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 SMs twice over (2 x tiles <= SMs), else one CTA per tile;
  *                 1: always one CTA; 2: always a pair. The same bits either
  *                 way.
+ *   "tma_dual"    32-reflector updates without row halves, 0 (default): two
+ *                 CTAs per SM (4 worker warps, 2 pass-1 stages, one pass-2
+ *                 accumulator, about 104 KB of shared memory each) when the
+ *                 launch has more tiles than SMs, so that one CTA's pass 1
+ *                 runs beside the other's pass 2; 1: one CTA per SM; 2: always
+ *                 two. The same bits either way.
  *   "narrow_update" 0: the tensor-core route updates the next panel's 32
  *                 columns with the TMA-fed kernel as well, instead of the
  *                 narrow kernel that splits their rows across a cluster

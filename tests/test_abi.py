@@ -225,6 +225,12 @@ def test_config_keys():
         assert _lib.get_config("tma_pair") == v
     with pytest.raises(_lib.QRBError):
         _lib.set_config("tma_pair", 3)
+    assert _lib.get_config("tma_dual") == 0
+    for v in (1, 2, 0):
+        _lib.set_config("tma_dual", v)
+        assert _lib.get_config("tma_dual") == v
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("tma_dual", 3)
     assert _lib.get_config("tma_ctas") == 0
     _lib.set_config("tma_ctas", 96)
     assert _lib.get_config("tma_ctas") == 96

@@ -374,3 +374,54 @@ def test_row_split_update_abandons_a_call_whose_waits_run_out():
         _restore(old)
     assert checker.check(A, H, tau).passed
     assert _lib.get_config("device_error") == 0
+
+
+@pytest.mark.parametrize("b,n,groups", [(3, 160, 1), (5, 300, 1), (2, 1000, 1), (8, 640, 4),
+                                        (320, 512, 2)])
+def test_two_ctas_per_sm_give_the_same_bits(b, n, groups):
+    # the 32-reflector update with two CTAs per SM (4 worker warps, 2 pass-1
+    # stages, one pass-2 accumulator, the epilogue in two column halves) runs
+    # the same FP32 operations in the same order as one CTA per SM
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(37 * n + b)).to(DEV)
+    old = _hooks(tma_dual=2, two_level=0, lookahead=0, groups=groups)
+    try:
+        assert "tcgen05_tma" in api.route(b, n)
+        Hd, td = api.geqrf(A)
+        _lib.set_config("tma_dual", 1)
+        H1, t1 = api.geqrf(A)
+        _lib.set_config("tma_dual", 0)
+        Ha, ta = api.geqrf(A)
+        torch.cuda.synchronize()
+    finally:
+        _restore(old)
+    assert torch.equal(Hd, H1) and torch.equal(td, t1)
+    assert torch.equal(Ha, H1) and torch.equal(ta, t1)
+    k = min(b, 8)
+    assert checker.check(A[:k], Hd[:k], td[:k]).passed
+    H64, t64 = torch.geqrf(A[:k].cpu().double())
+    par = checker.parity(Hd[:k].cpu(), td[:k].cpu(), H64.float(), t64.float())
+    assert par.h_rel < RTOL and par.col_rel < RTOL and par.tau_rel < 5e-4, par
+    assert _lib.get_config("device_error") == 0
+
+
+def test_two_ctas_per_sm_abandon_a_call_whose_waits_run_out():
+    A = torch.randn(2, 256, 256, generator=torch.Generator().manual_seed(2)).to(DEV)
+    _lib.set_config("device_error", 0)
+    old = _hooks(wait_limit=2_000_000, test_skip_mma=1, sync_check=1, tma_dual=2,
+                 two_level=0, lookahead=0)
+    try:
+        with pytest.raises(_lib.QRBError) as exc:
+            api.geqrf(A)
+        assert exc.value.status == 7
+    finally:
+        _restore(old)
+    assert _lib.get_config("device_error") == 1
+    _lib.set_config("device_error", 0)
+    old = _hooks(tma_dual=2, two_level=0, lookahead=0)
+    try:
+        H, tau = api.geqrf(A)
+        torch.cuda.synchronize()
+    finally:
+        _restore(old)
+    assert checker.check(A, H, tau).passed
+    assert _lib.get_config("device_error") == 0
