@@ -104,12 +104,15 @@ constexpr int B_FULL1 = 0, B_SPLIT1 = B_FULL1 + S1MAX, B_EMPTY1 = B_SPLIT1 + S1M
 //   and the C lo buffer. Pass 2 reuses the pass-1 region once every pass-1
 //   MMA of the tile is done: NV2 stages of V (hi and lo), NSTG staging boxes
 //   for -V W', and W' hi / lo as the K-major B operand.
-//   TMEM: pass 1 accumulates into NP1 = 4 partial accumulators of KR columns
-//   (chunk ch into partial ch % NP1), summed in FP32 afterwards: the tensor
-//   core's accumulation inside an MMA is not rounded to nearest at every add,
-//   so one accumulator over thousands of rows drifts ~5x further from FP64
-//   than FFMA; short chains keep it at FFMA's level. Pass 2 accumulates into
-//   NACC accumulators of 128 columns from column TM_D2.
+//   TMEM: pass 1 accumulates into NP1 = 256 / KR partial accumulators of KR
+//   columns (chunk ch into partial ch % NP1), summed in FP32 afterwards: the
+//   tensor core's accumulation inside an MMA is not rounded to nearest at
+//   every add, so one accumulator over thousands of rows drifts ~5x further
+//   from FP64 than FFMA; short chains keep it at FFMA's level. Pass 2
+//   accumulates into NACC accumulators of 128 columns from column TM_D2. The
+//   two may share columns: every partial is read (the W' step) before the
+//   first pass-2 MMA of the tile, and the next tile's first pass-1 MMA waits
+//   for the tile's last epilogue (through the staging tile and the producer).
 // DUAL (32 reflectors only): two CTAs per SM, so that one CTA's pass 1 (bound
 //   by issuing MMAs) runs beside the other's pass 2 (bound by the TMA
 //   reduce-adds reading the staging tile): 4 worker warps, 2 pass-1 stages, one
@@ -140,7 +143,7 @@ struct Lay {
   static constexpr uint32_t OFF_TMEMV = OFF_BAR + NBAR * 8;
   static constexpr uint32_t OFF_ABORT = OFF_TMEMV + 4;
   static constexpr size_t SMEM_BYTES = OFF_ABORT + 12 + 1024;  // slack for aligning the base
-  static constexpr int NP1 = 4;
+  static constexpr int NP1 = 256 / KR;
   static constexpr int NACC = DUAL ? 1 : 2;
   static constexpr uint32_t TM_COLS = DUAL ? 256 : 512;
   static constexpr uint32_t TM_D2 = TM_COLS - 128 * NACC;
@@ -150,7 +153,8 @@ struct Lay {
   static constexpr uint32_t OFF_X = OFF_STG;
   static_assert(!DUAL || KR == 32, "two CTAs per SM for 32 reflectors only");
   static_assert(S1 <= S1MAX, "pass-1 stages");
-  static_assert(NP1 * KR <= (int)TM_D2, "pass-1 partials below the pass-2 accumulators");
+  // one CTA with two row halves keeps 2 x NP1 partials (never with DUAL)
+  static_assert((DUAL ? 1 : 2) * NP1 * KR <= (int)TM_COLS, "pass-1 partials in TMEM");
   static_assert(TCOLS * KR * 4 <= NSTG * BOX2, "partial W must fit the staging boxes");
   static_assert(SMEM_BYTES <= (DUAL ? 113 * 1024 : 227 * 1024), "shared memory budget");
 };
@@ -329,11 +333,10 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
   const int nch2 = (rq + R2 - 1) / R2;
   // Pass-1 partial accumulators. Without halves (rsplit >= r, one CTA): chunk
   // ch into partial ch % NP1. With halves (rsplit < r): rows [0, rsplit) and
-  // [rsplit, r) each into NP1 / 2 interleaved partials and the two half sums
-  // added last -- one CTA keeps both halves (partials NP1 / 2 and up for the
+  // [rsplit, r) each into NP1 interleaved partials and the two half sums
+  // added last -- one CTA keeps both halves (partials NP1 and up for the
   // second), a 2-CTA cluster one half per CTA: the same FP32 operations in
   // the same order either way, so the bits do not depend on the CTA count.
-  constexpr int NPH = NP1 / 2;
   const bool halves = CS > 1 || rsplit < r;
   const int c1 = CS > 1 ? nch1 : (halves ? rsplit / R1 : nch1);  // chunks of the first half
   const int tfirst = (int)blockIdx.x / CS, tstep = (int)gridDim.x / CS;
@@ -450,11 +453,11 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
             slot = ch % NP1;
             first = ch < NP1;
           } else if (ch < c1) {
-            slot = ch % NPH;
-            first = ch < NPH;
+            slot = ch % NP1;
+            first = ch < NP1;
           } else {
-            slot = NPH + (ch - c1) % NPH;
-            first = ch - c1 < NPH;
+            slot = NP1 + (ch - c1) % NP1;
+            first = ch - c1 < NP1;
           }
           const uint32_t d1 = tmem + (uint32_t)KR * (uint32_t)slot;
           // the k-step's operands are 1024 bytes further on: add to the
@@ -562,7 +565,7 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
 #pragma unroll
         for (int a = 0; a < NA; ++a) tmem_ld32_nowait(tl + 32u * a, w + 32 * a);
         tmem_wait_ld();
-        const int np = halves ? min(c1, NPH) : min(nch1, NP1);
+        const int np = min(c1, NP1);
         for (int pp = 1; pp < np; ++pp) {
 #pragma unroll
           for (int a = 0; a < NA; ++a) {
@@ -573,14 +576,14 @@ k_larfb_tma(const __grid_constant__ CUtensorMap mC1, const __grid_constant__ CUt
           }
         }
         if (CS == 1 && halves) {  // the second half's sum (16 columns at a time), added
-          const int np2 = min(nch1 - c1, NPH);
+          const int np2 = min(nch1 - c1, NP1);
 #pragma unroll
           for (int a = 0; a < KR / 16; ++a) {
             float ws2[16];
-            tmem_ld16_nowait(tl + (uint32_t)(KR * NPH + 16 * a), ws2);
+            tmem_ld16_nowait(tl + (uint32_t)(KR * NP1 + 16 * a), ws2);
             tmem_wait_ld();
             for (int pp = 1; pp < np2; ++pp) {
-              tmem_ld16_nowait(tl + (uint32_t)(KR * (NPH + pp) + 16 * a), wp);
+              tmem_ld16_nowait(tl + (uint32_t)(KR * (NP1 + pp) + 16 * a), wp);
               tmem_wait_ld();
 #pragma unroll
               for (int b = 0; b < 16; ++b) ws2[b] += wp[b];
