@@ -75,6 +75,8 @@ def route(batch: int, n: int, workspace: int | None = None) -> str:
         parts.append("lookahead")
     if code & (1 << 9):
         parts.append("two_level")
+    if code & (1 << 10):
+        parts.append("depth2")
     return base + ":" + ",".join(parts)
 
 

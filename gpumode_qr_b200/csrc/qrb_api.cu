@@ -32,6 +32,7 @@ std::atomic<int64_t> g_tma_ctas{0};        // 0 = one per SM
 std::atomic<int64_t> g_tma_split{1024};    // two row halves from this height (0 = never)
 std::atomic<int64_t> g_tma_pair{0};        // halves on: 0 auto, 1 one CTA, 2 a CTA pair per tile
 std::atomic<int64_t> g_tma_dual{0};        // 32 reflectors: 0 auto, 1 one CTA per SM, 2 two
+std::atomic<int64_t> g_la_depth{0};        // two-level look-ahead depth: 0 auto, 1 or 2 blocks
 std::atomic<int64_t> g_narrow{1};          // narrow cluster kernel for the next panel's columns
 std::atomic<int64_t> g_panel_priority{1};  // look-ahead stream at the highest priority
 
@@ -306,7 +307,7 @@ int blocked_qr2(const float* A, int64_t strideA_b, int64_t strideA_row, float* H
 // the columns from j0+96). Both streams end joined into sb.
 int blocked_qr2_lookahead(float* H, float* tau, float* T64a, float* T64b, int64_t batch, int n,
                           cudaStream_t sb, cudaStream_t sp, cudaEvent_t evP, cudaEvent_t evB,
-                          cudaEvent_t joinP, const TmaRoute& tr) {
+                          cudaEvent_t joinP, const TmaRoute& tr, bool deep) {
   const int64_t nn = (int64_t)n * n;
   constexpr int W = qrb::kPanelW;
   constexpr int K2 = 2 * W;
@@ -330,12 +331,47 @@ int blocked_qr2_lookahead(float* H, float* tau, float* T64a, float* T64b, int64_
     float* T2 = T64 + W * K2 + W;
     const int r = n - j0;
     const int w1 = r < W ? r : W;
-    const bool wide = r > K2 + W;  // a 64-reflector update follows
+    // a 64-reflector update follows (of the columns from j0 + 96, or from
+    // j0 + 128 at depth two)
+    const bool wide = r > (deep ? 2 * K2 : K2 + W);
     float* Hp = H + (int64_t)j0 * n + j0;
     float* vs = wide ? tr.vsplit64(buf, n) : nullptr;
     rc = qrb::launch_panel(Hp, nn, n, Hp, nn, n, tau + j0, n, T1, tsb, K2, nullptr, batch, r, w1,
                            sp, vs, (int64_t)n * K2, vpl, j0, K2, wide);
     if (rc != QRB_OK || r <= W) break;
+    if (deep) {
+      // Depth two: the priority stream applies this block's reflectors to the
+      // whole next block, so the wide update (columns from j0 + 128) has a
+      // block of slack and leaves the critical path. Block k's stream sp:
+      // panel 1, its narrow update of panel 2's columns, panel 2, then (once
+      // block k-1's wide update, which covered the columns from j0 + 64, is
+      // done) both panels' narrow updates of the next 64 columns.
+      const int c1 = r - W < W ? r - W : W;
+      rc = narrow(Hp, T1, r, Hp + W, c1, sp);
+      if (rc != QRB_OK) break;
+      float* Hq = Hp + (int64_t)W * n + W;
+      rc = qrb::launch_panel(Hq, nn, n, Hq, nn, n, tau + j0 + W, n, T2, tsb, K2, nullptr, batch,
+                             r - W, c1, sp, wide ? vs + W : nullptr, (int64_t)n * K2, vpl,
+                             j0 + W, K2, false);
+      if (rc != QRB_OK) break;
+      if (cudaEventRecord(evP, sp) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+      const int c = r - K2;
+      if (c <= 0) break;
+      if (cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+      const int cb = c < K2 ? c : K2;
+      rc = narrow(Hp, T1, r, Hp + K2, cb, sp);
+      if (rc == QRB_OK) rc = narrow(Hq, T2, r - W, Hq + W, cb, sp);
+      if (rc != QRB_OK) break;
+      if (!wide) continue;
+      if (cudaStreamWaitEvent(sb, evP, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+      rc = qrb::launch_t64(Hp, nn, n, T64, tsb, batch, r, sb);
+      if (rc == QRB_OK)
+        rc = qrb::launch_larfb_tma(*tr.maps, T64, tsb, tr.m0, batch, j0, j0 + 2 * K2, n, n, buf,
+                                   sb);
+      if (rc != QRB_OK) break;
+      if (cudaEventRecord(evB, sb) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
+      continue;
+    }
     // the columns from j0+32 were last written by the previous block's wide update
     if (cudaStreamWaitEvent(sp, evB, 0) != cudaSuccess) { rc = QRB_ERR_LAUNCH; break; }
     const int c1 = r - W < K2 ? r - W : K2;
@@ -517,6 +553,7 @@ Plan make_plan(int64_t batch, int n, const FactorScratch& ws) {
   // two-level blocking combines with the look-ahead on the tensor-core route
   // (second 64 x 64 factor and double-buffered split reflectors)
   p.lookahead = la_want && (p.two_level ? tma_route && ws.T64b != nullptr : ws.T2 != nullptr);
+
   // Groups: automatic 4 from n = 1024 (measured on B200: 30.6 vs 32.8 ms for
   // 8 x 4096^2 on the FFMA update; 18.1 vs 18.5 ms and 3.45 vs 3.61 ms at
   // 8 x 4096^2 and 64 x 1024^2 on the tensor-core two-level look-ahead),
@@ -526,13 +563,21 @@ Plan make_plan(int64_t batch, int n, const FactorScratch& ws) {
   if (groups > batch / 2) groups = (int)(batch / 2);
   if (batch < 4) groups = 1;
   p.groups = groups < 1 ? 1 : groups;
+  // Look-ahead depth two (the wide update off the critical path) where one
+  // group has the GPU to itself at n >= 4096, the panels' chain is the whole
+  // time (1 x 4096^2: 8.66 vs 8.98 ms; 2 x 4096^2: 9.01 vs 9.31 ms); with
+  // several groups, or below n = 4096, its extra narrow updates cost more
+  // (8 x 4096^2: 15.66 vs 15.08 ms; 2 x 2048^2: 3.95 vs 3.70 ms).
+  const int64_t depth = g_la_depth.load();
+  p.deep = p.lookahead && p.two_level &&
+           (depth == 2 || (depth == 0 && p.groups == 1 && n >= 4096));
   return p;
 }
 
 int route_code(const Plan& p) {
   if (p.route != kRouteBlocked) return p.route;
   return p.route | (p.larfb << 4) | (p.lookahead ? 1 << 8 : 0) | (p.two_level ? 1 << 9 : 0) |
-         (p.groups << 12);
+         (p.deep ? 1 << 10 : 0) | (p.groups << 12);
 }
 
 // The whole factorization of validated arguments, enqueued on s, as
@@ -607,7 +652,7 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
       cudaStream_t sp = g_panel_priority.load() ? ss->sp[0] : ss->spl[0];
       rc = tl  // with la: two-level blocking with the look-ahead
                ? blocked_qr2_lookahead(H, tau, ws.T64, ws.T64b, batch, n, s, sp, ss->evP[0],
-                                       ss->evB[0], ss->joinP[0], r0)
+                                       ss->evB[0], ss->joinP[0], r0, plan.deep)
                : blocked_qr_lookahead(A, strideA_b, strideA_row, H, tau, ws.T, ws.T2, batch, n,
                                       s, sp, ss->evP[0], ss->evB[0], ss->joinP[0],
                                       tma ? &r0 : nullptr);
@@ -637,7 +682,7 @@ int geqrf_enqueue(const float* A, int64_t strideA_b, int64_t strideA_row, float*
       rc = blocked_qr2_lookahead(H + b0 * nn, tau + b0 * n, ws.T64 + b0 * 4 * tper,
                                  ws.T64b + b0 * 4 * tper, b1 - b0, n, gs,
                                  g_panel_priority.load() ? ss->sp[g] : ss->spl[g], ss->evP[g],
-                                 ss->evB[g], ss->joinP[g], rg);
+                                 ss->evB[g], ss->joinP[g], rg, plan.deep);
     else if (tl)
       rc = blocked_qr2(A + b0 * strideA_b, strideA_b, strideA_row, H + b0 * nn, tau + b0 * n,
                        ws.T64 + b0 * 4 * tper, b1 - b0, n, gs, tma ? &rg : nullptr);
@@ -832,6 +877,11 @@ int qrb_set_config(const char* key, int64_t value) {
     g_tma_dual.store(value);
     return QRB_OK;
   }
+  if (std::strcmp(key, "lookahead_depth") == 0) {
+    if (value < 0 || value > 2) return QRB_ERR_INVALID_ARG;
+    g_la_depth.store(value);
+    return QRB_OK;
+  }
   if (std::strcmp(key, "narrow_update") == 0) {
     if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
     g_narrow.store(value);
@@ -927,6 +977,7 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "tma_split_rows") == 0) { *value = g_tma_split.load(); return QRB_OK; }
   if (std::strcmp(key, "tma_pair") == 0) { *value = g_tma_pair.load(); return QRB_OK; }
   if (std::strcmp(key, "tma_dual") == 0) { *value = g_tma_dual.load(); return QRB_OK; }
+  if (std::strcmp(key, "lookahead_depth") == 0) { *value = g_la_depth.load(); return QRB_OK; }
   if (std::strcmp(key, "panel_priority") == 0) { *value = g_panel_priority.load(); return QRB_OK; }
   if (std::strcmp(key, "device_error") == 0) {
     int v = 0;

@@ -232,6 +232,7 @@ struct Plan {
   int groups = 1;      // batch groups on internal streams
   bool lookahead = false;
   bool two_level = false;
+  bool deep = false;   // two-level look-ahead of depth two (the wide update off the chain)
 };
 Plan make_plan(int64_t batch, int n, const FactorScratch& ws);
 int route_code(const Plan& p);

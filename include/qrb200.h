@@ -315,6 +315,12 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 launch has more tiles than SMs, so that one CTA's pass 1
  *                 runs beside the other's pass 2; 1: one CTA per SM; 2: always
  *                 two. The same bits either way.
+ *   "lookahead_depth" 0 (default: 2 where one batch group runs at
+ *                 n >= 4096, else 1), 1 or 2: with two-level blocking and the
+ *                 look-ahead, depth 2 has the look-ahead stream apply both
+ *                 panels' reflectors to all 64 columns of the next block (two
+ *                 narrow updates), so the wide update starts at j0 + 128 and
+ *                 has a block of slack before the next block needs it.
  *   "narrow_update" 0: the tensor-core route updates the next panel's 32
  *                 columns with the TMA-fed kernel as well, instead of the
  *                 narrow kernel that splits their rows across a cluster

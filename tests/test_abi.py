@@ -225,6 +225,12 @@ def test_config_keys():
         assert _lib.get_config("tma_pair") == v
     with pytest.raises(_lib.QRBError):
         _lib.set_config("tma_pair", 3)
+    assert _lib.get_config("lookahead_depth") == 0
+    for v in (1, 2, 0):
+        _lib.set_config("lookahead_depth", v)
+        assert _lib.get_config("lookahead_depth") == v
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("lookahead_depth", 3)
     assert _lib.get_config("tma_dual") == 0
     for v in (1, 2, 0):
         _lib.set_config("tma_dual", v)

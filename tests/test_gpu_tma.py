@@ -287,16 +287,19 @@ def test_tall_panels_stage_the_narrow_update_in_chunks():
     assert _lib.get_config("device_error") == 0
 
 
+@pytest.mark.parametrize("depth", [1, 2])
 @pytest.mark.parametrize("b,n,groups", [(3, 160, 1), (2, 196, 1), (4, 300, 2), (3, 512, 1),
                                         (8, 640, 4), (2, 1028, 1), (2, 2048, 2)])
-def test_two_level_lookahead_route(b, n, groups):
+def test_two_level_lookahead_route(b, n, groups, depth):
     # two-level blocking with the look-ahead: per 64 columns panel 1, the
     # narrow update of the next 64 columns, panel 2, the narrow update of the
     # next 32; t64 and the 64-reflector update of the rest on the other
     # stream. FP64 gates, within 1e-4 of FP64 LAPACK, and the batch groups
     # leave the bits unchanged
     A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(29 * n + b))
-    old = _hooks(two_level=1, lookahead=1, groups=groups)
+    # depth 2: the priority stream also applies both panels' reflectors to the
+    # next block's second 32 columns, and the wide update starts at j0 + 128
+    old = _hooks(two_level=1, lookahead=1, groups=groups, lookahead_depth=depth)
     try:
         route = api.route(b, n)
         H, tau = api.geqrf(A.to(DEV))
@@ -306,6 +309,7 @@ def test_two_level_lookahead_route(b, n, groups):
     finally:
         _restore(old)
     assert "two_level" in route and "lookahead" in route and "tcgen05_tma" in route, route
+    assert ("depth2" in route) == (depth == 2), route
     assert torch.equal(H, H1) and torch.equal(tau, t1)
     assert checker.check(A, H.cpu(), tau.cpu()).passed
     H64, t64 = torch.geqrf(A.double())
