@@ -6,37 +6,49 @@
 // Operands (all row-major in HBM, read through swizzled TMA boxes):
 //   C   the trailing block of H itself (rows j0.., the tile's columns);
 //   V   the panel's unit-lower reflectors, already split by the panel kernel
-//       into a TF32 high part and a TF32 remainder (Vs[hi|lo][matrix][row][32]);
-//   T   the panel's 32 x 32 compact-WY factor.
+//       into a TF32 high part and a TF32 remainder (Vs[hi|lo][matrix][row][KR]);
+//   T   the panels' KR x KR compact-WY factor (KR = 32, or 64 for two-level
+//       blocking).
 // Each FP32 product a*b is formed as a_hi b_hi + a_hi b_lo + a_lo b_hi with
 // FP32 accumulation in TMEM (the lo*lo term, ~2^-22 relative, is dropped);
 // plain TF32 would not meet the FP32 accuracy gates.
 //
 // Per tile:
 //   pass 1  W^T = C^T V over all rows: D1 in TMEM (128 lanes = tile columns x
-//           32 columns = reflectors), as 8 interleaved partial sums. Both
-//           operands are MN-major (row-major C and V, contraction over rows),
-//           which kind::tf32 takes straight from TMA boxes in the 32-byte-atom
-//           128-byte swizzle. A 4-stage ring of 32-row chunks; the worker
+//           KR columns = reflectors), as 256 / KR interleaved partial sums.
+//           Both operands are MN-major (row-major C and V, contraction over
+//           rows), which kind::tf32 takes straight from TMA boxes in the
+//           32-byte-atom 128-byte swizzle. A ring of 32-row chunks; the worker
 //           warps split each C chunk into hi (in place) and lo (a second
 //           buffer) while earlier chunks' MMAs run.
 //   T^T     W' = T^T W on the CUDA cores (each worker thread one column, read
 //           from TMEM), split into hi / lo and stored as the K-major B operand
 //           of pass 2.
-//   pass 2  D2 = V W' per 128-row chunk (K-major V boxes from TMA, two TMEM
-//           accumulators so one chunk's epilogue overlaps the next chunk's
-//           MMAs); the epilogue writes -D2 into a swizzled staging tile and a
-//           TMA reduce-add adds it to C in place (the L2 does the
+//   pass 2  D2 = V W' per 128-row chunk (K-major V boxes from TMA); the
+//           epilogue writes -D2 into a swizzled staging tile and a TMA
+//           reduce-add adds it to C in place (the L2 does the
 //           read-modify-write).
 // Warp roles: warp 0 = TMA producer (one lane), warp 1 = MMA issuer (one
-// lane; the warp owns the TMEM allocation), warps 2-9 = workers. The roles
-// hand chunks to each other through mbarriers, so loads run up to four
-// chunks ahead of the MMAs and the MMAs overlap the workers' splitting and
-// epilogues. Every wait is bounded: a timeout sets a block-wide abort flag and
-// the device error flag; every role then skips its remaining work (its
-// waits return at once), the block waits (bounded) for what it already
-// issued, frees its TMEM and returns. The test hook "test_skip_mma" withholds
-// the pass-1 MMAs so that this path runs.
+// lane; the warp owns the TMEM allocation), the rest = workers. The roles
+// hand chunks to each other through mbarriers, so loads run ahead of the MMAs
+// and the MMAs overlap the workers' splitting and epilogues.
+// Three forms, chosen per launch, with the same FP32 operations in the same
+// order (the same bits):
+//   one CTA per SM    8 workers, 4 pass-1 stages, two pass-2 accumulators;
+//   row-split pairs   (CS = 2; trailing blocks of 1024+ rows, 2 x tiles <=
+//                     SMs) the rows in two halves, one per CTA of a 2-CTA
+//                     cluster, the partial W swapped through distributed
+//                     shared memory; a single CTA computes the same two half
+//                     sums when the launch has more tiles;
+//   two CTAs per SM   (DUAL; 32 reflectors, more tiles than SMs) 4 workers,
+//                     2 pass-1 stages, one pass-2 accumulator, the epilogue in
+//                     two column halves, so that one CTA's pass 1 runs beside
+//                     the other's pass 2.
+// Every wait is bounded: a timeout sets a block-wide abort flag and the device
+// error flag; every role then skips its remaining work (its waits return at
+// once), the block waits (bounded) for what it already issued, frees its TMEM
+// and returns (a pair meets at a closing cluster barrier first). The test hook
+// "test_skip_mma" withholds the pass-1 MMAs so that this path runs.
 #include <mutex>
 
 #include "qrb_tc.cuh"
