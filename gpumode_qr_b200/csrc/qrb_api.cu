@@ -15,6 +15,8 @@ std::atomic<int64_t> g_fail_next{0};
 std::atomic<int64_t> g_sync_check{0};
 std::atomic<int64_t> g_larfb_kind{-1};  // -1 automatic, else a kLarfb* kind
 std::atomic<int64_t> g_launches{0};
+std::atomic<int64_t> g_graph{1};           // replay cached CUDA graphs of repeated calls
+std::atomic<uint64_t> g_generation{0};     // bumped by routing-relevant qrb_set_config calls
 std::atomic<int64_t> g_groups{0};  // 0 = automatic
 std::atomic<int64_t> g_host_direct{3};
 std::atomic<int64_t> g_direct_blocks{0};
@@ -451,6 +453,9 @@ SideStreams* side_streams() {
 
 namespace qrb {
 void note_launches(int64_t count) { g_launches.fetch_add(count); }
+int64_t launch_count() { return g_launches.load(); }
+bool graph_cache_enabled() { return g_graph.load() != 0 && g_sync_check.load() == 0; }
+uint64_t config_generation() { return g_generation.load(); }
 }  // namespace qrb
 
 namespace qrb {
@@ -826,11 +831,27 @@ int qrb_geqrf_f32(const float* A, int64_t strideA_b, int64_t strideA_row,
   }
   if (take_injected_failure()) return QRB_ERR_INJECTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bool replayed = false;
+  const int rc = qrb::geqrf_graph(A, strideA_b, strideA_row, H, tau, fs, workspace,
+                                  workspace_bytes, batch, n, s, &replayed);
+  if (rc != QRB_OK || replayed) return finish(rc, s);
   return finish(qrb::geqrf_enqueue(A, strideA_b, strideA_row, H, tau, fs, batch, n, s), s);
 }
 
 int qrb_set_config(const char* key, int64_t value) {
   if (!key) return QRB_ERR_INVALID_ARG;
+  // every key but the counters and one-shot actions can change what a call
+  // enqueues (routes, kernel parameters): cached graphs of older calls no
+  // longer match
+  if (std::strcmp(key, "launches") != 0 && std::strcmp(key, "device_error") != 0 &&
+      std::strcmp(key, "fail_next") != 0 && std::strcmp(key, "wait_probe") != 0)
+    g_generation.fetch_add(1);
+  if (std::strcmp(key, "graph_cache") == 0) {
+    if (value != 0 && value != 1) return QRB_ERR_INVALID_ARG;
+    g_graph.store(value);
+    if (value == 0) qrb::graph_cache_clear();
+    return QRB_OK;
+  }
   if (std::strcmp(key, "fail_next") == 0) {
     if (value < 0) return QRB_ERR_INVALID_ARG;
     g_fail_next.store(value);
@@ -977,6 +998,11 @@ int qrb_get_config(const char* key, int64_t* value) {
   if (std::strcmp(key, "tma_split_rows") == 0) { *value = g_tma_split.load(); return QRB_OK; }
   if (std::strcmp(key, "tma_pair") == 0) { *value = g_tma_pair.load(); return QRB_OK; }
   if (std::strcmp(key, "tma_dual") == 0) { *value = g_tma_dual.load(); return QRB_OK; }
+  if (std::strcmp(key, "graph_cache") == 0) { *value = g_graph.load(); return QRB_OK; }
+  if (std::strcmp(key, "graph_cache_entries") == 0) {
+    *value = qrb::graph_cache_entries();
+    return QRB_OK;
+  }
   if (std::strcmp(key, "lookahead_depth") == 0) { *value = g_la_depth.load(); return QRB_OK; }
   if (std::strcmp(key, "panel_priority") == 0) { *value = g_panel_priority.load(); return QRB_OK; }
   if (std::strcmp(key, "device_error") == 0) {

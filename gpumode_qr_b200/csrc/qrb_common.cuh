@@ -235,6 +235,22 @@ struct Plan {
   bool deep = false;   // two-level look-ahead of depth two (the wide update off the chain)
 };
 Plan make_plan(int64_t batch, int n, const FactorScratch& ws);
+
+// The launch attribute that carries the stream's priority into the kernel
+// node when a launch is captured into a CUDA graph (an eager launch gets the
+// same priority from its stream). Writes *a and returns 1 for a stream of
+// non-default priority, else returns 0.
+inline int stream_priority_attr(cudaStream_t s, cudaLaunchAttribute* a) {
+  int p = 0;
+  if (cudaStreamGetPriority(s, &p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  if (p == 0) return 0;
+  a->id = cudaLaunchAttributePriority;
+  a->val.priority = p;
+  return 1;
+}
 int route_code(const Plan& p);
 
 // Whole factorization of already validated arguments, enqueued on `stream`
@@ -256,6 +272,29 @@ struct GroupHooks {
 int geqrf_enqueue(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau,
                   const FactorScratch& ws, int64_t batch, int n, cudaStream_t stream,
                   GroupHooks* hooks = nullptr);
+
+// CUDA graph replay of repeated blocked calls (qrb_graph.cu): on the second
+// call with the same arguments the call is captured, then replayed; sets
+// *handled when the call was enqueued that way (else the caller enqueues it).
+int geqrf_graph(const float* A, int64_t sAb, int64_t sAr, float* H, float* tau,
+                const FactorScratch& fs, const void* ws, size_t ws_bytes, int64_t batch, int n,
+                cudaStream_t s, bool* handled);
+void graph_cache_clear();
+int graph_cache_entries();
+// While one lives, this thread's calls enqueue eagerly: graph instantiation
+// may allocate device memory (the no-alloc entry point).
+struct NoGraphScope {
+  NoGraphScope();
+  ~NoGraphScope();
+  NoGraphScope(const NoGraphScope&) = delete;
+  NoGraphScope& operator=(const NoGraphScope&) = delete;
+};
+// qrb_set_config("graph_cache") and not "sync_check".
+bool graph_cache_enabled();
+// Bumped by every qrb_set_config call that can change what a call enqueues.
+uint64_t config_generation();
+// The launch counter (qrb_get_config("launches")).
+int64_t launch_count();
 
 // The public entry points' shared epilogue pieces: consume one injected
 // failure (fail_next), and apply the sync_check mode to a call's status.

@@ -260,13 +260,18 @@ int launch_larfb_narrow(const float* V, int64_t sVb, int64_t ldv, const float* T
   cfg.blockDim = dim3(NT, 1, 1);
   cfg.dynamicSmemBytes = L.bytes();
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (cs > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)cs;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  na += stream_priority_attr(stream, &attr[na]);
   cfg.attrs = attr;
-  cfg.numAttrs = cs > 1 ? 1 : 0;
+  cfg.numAttrs = (unsigned)na;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, k_larfb_narrow, V, sVb, ldv, T, sTb, t_ld, C,
                                            sCb, ldc, r, cw, cs, rs, rch);
   note_launches(1);

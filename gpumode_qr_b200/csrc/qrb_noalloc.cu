@@ -74,6 +74,7 @@ extern "C" int qrb_geqrf_f32_noalloc(const float* A, int64_t strideA_b,
                                      int64_t batch, int32_t n, void* stream) {
   if (batch < 0 || n < 0) return QRB_ERR_INVALID_ARG;
   if (batch == 0 || n == 0) return QRB_OK;
+  qrb::NoGraphScope eager;  // no graph instantiation: it may allocate device memory
   if (n <= qrb::kFusedMaxN)  // the small-n kernel uses no scratch
     return qrb_geqrf_f32(A, strideA_b, strideA_row, H, tau, batch, n, nullptr, 0, stream);
   if (batch > kNoAllocMaxBatch) return QRB_ERR_UNSUPPORTED;

@@ -382,13 +382,18 @@ int launch_panel_rpt(const float* src, int64_t sb_src, int64_t ld_src,
   cfg.blockDim = dim3((unsigned)nt, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (cs > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)cs;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  na += stream_priority_attr(stream, &attr[na]);
   cfg.attrs = attr;
-  cfg.numAttrs = cs > 1 ? 1 : 0;
+  cfg.numAttrs = (unsigned)na;
   static int* err_ptr[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QRB_ERR_DEVICE;

@@ -315,6 +315,16 @@ QRB_API int qrb_gram_geqrf_f32(const float* G, int64_t strideG_b, int64_t stride
  *                 launch has more tiles than SMs, so that one CTA's pass 1
  *                 runs beside the other's pass 2; 1: one CTA per SM; 2: always
  *                 two. The same bits either way.
+ *   "graph_cache" 1 (default): a blocked-route call repeated with the same
+ *                 arguments (every pointer, stride, size and the workspace)
+ *                 and no qrb_set_config change in between is captured into a
+ *                 CUDA graph on its second occurrence and replayed from then
+ *                 on (forked from and joined back into the caller's stream;
+ *                 the same kernels, the same bits; up to 8 graphs cached).
+ *                 Calls on a stream being captured, under "sync_check", and
+ *                 through qrb_geqrf_f32_noalloc run eagerly. 0: always
+ *                 eagerly (drops the cached graphs). Read
+ *                 "graph_cache_entries" for the number of graphs held.
  *   "lookahead_depth" 0 (default: 2 where one batch group runs at
  *                 n >= 4096, else 1), 1 or 2: with two-level blocking and the
  *                 look-ahead, depth 2 has the look-ahead stream apply both

@@ -225,6 +225,13 @@ def test_config_keys():
         assert _lib.get_config("tma_pair") == v
     with pytest.raises(_lib.QRBError):
         _lib.set_config("tma_pair", 3)
+    assert _lib.get_config("graph_cache") == 1
+    _lib.set_config("graph_cache", 0)
+    assert _lib.get_config("graph_cache") == 0
+    assert _lib.get_config("graph_cache_entries") == 0
+    _lib.set_config("graph_cache", 1)
+    with pytest.raises(_lib.QRBError):
+        _lib.set_config("graph_cache", 2)
     assert _lib.get_config("lookahead_depth") == 0
     for v in (1, 2, 0):
         _lib.set_config("lookahead_depth", v)

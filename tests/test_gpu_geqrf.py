@@ -392,3 +392,37 @@ def test_cuda_graph_capture_and_replay(b, n):
         torch.cuda.synchronize()
         assert torch.equal(H, He) and torch.equal(tau, te)
     del g
+
+
+@pytest.mark.parametrize("b,n", [(8, 512), (2, 4096), (64, 1024), (3, 300)])
+def test_repeated_calls_replay_a_cached_graph(b, n):
+    # The second call with the same arguments is captured into a CUDA graph
+    # and later calls replay it: the bits of the eager call, and the same
+    # launch count per call; a qrb_set_config change drops the match.
+    A = torch.randn(b, n, n, generator=torch.Generator().manual_seed(3 * n + b)).to(DEV)
+    H = torch.empty_like(A)
+    tau = torch.empty(b, n, device=DEV)
+    step = api.geqrf_into_fn(A, H, tau)
+    _lib.set_config("graph_cache", 0)
+    try:
+        step()
+        torch.cuda.synchronize()
+        He, te = H.clone(), tau.clone()
+        _lib.set_config("graph_cache", 1)
+        counts = []
+        for k in range(5):
+            if k == 3:
+                _lib.set_config("lookahead", _lib.get_config("lookahead"))  # new generation
+            H.fill_(float("nan"))
+            tau.fill_(float("nan"))
+            _lib.set_config("launches", 0)
+            step()
+            torch.cuda.synchronize()
+            counts.append(_lib.get_config("launches"))
+            assert torch.equal(H, He) and torch.equal(tau, te), k
+        assert _lib.get_config("graph_cache_entries") >= 1
+        assert len(set(counts)) == 1 and counts[0] > 0, counts
+    finally:
+        _lib.set_config("graph_cache", 1)
+    assert checker.check(A, H, tau).passed
+    assert _lib.get_config("device_error") == 0
