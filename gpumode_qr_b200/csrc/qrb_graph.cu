@@ -54,6 +54,9 @@ struct GraphEntry {
 constexpr int kEntries = 8;
 constexpr int kMaxDevices = 64;
 
+// The replay streams, their events and the cached graphs live as long as the
+// process (released with its CUDA context; no CUDA calls from static
+// destructors at exit); evicted and invalidated graphs are destroyed at once.
 struct GraphCache {
   std::mutex mu;
   GraphEntry e[kEntries];
